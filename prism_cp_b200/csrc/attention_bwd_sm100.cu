@@ -1,0 +1,529 @@
+// Flash-attention backward on tcgen05 (sm_100a), varlen / causal / GQA, head_dim 128.
+//
+// Two atomic-free kernels share the CTA shape of the forward (warps 0-3 compute
+// with thread == TMEM lane == tile row, warp 4 TMA producer, warp 5 MMA issuer):
+//   kv kernel  one CTA per (128-key tile, kv head), looping over the query heads
+//              of the GQA group and the query tiles that see the keys:
+//                S^T = K Q^T, dP^T = V dO^T            (TMEM cols 0-255)
+//                P^T = exp2(S^T*c - lse), dS^T = P^T (dP^T - D)  -> smem (bf16)
+//                dV += P^T dO, dK += dS^T Q            (TMEM cols 256-511)
+//   q kernel   one CTA per (128-query tile, query head), looping over key tiles:
+//                S = Q K^T, dP = dO V^T, dS = P (dP - D) -> smem, dQ += dS K
+// dK/dV/dQ are written once in bf16; nothing is accumulated with atomics, so the
+// result is deterministic. D = rowsum(dO * O) comes from a small preprocess kernel.
+// For context-parallel ring steps the caller passes the merged (global) O and LSE,
+// which makes P the correctly normalised global probabilities for that KV chunk.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "tma_host.cuh"
+
+namespace prism {
+namespace attnb {
+
+constexpr int D = 128;
+constexpr int TILE = 128;
+constexpr int TILE_BYTES = 128 * D * 2;  // 32 KiB
+constexpr int HALF = TILE_BYTES / 2;     // one 64-column box
+constexpr int NUM_THREADS = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Params {
+  const int* cu_q;
+  const int* cu_k;
+  const int* tiles;
+  int hq, hkv;
+  int causal;
+  float scale;       // softmax scale
+  const float* lse;  // [hq, Tq] natural log
+  const float* dsum; // [hq, Tq]
+  int tq;
+  __nv_bfloat16* out;  // dK / dV (kv kernel) or dQ (q kernel)
+  __nv_bfloat16* out2;
+  long out_stride;
+  int* status;
+};
+
+__device__ __forceinline__ void write_chunk_sw128(uint8_t* base, int row, int chunk, uint4 val) {
+  const int blk = chunk >> 3, cc = chunk & 7;
+  *reinterpret_cast<uint4*>(base + blk * HALF + row * 128 + ((cc ^ (row & 7)) << 4)) = val;
+}
+
+__device__ __forceinline__ void named_sync_compute() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// K-major operand (rows x 128 dims as two 64-dim boxes); k = 16-element step.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t base, int k) {
+  return make_smem_desc_sw128(base + (k >> 2) * HALF + (k & 3) * 32, 16, 1024);
+}
+// MN-major operand: rows are the reduction dim, two 64-wide boxes along MN.
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int k) {
+  return make_smem_desc_sw128(base + k * 2048, HALF, 1024);
+}
+
+// ------------------------------------------------------------------ dK, dV
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                       Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + TILE_BYTES;
+  uint8_t* sQ = smem + 2 * TILE_BYTES;
+  uint8_t* sdO = smem + 3 * TILE_BYTES;
+  uint8_t* sPT = smem + 4 * TILE_BYTES;
+  uint8_t* sdST = smem + 5 * TILE_BYTES;
+  float* lse_s = reinterpret_cast<float*>(smem + 6 * TILE_BYTES);
+  float* dsum_s = lse_s + 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(dsum_s + 128);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* q_full = bars + 1;
+  uint64_t* s_full = bars + 2;
+  uint64_t* p_full = bars + 3;
+  uint64_t* mma_done = bars + 4;
+  uint64_t* acc_done = bars + 5;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 7);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kv_head = blockIdx.y;
+  const int rep = p.hq / p.hkv;
+  const int seq = p.tiles[2 * blockIdx.x];
+  const int ktile = p.tiles[2 * blockIdx.x + 1];
+  const int q_seg = p.cu_q[seq], q_len = p.cu_q[seq + 1] - q_seg;
+  const int k_seg = p.cu_k[seq], k_len = p.cu_k[seq + 1] - k_seg;
+  const int k0 = ktile * TILE;
+  const int n_qt = (q_len + TILE - 1) / TILE;
+  const int i_start = p.causal ? ktile : 0;
+  const int per_head = max(0, n_qt - i_start);
+  const int n_it = rep * per_head;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(q_full, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(mma_done, 1);
+    mbar_init(acc_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0 && n_it > 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+      tma_load_3d(sK, &tmK, kv_full, 0, kv_head, k_seg + k0);
+      tma_load_3d(sK + HALF, &tmK, kv_full, 64, kv_head, k_seg + k0);
+      tma_load_3d(sV, &tmV, kv_full, 0, kv_head, k_seg + k0);
+      tma_load_3d(sV + HALF, &tmV, kv_full, 64, kv_head, k_seg + k0);
+      for (int it = 0; it < n_it; ++it) {
+        const int h = kv_head * rep + it / per_head;
+        const int i = i_start + it % per_head;
+        if (it > 0 && !mbar_wait_bounded(mma_done, (it - 1) & 1, abort_flag, p.status, kTimeoutProducer)) break;
+        mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+        const int qrow = q_seg + i * TILE;
+        tma_load_3d(sQ, &tmQ, q_full, 0, h, qrow);
+        tma_load_3d(sQ + HALF, &tmQ, q_full, 64, h, qrow);
+        tma_load_3d(sdO, &tmO, q_full, 0, h, qrow);
+        tma_load_3d(sdO + HALF, &tmO, q_full, 64, h, qrow);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0 && n_it > 0) {
+      constexpr uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idesc_km = make_idesc_bf16(128, 128, 0, 1);
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), adO = smem_u32(sdO);
+      const uint32_t aPT = smem_u32(sPT), adST = smem_u32(sdST);
+      bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, p.status, kTimeoutMma);
+      for (int it = 0; ok && it < n_it; ++it) {
+        if (!mbar_wait_bounded(q_full, it & 1, abort_flag, p.status, kTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_bf16_ss(tmem + 0, desc_kmajor(aK, k), desc_kmajor(aQ, k), idesc_kk, k > 0);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_bf16_ss(tmem + 128, desc_kmajor(aV, k), desc_kmajor(adO, k), idesc_kk, k > 0);
+        umma_commit(s_full);
+        if (!mbar_wait_bounded(p_full, it & 1, abort_flag, p.status, kTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_bf16_ss(tmem + 256, desc_kmajor(aPT, k), desc_mnmajor(adO, k), idesc_km, (it > 0 || k > 0));
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_bf16_ss(tmem + 384, desc_kmajor(adST, k), desc_mnmajor(aQ, k), idesc_km, (it > 0 || k > 0));
+        umma_commit(mma_done);
+      }
+      umma_commit(acc_done);
+    }
+  } else {
+    const int r = threadIdx.x;
+    const int kk = k0 + r;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const float c_log2 = p.scale * kLog2e;
+    bool ok = true;
+    for (int it = 0; it < n_it && ok; ++it) {
+      const int h = kv_head * rep + it / per_head;
+      const int i = i_start + it % per_head;
+      const int q0 = i * TILE;
+      if (it > 0) named_sync_compute();
+      {
+        const int qq = q0 + r;
+        const bool v = qq < q_len;
+        lse_s[r] = v ? p.lse[(long)h * p.tq + q_seg + qq] * kLog2e : INFINITY;
+        dsum_s[r] = v ? p.dsum[(long)h * p.tq + q_seg + qq] : 0.f;
+      }
+      named_sync_compute();
+      if (!mbar_wait_bounded(s_full, it & 1, abort_flag, p.status, kTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      if (it > 0 && !mbar_wait_bounded(mma_done, (it - 1) & 1, abort_flag, p.status, kTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool row_ok = kk < k_len;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t s_raw[32], dp_raw[32];
+        tmem_ld_32x32b_x32(lane_base + c * 32, s_raw);
+        tmem_ld_32x32b_x32(lane_base + 128 + c * 32, dp_raw);
+        tmem_wait_ld();
+        float pv[32], dsv[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int col = c * 32 + e;
+          const int qq = q0 + col;
+          const bool valid = row_ok && qq < q_len && (!p.causal || kk <= qq);
+          const float pe = valid ? exp2f(__uint_as_float(s_raw[e]) * c_log2 - lse_s[col]) : 0.f;
+          pv[e] = pe;
+          dsv[e] = pe * (__uint_as_float(dp_raw[e]) - dsum_s[col]);
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int chunk = c * 4 + g;
+          write_chunk_sw128(sPT, r, chunk,
+                            make_uint4(pack_bf16x2(pv[8 * g], pv[8 * g + 1]), pack_bf16x2(pv[8 * g + 2], pv[8 * g + 3]),
+                                       pack_bf16x2(pv[8 * g + 4], pv[8 * g + 5]),
+                                       pack_bf16x2(pv[8 * g + 6], pv[8 * g + 7])));
+          write_chunk_sw128(sdST, r, chunk,
+                            make_uint4(pack_bf16x2(dsv[8 * g], dsv[8 * g + 1]),
+                                       pack_bf16x2(dsv[8 * g + 2], dsv[8 * g + 3]),
+                                       pack_bf16x2(dsv[8 * g + 4], dsv[8 * g + 5]),
+                                       pack_bf16x2(dsv[8 * g + 6], dsv[8 * g + 7])));
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && n_it > 0) ok = mbar_wait_bounded(acc_done, 0, abort_flag, p.status, kTimeoutEpilogue);
+    tc_fence_after();
+    if (kk < k_len) {
+      __nv_bfloat16* dv_row = p.out2 + (long)(k_seg + kk) * p.out_stride + (long)kv_head * D;
+      __nv_bfloat16* dk_row = p.out + (long)(k_seg + kk) * p.out_stride + (long)kv_head * D;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t a[32], b[32];
+        if (n_it > 0 && ok) {
+          tmem_ld_32x32b_x32(lane_base + 256 + c * 32, a);
+          tmem_ld_32x32b_x32(lane_base + 384 + c * 32, b);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) a[e] = b[e] = 0u;
+        }
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          reinterpret_cast<uint4*>(dv_row + c * 32)[v] = make_uint4(
+              pack_bf16x2(__uint_as_float(a[8 * v]), __uint_as_float(a[8 * v + 1])),
+              pack_bf16x2(__uint_as_float(a[8 * v + 2]), __uint_as_float(a[8 * v + 3])),
+              pack_bf16x2(__uint_as_float(a[8 * v + 4]), __uint_as_float(a[8 * v + 5])),
+              pack_bf16x2(__uint_as_float(a[8 * v + 6]), __uint_as_float(a[8 * v + 7])));
+          reinterpret_cast<uint4*>(dk_row + c * 32)[v] = make_uint4(
+              pack_bf16x2(__uint_as_float(b[8 * v]) * p.scale, __uint_as_float(b[8 * v + 1]) * p.scale),
+              pack_bf16x2(__uint_as_float(b[8 * v + 2]) * p.scale, __uint_as_float(b[8 * v + 3]) * p.scale),
+              pack_bf16x2(__uint_as_float(b[8 * v + 4]) * p.scale, __uint_as_float(b[8 * v + 5]) * p.scale),
+              pack_bf16x2(__uint_as_float(b[8 * v + 6]) * p.scale, __uint_as_float(b[8 * v + 7]) * p.scale));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ dQ
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    attn_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sdO = smem + TILE_BYTES;
+  uint8_t* sK = smem + 2 * TILE_BYTES;  // [2]
+  uint8_t* sV = smem + 4 * TILE_BYTES;  // [2]
+  uint8_t* sdS = smem + 6 * TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * TILE_BYTES);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* ds_full = bars + 6;
+  uint64_t* acc_done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 9);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const int kv_head = head / (p.hq / p.hkv);
+  const int seq = p.tiles[2 * blockIdx.x];
+  const int qtile = p.tiles[2 * blockIdx.x + 1];
+  const int q_seg = p.cu_q[seq], q_len = p.cu_q[seq + 1] - q_seg;
+  const int k_seg = p.cu_k[seq], k_len = p.cu_k[seq + 1] - k_seg;
+  const int q0 = qtile * TILE;
+  const int kv_end = p.causal ? min(k_len, q0 + TILE) : k_len;
+  const int n_kv = kv_end > 0 ? (kv_end + TILE - 1) / TILE : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(ds_full, 128);
+    mbar_init(acc_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0 && n_kv > 0) {
+      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+      tma_load_3d(sQ, &tmQ, q_full, 0, head, q_seg + q0);
+      tma_load_3d(sQ + HALF, &tmQ, q_full, 64, head, q_seg + q0);
+      tma_load_3d(sdO, &tmO, q_full, 0, head, q_seg + q0);
+      tma_load_3d(sdO + HALF, &tmO, q_full, 64, head, q_seg + q0);
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait_bounded(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.status, kTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * TILE_BYTES);
+        const int krow = k_seg + j * TILE;
+        uint8_t* kd = sK + s * TILE_BYTES;
+        uint8_t* vd = sV + s * TILE_BYTES;
+        tma_load_3d(kd, &tmK, &kv_full[s], 0, kv_head, krow);
+        tma_load_3d(kd + HALF, &tmK, &kv_full[s], 64, kv_head, krow);
+        tma_load_3d(vd, &tmV, &kv_full[s], 0, kv_head, krow);
+        tma_load_3d(vd + HALF, &tmV, &kv_full[s], 64, kv_head, krow);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0 && n_kv > 0) {
+      constexpr uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idesc_km = make_idesc_bf16(128, 128, 0, 1);
+      const uint32_t aQ = smem_u32(sQ), adO = smem_u32(sdO), adS = smem_u32(sdS);
+      bool ok = mbar_wait_bounded(q_full, 0, abort_flag, p.status, kTimeoutMma);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait_bounded(&kv_full[s], (j >> 1) & 1, abort_flag, p.status, kTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t aK = smem_u32(sK + s * TILE_BYTES), aV = smem_u32(sV + s * TILE_BYTES);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_bf16_ss(tmem + 0, desc_kmajor(aQ, k), desc_kmajor(aK, k), idesc_kk, k > 0);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_bf16_ss(tmem + 128, desc_kmajor(adO, k), desc_kmajor(aV, k), idesc_kk, k > 0);
+        umma_commit(s_full);
+        if (!mbar_wait_bounded(ds_full, j & 1, abort_flag, p.status, kTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_bf16_ss(tmem + 256, desc_kmajor(adS, k), desc_mnmajor(aK, k), idesc_km, (j > 0 || k > 0));
+        umma_commit(&kv_empty[s]);
+      }
+      umma_commit(acc_done);
+    }
+  } else {
+    const int r = threadIdx.x;
+    const int qq = q0 + r;
+    const bool row_ok = qq < q_len;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const float c_log2 = p.scale * kLog2e;
+    const float lse2 = row_ok ? p.lse[(long)head * p.tq + q_seg + qq] * kLog2e : INFINITY;
+    const float dsum = row_ok ? p.dsum[(long)head * p.tq + q_seg + qq] : 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv && ok; ++j) {
+      if (!mbar_wait_bounded(s_full, j & 1, abort_flag, p.status, kTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int kbase = j * TILE;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t s_raw[32], dp_raw[32];
+        tmem_ld_32x32b_x32(lane_base + c * 32, s_raw);
+        tmem_ld_32x32b_x32(lane_base + 128 + c * 32, dp_raw);
+        tmem_wait_ld();
+        float dsv[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int kk = kbase + c * 32 + e;
+          const bool valid = row_ok && kk < k_len && (!p.causal || kk <= qq);
+          const float pe = valid ? exp2f(__uint_as_float(s_raw[e]) * c_log2 - lse2) : 0.f;
+          dsv[e] = pe * (__uint_as_float(dp_raw[e]) - dsum);
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          write_chunk_sw128(sdS, r, c * 4 + g,
+                            make_uint4(pack_bf16x2(dsv[8 * g], dsv[8 * g + 1]),
+                                       pack_bf16x2(dsv[8 * g + 2], dsv[8 * g + 3]),
+                                       pack_bf16x2(dsv[8 * g + 4], dsv[8 * g + 5]),
+                                       pack_bf16x2(dsv[8 * g + 6], dsv[8 * g + 7])));
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(ds_full);
+    }
+    if (ok && n_kv > 0) ok = mbar_wait_bounded(acc_done, 0, abort_flag, p.status, kTimeoutEpilogue);
+    tc_fence_after();
+    if (row_ok) {
+      __nv_bfloat16* dq_row = p.out + (long)(q_seg + qq) * p.out_stride + (long)head * D;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t a[32];
+        if (n_kv > 0 && ok) {
+          tmem_ld_32x32b_x32(lane_base + 256 + c * 32, a);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) a[e] = 0u;
+        }
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          reinterpret_cast<uint4*>(dq_row + c * 32)[v] = make_uint4(
+              pack_bf16x2(__uint_as_float(a[8 * v]) * p.scale, __uint_as_float(a[8 * v + 1]) * p.scale),
+              pack_bf16x2(__uint_as_float(a[8 * v + 2]) * p.scale, __uint_as_float(a[8 * v + 3]) * p.scale),
+              pack_bf16x2(__uint_as_float(a[8 * v + 4]) * p.scale, __uint_as_float(a[8 * v + 5]) * p.scale),
+              pack_bf16x2(__uint_as_float(a[8 * v + 6]) * p.scale, __uint_as_float(a[8 * v + 7]) * p.scale));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// D[h, t] = sum_d dO[t, h, d] * O[t, h, d]   (one warp per (t, h))
+__global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ dO, long dos, const __nv_bfloat16* __restrict__ O,
+                                    long os, float* __restrict__ out, int T, int H) {
+  const long w = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (long)T * H) return;
+  const long t = w / H;
+  const int h = w % H;
+  const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(dO + t * dos + (long)h * D) + lane * 2;
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(O + t * os + (long)h * D) + lane * 2;
+  float acc = 0.f;
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const float2 x = __bfloat1622float2(a[e]);
+    const float2 y = __bfloat1622float2(b[e]);
+    acc += x.x * y.x + x.y * y.y;
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) out[(long)h * T + t] = acc;
+}
+
+constexpr int SMEM_KV = 6 * TILE_BYTES + 1024 + 256 + 1024;
+constexpr int SMEM_Q = 7 * TILE_BYTES + 256 + 1024;
+
+}  // namespace attnb
+
+void attention_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& out,
+                         const at::Tensor& lse, const at::Tensor& dout, const at::Tensor& cu_q, const at::Tensor& cu_k,
+                         const at::Tensor& tiles_q, const at::Tensor& tiles_k, at::Tensor& dq, at::Tensor& dk,
+                         at::Tensor& dv, bool causal, double softmax_scale, at::Tensor& status) {
+  using namespace attnb;
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int Tq = q.size(0), hq = q.size(1), hkv = k.size(1);
+  TORCH_CHECK(dk.stride(0) == dv.stride(0), "attention bwd: dk/dv must share a row stride");
+  at::Tensor dsum = at::empty({hq, Tq}, q.options().dtype(at::kFloat));
+  {
+    const long warps = (long)Tq * hq;
+    if (warps > 0)
+      attn_bwd_dot_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(
+          reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
+          reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), out.stride(0), dsum.data_ptr<float>(), Tq, hq);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  CUtensorMap tq = make_head_map_128(q), tk = make_head_map_128(k), tv = make_head_map_128(v),
+              tdo = make_head_map_128(dout);
+  Params p;
+  p.cu_q = cu_q.data_ptr<int>();
+  p.cu_k = cu_k.data_ptr<int>();
+  p.hq = hq;
+  p.hkv = hkv;
+  p.causal = causal ? 1 : 0;
+  p.scale = (float)softmax_scale;
+  p.lse = lse.data_ptr<float>();
+  p.dsum = dsum.data_ptr<float>();
+  p.tq = Tq;
+  p.status = status.data_ptr<int>();
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_KV));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_Q));
+    configured = true;
+  }
+  if (tiles_k.size(0) > 0) {
+    Params pk = p;
+    pk.tiles = tiles_k.data_ptr<int>();
+    pk.out = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+    pk.out2 = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+    pk.out_stride = dk.stride(0);
+    attn_bwd_kv_kernel<<<dim3(tiles_k.size(0), hkv), NUM_THREADS, SMEM_KV, stream>>>(tq, tk, tv, tdo, pk);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  if (tiles_q.size(0) > 0) {
+    Params pq = p;
+    pq.tiles = tiles_q.data_ptr<int>();
+    pq.out = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
+    pq.out2 = nullptr;
+    pq.out_stride = dq.stride(0);
+    attn_bwd_q_kernel<<<dim3(tiles_q.size(0), hq), NUM_THREADS, SMEM_Q, stream>>>(tq, tk, tv, tdo, pq);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
+}  // namespace prism

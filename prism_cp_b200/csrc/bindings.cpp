@@ -1,0 +1,57 @@
+// Python bindings of the sm_100a kernel library (module prism_cp_b200._C).
+#include <torch/extension.h>
+
+namespace prism {
+void gemm_sm100(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, bool a_mn, bool b_mn, bool accumulate,
+                const c10::optional<at::Tensor>& row_scale, at::Tensor& status);
+void rownorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& z,
+                 at::Tensor& y, at::Tensor& rstd, int64_t heads, int64_t n, double inv_n, double eps);
+c10::optional<at::Tensor> rownorm_bwd(const at::Tensor& dy, const at::Tensor& x, const c10::optional<at::Tensor>& w,
+                                      const c10::optional<at::Tensor>& z, const at::Tensor& rstd, at::Tensor& dx,
+                                      const c10::optional<at::Tensor>& dz, int64_t heads, int64_t n, double inv_n);
+void rope_inplace(at::Tensor& x, const at::Tensor& pos, int64_t heads, int64_t d, double base, bool inverse);
+at::Tensor conv1d_silu_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& halo,
+                           const at::Tensor& cu);
+std::vector<at::Tensor> conv1d_silu_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                                        const c10::optional<at::Tensor>& halo, const at::Tensor& cu, at::Tensor& dx);
+void swiglu_fwd(const at::Tensor& x, at::Tensor& y);
+void swiglu_bwd(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dx);
+void ce_fused(at::Tensor& logits, const at::Tensor& labels, const at::Tensor& weight, at::Tensor& loss,
+              const c10::optional<at::Tensor>& lse);
+void sumsq_accumulate(const at::Tensor& g, at::Tensor& out);
+void adamw_step(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v,
+                const c10::optional<at::Tensor>& p_bf16, const at::Tensor& sumsq, double max_norm, double lr,
+                double b1, double b2, double eps, double wd, double bc1, double bc2);
+void attention_fwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu_q,
+                         const at::Tensor& cu_k, const at::Tensor& tiles, at::Tensor& out, at::Tensor& lse,
+                         bool causal, double softmax_scale, at::Tensor& status);
+void attention_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& out,
+                         const at::Tensor& lse, const at::Tensor& dout, const at::Tensor& cu_q, const at::Tensor& cu_k,
+                         const at::Tensor& tiles_q, const at::Tensor& tiles_k, at::Tensor& dq, at::Tensor& dk,
+                         at::Tensor& dv, bool causal, double softmax_scale, at::Tensor& status);
+void gdn_state_fwd(const at::Tensor& W, const at::Tensor& U, const at::Tensor& Kd, const at::Tensor& gamma,
+                   const c10::optional<at::Tensor>& S0, const at::Tensor& seq_chunks, at::Tensor& Delta,
+                   at::Tensor& S_all, at::Tensor& S_final);
+void gdn_state_bwd(const at::Tensor& W, const at::Tensor& dDelta_ext, const at::Tensor& Kd, const at::Tensor& gamma,
+                   const at::Tensor& dS_ext, const c10::optional<at::Tensor>& dS_final, const at::Tensor& seq_chunks,
+                   at::Tensor& dDelta, at::Tensor& G_next, at::Tensor& dS0);
+}  // namespace prism
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "prism_cp_b200 sm_100a kernels";
+  m.def("gemm", &prism::gemm_sm100, "tcgen05 GEMM C (+)= rowscale * A B^T");
+  m.def("rownorm_fwd", &prism::rownorm_fwd);
+  m.def("rownorm_bwd", &prism::rownorm_bwd);
+  m.def("rope_inplace", &prism::rope_inplace);
+  m.def("conv1d_silu_fwd", &prism::conv1d_silu_fwd);
+  m.def("conv1d_silu_bwd", &prism::conv1d_silu_bwd);
+  m.def("swiglu_fwd", &prism::swiglu_fwd);
+  m.def("swiglu_bwd", &prism::swiglu_bwd);
+  m.def("ce_fused", &prism::ce_fused);
+  m.def("sumsq_accumulate", &prism::sumsq_accumulate);
+  m.def("adamw_step", &prism::adamw_step);
+  m.def("attention_fwd", &prism::attention_fwd_sm100, "tcgen05 varlen GQA flash attention forward");
+  m.def("attention_bwd", &prism::attention_bwd_sm100, "tcgen05 varlen GQA flash attention backward");
+  m.def("gdn_state_fwd", &prism::gdn_state_fwd);
+  m.def("gdn_state_bwd", &prism::gdn_state_bwd);
+}

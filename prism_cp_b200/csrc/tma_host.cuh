@@ -1,0 +1,42 @@
+// Host-side helpers for building TMA tensor maps (no driver library link needed:
+// cuTensorMapEncodeTiled is resolved through the runtime's driver entry point).
+#pragma once
+
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+#include <c10/cuda/CUDAException.h>
+
+namespace prism {
+
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    C10_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && ptr != nullptr, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// [tokens, heads, 128] bf16 view, boxes of {64 dims, 1 head, 128 tokens}, 128-byte swizzle.
+inline CUtensorMap make_head_map_128(const at::Tensor& t) {
+  TORCH_CHECK(t.dim() == 3 && t.size(2) == 128 && t.stride(2) == 1 && t.stride(1) == 128,
+              "attention: tensors must be [tokens, heads, 128] with contiguous heads");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, "attention: bf16 tensors required");
+  TORCH_CHECK(t.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0,
+              "attention: 16-byte aligned rows required");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {128, (cuuint64_t)t.size(1), (cuuint64_t)t.size(0)};
+  cuuint64_t strides[2] = {256, (cuuint64_t)t.stride(0) * 2};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, t.data_ptr(), dims, strides, box,
+                                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return map;
+}
+
+}  // namespace prism

@@ -1,0 +1,179 @@
+"""Native PyTorch hybrid Gated-DeltaNet : GQA decoder (no Megatron dependency).
+
+Layer structure (pre-norm, residual, TP = PP = 1 inside a stage):
+  * GQA mixer: RMSNorm -> fused QKV GEMM -> RoPE(q, k) -> causal varlen GQA
+    attention (ring over the CP team when CP > 1) -> output GEMM.
+  * GDN mixer: RMSNorm -> fused in-projection GEMM (q, k, v, z, beta, decay) ->
+    causal conv1d(4) + SiLU on q/k/v (halo from the previous CP rank) -> L2 norm
+    of q/k -> chunked gated delta rule (state carried across CP ranks) ->
+    gated RMSNorm with silu(z) -> output GEMM.
+  * MLP: RMSNorm -> fc1 GEMM -> SwiGLU -> fc2 GEMM.
+Untied embedding and output head; the head is fused with cross-entropy.
+
+Every mixer receives a ``LocalLayout`` (``parallel/layout.py``) that describes
+this rank's tokens for the layer's ownership layout and performs the layer's
+context-parallel communication, so the same module runs CP = 1 (one GPU) and
+any per-layer CP degree chosen by the planner.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..ops.cross_entropy import head_cross_entropy
+from ..ops.elementwise import causal_conv1d_silu, rope, swiglu
+from ..ops.gemm import linear
+from ..ops.norms import gated_rms_norm, l2_norm, rms_norm
+from .config import HybridConfig
+
+
+def _normal(shape, std, dtype, device, generator):
+    t = torch.empty(shape, dtype=torch.float32, device="cpu")
+    t.normal_(0.0, std, generator=generator)
+    return nn.Parameter(t.to(device=device, dtype=dtype))
+
+
+class MLP(nn.Module):
+    def __init__(self, cfg: HybridConfig, dtype, device, gen):
+        super().__init__()
+        h, f = cfg.hidden_size, cfg.ffn_hidden_size
+        out_std = cfg.init_method_std / math.sqrt(2.0 * cfg.num_layers)
+        self.norm = nn.Parameter(torch.ones(h, dtype=dtype, device=device))
+        self.fc1 = _normal((2 * f, h), cfg.init_method_std, dtype, device, gen)
+        self.fc2 = _normal((h, f), out_std, dtype, device, gen)
+        self.eps = cfg.norm_epsilon
+
+    def forward(self, x):
+        y = rms_norm(x, self.norm, self.eps)
+        return linear(swiglu(linear(y, self.fc1)), self.fc2)
+
+
+class GQAMixer(nn.Module):
+    def __init__(self, cfg: HybridConfig, dtype, device, gen):
+        super().__init__()
+        h = cfg.hidden_size
+        self.hq, self.hkv, self.d = cfg.num_attention_heads, cfg.num_query_groups, cfg.kv_channels
+        out_std = cfg.init_method_std / math.sqrt(2.0 * cfg.num_layers)
+        self.norm = nn.Parameter(torch.ones(h, dtype=dtype, device=device))
+        self.qkv = _normal((cfg.qkv_dim, h), cfg.init_method_std, dtype, device, gen)
+        self.proj = _normal((h, self.hq * self.d), out_std, dtype, device, gen)
+        self.eps, self.base = cfg.norm_epsilon, cfg.rotary_base
+
+    def forward(self, x, ctx):
+        T = x.shape[0]
+        y = rms_norm(x, self.norm, self.eps)
+        qkv = linear(y, self.qkv)
+        qd, kd = self.hq * self.d, self.hkv * self.d
+        q = rope(qkv[:, :qd], ctx.positions, self.hq, self.d, self.base).view(T, self.hq, self.d)
+        k = rope(qkv[:, qd:qd + kd], ctx.positions, self.hkv, self.d, self.base).view(T, self.hkv, self.d)
+        v = qkv[:, qd + kd:].view(T, self.hkv, self.d)
+        o = ctx.attention(q, k, v)
+        return linear(o.reshape(T, qd), self.proj)
+
+
+class GDNMixer(nn.Module):
+    def __init__(self, cfg: HybridConfig, dtype, device, gen):
+        super().__init__()
+        h = cfg.hidden_size
+        self.H, self.dk, self.dv = cfg.linear_num_key_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim
+        self.qk_dim, self.v_dim = cfg.gdn_qk_dim, cfg.gdn_v_dim
+        out_std = cfg.init_method_std / math.sqrt(2.0 * cfg.num_layers)
+        conv_ch = 2 * self.qk_dim + self.v_dim
+        self.norm = nn.Parameter(torch.ones(h, dtype=dtype, device=device))
+        self.in_proj = _normal((cfg.gdn_in_proj, h), cfg.init_method_std, dtype, device, gen)
+        bound = 1.0 / math.sqrt(cfg.linear_conv_kernel_dim)
+        conv = torch.empty((conv_ch, cfg.linear_conv_kernel_dim)).uniform_(-bound, bound, generator=gen)
+        self.conv = nn.Parameter(conv.to(device=device, dtype=dtype))
+        a = torch.empty(self.H).uniform_(1.0, 16.0, generator=gen)
+        self.A_log = nn.Parameter(a.log().to(device=device, dtype=torch.float32))
+        dt = torch.exp(torch.empty(self.H).uniform_(math.log(1e-3), math.log(1e-1), generator=gen))
+        self.dt_bias = nn.Parameter((dt + torch.log(-torch.expm1(-dt))).to(device=device, dtype=torch.float32))
+        self.out_norm = nn.Parameter(torch.ones(self.dv, dtype=dtype, device=device))
+        self.proj = _normal((h, self.v_dim), out_std, dtype, device, gen)
+        self.eps = cfg.norm_epsilon
+
+    def forward(self, x, ctx):
+        T = x.shape[0]
+        y = rms_norm(x, self.norm, self.eps)
+        p = linear(y, self.in_proj)
+        c_end = 2 * self.qk_dim + self.v_dim
+        qkv = ctx.conv(p[:, :c_end], self.conv)
+        q = l2_norm(qkv[:, :self.qk_dim], self.H).view(T, self.H, self.dk)
+        k = l2_norm(qkv[:, self.qk_dim:2 * self.qk_dim], self.H).view(T, self.H, self.dk)
+        v = qkv[:, 2 * self.qk_dim:].view(T, self.H, self.dv)
+        z = p[:, c_end:c_end + self.v_dim]
+        b = p[:, c_end + self.v_dim:c_end + self.v_dim + self.H].float()
+        a = p[:, c_end + self.v_dim + self.H:].float()
+        beta = torch.sigmoid(b)
+        g = -self.A_log.exp() * F.softplus(a + self.dt_bias)
+        o = ctx.delta_rule(q, k, v, g, beta)
+        o = gated_rms_norm(o.reshape(T, self.v_dim), z, self.out_norm, self.H, self.eps)
+        return linear(o, self.proj)
+
+
+class HybridLayer(nn.Module):
+    def __init__(self, cfg: HybridConfig, symbol: str, dtype, device, gen):
+        super().__init__()
+        self.symbol = symbol
+        self.mixer = (GQAMixer if symbol == "*" else GDNMixer)(cfg, dtype, device, gen)
+        self.mlp = MLP(cfg, dtype, device, gen)
+
+    def forward(self, x, ctx, mlp_ctx=None):
+        x = x + self.mixer(x, ctx)
+        if mlp_ctx is None or mlp_ctx is ctx:
+            return x + self.mlp(x)
+        # joint plans may run the MLP in a different ownership layout
+        moved = mlp_ctx.enter(x, ctx)
+        return x + mlp_ctx.leave(self.mlp(moved), ctx)
+
+
+class HybridModel(nn.Module):
+    def __init__(self, cfg: HybridConfig, dtype=torch.bfloat16, device="cpu", seed: int = 0,
+                 layers: range | None = None, pre_process: bool = True, post_process: bool = True):
+        super().__init__()
+        self.cfg = cfg
+        gen = torch.Generator(device="cpu")
+        gen.manual_seed(seed)
+        pattern = cfg.pattern
+        # Parameters are created for every layer in order so that a pipeline
+        # stage owning ``layers`` gets bitwise the same weights as the full model.
+        self.layer_ids = list(layers if layers is not None else range(cfg.num_layers))
+        self.pre_process, self.post_process = pre_process, post_process
+        emb = _normal((cfg.vocab_size, cfg.hidden_size), cfg.init_method_std, dtype, device, gen)
+        self.embedding = emb if pre_process else None
+        built = nn.ModuleList()
+        for i, symbol in enumerate(pattern):
+            layer = HybridLayer(cfg, symbol, dtype, device, gen)
+            if i in self.layer_ids:
+                built.append(layer)
+        self.layers = built
+        self.final_norm = nn.Parameter(torch.ones(cfg.hidden_size, dtype=dtype, device=device))
+        head = _normal((cfg.vocab_size, cfg.hidden_size), cfg.init_method_std, dtype, device, gen)
+        self.head = head if post_process else None
+        if not post_process:
+            self.final_norm = None
+
+    @property
+    def pattern(self) -> str:
+        return "".join(layer.symbol for layer in self.layers)
+
+    def embed(self, tokens):
+        return F.embedding(tokens, self.embedding)
+
+    def run_layers(self, x, contexts, mlp_contexts=None):
+        for i, layer in enumerate(self.layers):
+            x = layer(x, contexts[i], None if mlp_contexts is None else mlp_contexts[i])
+        return x
+
+    def loss(self, x, labels, token_weight):
+        y = rms_norm(x, self.final_norm, self.cfg.norm_epsilon)
+        return head_cross_entropy(y, self.head, labels, token_weight)
+
+    def forward(self, tokens, labels, token_weight, contexts, mlp_contexts=None):
+        x = self.embed(tokens)
+        x = self.run_layers(x, contexts, mlp_contexts)
+        return self.loss(x, labels, token_weight)

@@ -1,0 +1,53 @@
+"""Loader for the in-tree sm_100a kernel library ``prism_cp_b200._C``.
+
+CUDA tensors always go through the compiled kernels; if the library is missing
+on a machine with a GPU the first CUDA op raises instead of silently falling
+back to PyTorch. CPU tensors use the plain PyTorch formulations in each op
+module (fp32 oracle and the gloo/CPU plumbing path).
+"""
+
+from __future__ import annotations
+
+import functools
+import importlib
+
+import torch
+
+
+class KernelLibraryMissing(RuntimeError):
+    pass
+
+
+@functools.lru_cache(maxsize=1)
+def lib():
+    try:
+        return importlib.import_module("prism_cp_b200._C")
+    except ImportError as error:  # pragma: no cover - exercised on GPU hosts only
+        raise KernelLibraryMissing(
+            "prism_cp_b200._C is not built; run `python -m prism_cp_b200.csrc.build` "
+            "(CUDA ops never fall back to PyTorch)") from error
+
+
+_STATUS: dict[int, torch.Tensor] = {}
+
+
+def status(device: torch.device) -> torch.Tensor:
+    """Per-device int32 word that bounded device waits write an error code into."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    word = _STATUS.get(index)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
+        _STATUS[index] = word
+    return word
+
+
+def check_status(device: torch.device) -> None:
+    """Raise if any kernel on `device` recorded a timeout (synchronises)."""
+    code = int(status(device).item())
+    if code:
+        status(device).zero_()
+        raise RuntimeError(f"device wait timed out in a prism kernel (code {code})")
+
+
+def is_cuda(*tensors) -> bool:
+    return any(t is not None and t.is_cuda for t in tensors)

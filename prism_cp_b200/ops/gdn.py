@@ -1,0 +1,217 @@
+"""Chunked gated delta rule (the Gated-DeltaNet recurrence).
+
+Per head, with log-decay ``g_t <= 0``, ``beta_t`` in (0, 1) and state ``S`` of shape
+``[dk, dv]`` (outputs ``o_t = S_t^T q_t``)::
+
+    S_t = exp(g_t) (I - beta_t k_t k_t^T) S_{t-1} + beta_t k_t v_t^T
+
+This is the recurrence of Yang et al. (Gated Delta Networks, 2024), the same op
+as FLA's ``chunk_gated_delta_rule`` that the reference trains through
+(oracle: ``experiments/performance_model/module_bench.py:148-160``). It is
+evaluated in chunks of 64 tokens in the WY form: with in-chunk cumulative decay
+``G`` and ``L_ij = beta_i exp(G_i - G_j) k_i.k_j`` (i > j)::
+
+    Delta = (I + L)^-1 (beta V) - (I + L)^-1 (beta e^G K) S_c   = U - W S_c
+    S_{c+1} = e^{G_last} S_c + (e^{G_last - G} K)^T Delta
+    O = (e^G Q) S_c + tril(Q K^T * e^{G_i - G_j}) Delta
+
+The chunk-parallel algebra runs as batched tensor products; the sequential
+state pass is ``_StatePass`` (CUDA kernels in ``csrc/gdn_state.cu``, a chunk
+loop on CPU). Sequences are padded to whole chunks with ``beta = g = 0``
+tokens, which leave the state untouched. ``initial_state`` / ``final_state``
+carry the recurrent state across context-parallel ranks.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._lib import is_cuda, lib
+
+CHUNK = 64
+
+
+# ---------------------------------------------------------------- state pass
+def _state_pass_reference(W, U, Kd, gamma, S0, seq_chunks):
+    Nc, H, C, DK = W.shape
+    DV = U.shape[-1]
+    nseq = len(seq_chunks) - 1
+    Delta = torch.empty_like(U)
+    S_all = torch.empty((Nc, H, DK, DV), dtype=W.dtype, device=W.device)
+    S_final = torch.empty((nseq, H, DK, DV), dtype=W.dtype, device=W.device)
+    for s in range(nseq):
+        S = S0[s].clone() if S0 is not None else torch.zeros((H, DK, DV), dtype=W.dtype, device=W.device)
+        for c in range(seq_chunks[s], seq_chunks[s + 1]):
+            S_all[c] = S
+            d = U[c] - W[c] @ S
+            Delta[c] = d
+            S = gamma[c][:, None, None] * S + Kd[c].transpose(-1, -2) @ d
+        S_final[s] = S
+    return Delta, S_all, S_final
+
+
+def _state_pass_backward_reference(W, dDelta_ext, Kd, gamma, dS_ext, dS_final, seq_chunks):
+    Nc, H, C, DK = W.shape
+    DV = dDelta_ext.shape[-1]
+    nseq = len(seq_chunks) - 1
+    dDelta = torch.empty_like(dDelta_ext)
+    G_next = torch.empty((Nc, H, DK, DV), dtype=W.dtype, device=W.device)
+    dS0 = torch.empty((nseq, H, DK, DV), dtype=W.dtype, device=W.device)
+    for s in range(nseq):
+        G = dS_final[s].clone() if dS_final is not None else torch.zeros((H, DK, DV), dtype=W.dtype,
+                                                                          device=W.device)
+        for c in range(seq_chunks[s + 1] - 1, seq_chunks[s] - 1, -1):
+            G_next[c] = G
+            dd = dDelta_ext[c] + Kd[c] @ G
+            dDelta[c] = dd
+            G = dS_ext[c] + gamma[c][:, None, None] * G - W[c].transpose(-1, -2) @ dd
+        dS0[s] = G
+    return dDelta, G_next, dS0
+
+
+class _StatePass(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, W, U, Kd, gamma, S0, seq_chunks, seq_chunks_dev):
+        W, U, Kd, gamma = (t.contiguous() for t in (W, U, Kd, gamma))
+        if W.is_cuda:
+            Nc, H, C, DK = W.shape
+            DV = U.shape[-1]
+            nseq = len(seq_chunks) - 1
+            Delta = torch.empty_like(U)
+            S_all = torch.empty((Nc, H, DK, DV), dtype=torch.float32, device=W.device)
+            S_final = torch.empty((nseq, H, DK, DV), dtype=torch.float32, device=W.device)
+            lib().gdn_state_fwd(W, U, Kd, gamma, S0.contiguous() if S0 is not None else None,
+                                seq_chunks_dev, Delta, S_all, S_final)
+        else:
+            Delta, S_all, S_final = _state_pass_reference(W, U, Kd, gamma, S0, seq_chunks)
+        ctx.save_for_backward(W, Kd, gamma, S_all, Delta)
+        ctx.seq_chunks, ctx.seq_chunks_dev = seq_chunks, seq_chunks_dev
+        ctx.has_s0 = S0 is not None
+        return Delta, S_all, S_final
+
+    @staticmethod
+    def backward(ctx, dDelta_ext, dS_ext, dS_final):
+        W, Kd, gamma, S_all, Delta = ctx.saved_tensors
+        if dDelta_ext is None:
+            dDelta_ext = torch.zeros_like(Delta)
+        if dS_ext is None:
+            dS_ext = torch.zeros_like(S_all)
+        dDelta_ext, dS_ext = dDelta_ext.contiguous(), dS_ext.contiguous()
+        if W.is_cuda:
+            dDelta = torch.empty_like(dDelta_ext)
+            G_next = torch.empty_like(S_all)
+            dS0 = torch.empty((len(ctx.seq_chunks) - 1,) + S_all.shape[1:], dtype=torch.float32, device=W.device)
+            lib().gdn_state_bwd(W, dDelta_ext, Kd, gamma, dS_ext,
+                                dS_final.contiguous() if dS_final is not None else None,
+                                ctx.seq_chunks_dev, dDelta, G_next, dS0)
+        else:
+            dDelta, G_next, dS0 = _state_pass_backward_reference(W, dDelta_ext, Kd, gamma, dS_ext, dS_final,
+                                                                 ctx.seq_chunks)
+        # chunk-local gradients: dU = dDelta, dW = -dDelta S^T, dKd = Delta G^T, dgamma = <S, G>
+        dU = dDelta
+        dW = -(dDelta @ S_all.transpose(-1, -2))
+        dKd = Delta @ G_next.transpose(-1, -2)
+        dgamma = (S_all * G_next).sum(dim=(-1, -2))
+        return dW, dU, dKd, dgamma, (dS0 if ctx.has_s0 else None), None, None
+
+
+# ---------------------------------------------------------------- packing helpers
+class ChunkLayout:
+    """Maps packed varlen tokens to whole 64-token chunks (per sequence padding)."""
+
+    def __init__(self, lengths: tuple[int, ...], device):
+        self.lengths = tuple(int(n) for n in lengths)
+        chunks = [(n + CHUNK - 1) // CHUNK for n in self.lengths]
+        self.seq_chunks = [0]
+        for c in chunks:
+            self.seq_chunks.append(self.seq_chunks[-1] + c)
+        self.num_chunks = self.seq_chunks[-1]
+        index = []
+        offset = 0
+        for n, c in zip(self.lengths, chunks):
+            base = len(index)
+            index.extend(range(offset, offset + n))
+            index.extend([-1] * (c * CHUNK - n))
+            offset += n
+        idx = torch.tensor(index, dtype=torch.int64)
+        self.valid = idx >= 0
+        self.padded_to_token = idx.clamp(min=0).to(device)
+        self.valid_dev = self.valid.to(device)
+        self.token_to_padded = torch.nonzero(self.valid).flatten().to(device)
+        self.aligned = bool(self.valid.all())
+        self.seq_chunks_dev = torch.tensor(self.seq_chunks, dtype=torch.int32, device=device)
+
+    def pad(self, x: torch.Tensor) -> torch.Tensor:
+        """[T, ...] -> [Nc, C, ...] with zeros in padded slots."""
+        if self.aligned:
+            return x.reshape(self.num_chunks, CHUNK, *x.shape[1:])
+        out = x.new_zeros((self.num_chunks * CHUNK,) + tuple(x.shape[1:]))
+        out = out.index_copy(0, self.token_to_padded, x)
+        return out.reshape(self.num_chunks, CHUNK, *x.shape[1:])
+
+    def unpad(self, y: torch.Tensor) -> torch.Tensor:
+        flat = y.reshape(self.num_chunks * CHUNK, *y.shape[2:])
+        if self.aligned:
+            return flat
+        return flat.index_select(0, self.token_to_padded)
+
+
+def chunk_gated_delta_rule(q, k, v, g, beta, layout: ChunkLayout, scale: float | None = None,
+                           initial_state: torch.Tensor | None = None):
+    """Return ``(o, final_state)``.
+
+    q, k: [T, H, dk]; v: [T, H, dv]; g (log decay), beta: [T, H];
+    initial_state / final_state: [nseq, H, dk, dv] fp32.
+    """
+    T, H, DK = q.shape
+    scale = DK ** -0.5 if scale is None else scale
+    f32 = torch.float32
+    # [Nc, H, C, d]
+    Q = layout.pad(q.to(f32)).permute(0, 2, 1, 3) * scale
+    K = layout.pad(k.to(f32)).permute(0, 2, 1, 3)
+    V = layout.pad(v.to(f32)).permute(0, 2, 1, 3)
+    gl = layout.pad(g.to(f32)).permute(0, 2, 1)           # [Nc, H, C]
+    bt = layout.pad(beta.to(f32)).permute(0, 2, 1)        # [Nc, H, C]
+    G = gl.cumsum(-1)
+    diff = G[..., :, None] - G[..., None, :]              # G_i - G_j
+    lower = torch.ones((CHUNK, CHUNK), dtype=torch.bool, device=q.device).tril()
+    decay = torch.where(lower, diff, torch.zeros_like(diff)).exp() * lower
+    strict = decay * (~torch.eye(CHUNK, dtype=torch.bool, device=q.device))
+    KK = K @ K.transpose(-1, -2)
+    A = torch.eye(CHUNK, dtype=f32, device=q.device) + bt[..., :, None] * KK * strict
+    rhs = torch.cat([bt[..., None] * G.exp()[..., None] * K, bt[..., None] * V], dim=-1)
+    sol = torch.linalg.solve_triangular(A, rhs, upper=False, unitriangular=True)
+    W, U = sol[..., :DK], sol[..., DK:]
+    G_last = G[..., -1:]
+    Kd = (G_last - G).exp()[..., None] * K
+    gamma = G_last[..., 0].exp()
+    Delta, S_all, S_final = _StatePass.apply(W, U, Kd, gamma, initial_state, layout.seq_chunks,
+                                             layout.seq_chunks_dev)
+    QK = (Q @ K.transpose(-1, -2)) * decay
+    O = (G.exp()[..., None] * Q) @ S_all + QK @ Delta      # [Nc, H, C, dv]
+    o = layout.unpad(O.permute(0, 2, 1, 3))
+    return o.to(v.dtype), S_final
+
+
+def naive_gated_delta_rule(q, k, v, g, beta, lengths, scale=None, initial_state=None):
+    """Token-by-token fp64 oracle of the same recurrence (tests only)."""
+    T, H, DK = q.shape
+    DV = v.shape[-1]
+    scale = DK ** -0.5 if scale is None else scale
+    out = torch.zeros((T, H, DV), dtype=torch.float64)
+    finals = []
+    off = 0
+    for s, n in enumerate(lengths):
+        S = (initial_state[s].double().clone() if initial_state is not None
+             else torch.zeros((H, DK, DV), dtype=torch.float64))
+        for t in range(off, off + n):
+            kt, vt, qt = k[t].double(), v[t].double(), q[t].double() * scale
+            a = g[t].double().exp()[:, None, None]
+            b = beta[t].double()
+            S = a * S
+            pred = torch.einsum("hk,hkv->hv", kt, S)
+            S = S + torch.einsum("hk,hv->hkv", kt, b[:, None] * (vt - pred))
+            out[t] = torch.einsum("hk,hkv->hv", qt, S)
+        finals.append(S)
+        off += n
+    return out, torch.stack(finals)

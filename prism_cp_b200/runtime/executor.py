@@ -1,0 +1,58 @@
+"""Plan-driven executor: runs one microbatch of a joint plan through the model.
+
+For every layer the hidden rows are resharded from the previous layer's
+attention layout to this layer's attention layout (identity routes are free),
+the mixer runs with its ``LocalLayout`` (ring attention / GDN state passing
+over the layer's CP team), the MLP optionally runs in its own placement, and
+before the head the rows return to the ingress layout so labels and loss
+weights line up (reference: joint_cp/adapter.py:125-186, without Megatron
+monkeypatching). Local layouts are cached per (layout, lengths).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ..parallel.layout import LocalLayout
+from ..parallel.transport import move
+from ..planner.joint.ir import Microbatch
+
+
+class LayoutCache:
+    def __init__(self, world: int, rank: int, device, teams=None):
+        self.world, self.rank, self.device, self.teams = world, rank, device, teams
+        self._cache: dict = {}
+
+    def get(self, layout, lengths: dict) -> LocalLayout:
+        key = (layout, tuple(sorted(lengths.items())))
+        hit = self._cache.get(key)
+        if hit is None:
+            if len(self._cache) > 4096:
+                self._cache.clear()
+            hit = LocalLayout(layout, lengths, self.world, self.rank, self.device, self.teams)
+            self._cache[key] = hit
+        return hit
+
+
+class MicrobatchRun:
+    def __init__(self, mb: Microbatch, lengths: dict, cache: LayoutCache, first_layer: int = 0,
+                 num_layers: int | None = None):
+        self.lengths = {s: lengths[s] for g in mb.ingress.groups for s in g.samples}
+        self.ingress = cache.get(mb.ingress, self.lengths)
+        layers = mb.layers[first_layer:first_layer + num_layers] if num_layers else mb.layers[first_layer:]
+        self.contexts = [cache.get(a, self.lengths) for a, _ in layers]
+        self.mlp_contexts = [None if m == a else cache.get(m, self.lengths) for a, m in layers]
+
+    def forward_layers(self, model, x, start_ctx=None):
+        prev = start_ctx or self.ingress
+        for layer, ctx, mctx in zip(model.layers, self.contexts, self.mlp_contexts):
+            x = move(x, prev, ctx)
+            x = layer(x, ctx, mctx)
+            prev = ctx
+        return x, prev
+
+    def forward(self, model, tokens, labels, weights):
+        x = model.embed(tokens)
+        x, prev = self.forward_layers(model, x)
+        x = move(x, prev, self.ingress)
+        return model.loss(x, labels, weights)

@@ -1,0 +1,168 @@
+"""Distributed AdamW over flat buffers (Megatron ``--use-distributed-optimizer``).
+
+All model parameters become views into one flat bf16 buffer and every
+parameter gets a ``main_grad`` view into one flat fp32 gradient buffer (the
+linear layers accumulate their weight gradients straight into it from the
+GEMM epilogue). The flat buffers are padded to a multiple of the world size;
+rank r owns shard r: fp32 master weights, Adam m and v. One update is
+
+    reduce-scatter(grad, SUM) -> shard grad          (NCCL; gloo on CPU)
+    sumsq(shard grad) -> all-reduce(SUM)             (device scalar, no host sync)
+    AdamW(shard) with clip coef = min(1, max_norm / ||g||)   (one kernel)
+    all-gather(bf16 shard) -> flat bf16 params
+
+Gradient buckets (``bucket_bytes``) let the reduce-scatter of finished layers
+overlap the rest of the backward on a side stream (``--overlap-grad-reduce``).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from ..ops._lib import is_cuda, lib
+
+
+class FlatParameters:
+    def __init__(self, model: torch.nn.Module, world: int, dtype=torch.bfloat16):
+        params = [p for p in model.parameters() if p.requires_grad]
+        self.params = params
+        device = params[0].device
+        total = sum(p.numel() for p in params)
+        align = 128 * world
+        self.padded = (total + align - 1) // align * align
+        self.numel = total
+        self.flat = torch.zeros(self.padded, dtype=dtype, device=device)
+        self.grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
+        self.offsets = []
+        off = 0
+        for p in params:
+            n = p.numel()
+            view = self.flat[off:off + n].view_as(p)
+            view.copy_(p.detach().to(dtype))
+            p.data = view
+            p.main_grad = self.grad[off:off + n].view_as(p)
+            self.offsets.append((off, n))
+            off += n
+        # decoupled weight decay only on matrices (Megatron excludes norms/biases/1-D)
+        self.decay_mask = torch.zeros(self.padded, dtype=torch.bool, device=device)
+        for p, (o, n) in zip(params, self.offsets):
+            if p.dim() >= 2:
+                self.decay_mask[o:o + n] = True
+
+    def zero_grad(self):
+        self.grad.zero_()
+        for p in self.params:
+            p.grad = None
+
+    def fold_param_grads(self):
+        """Accumulate autograd ``.grad`` of params whose ops do not write main_grad."""
+        for p in self.params:
+            if p.grad is not None:
+                p.main_grad.add_(p.grad.to(torch.float32))
+                p.grad = None
+
+
+class DistributedAdamW:
+    def __init__(self, flat: FlatParameters, group=None, lr=3e-4, min_lr=3e-5, betas=(0.9, 0.95), eps=1e-8,
+                 weight_decay=0.1, clip_grad=1.0, warmup_steps=0, decay_steps=1000, decay_style="cosine"):
+        self.flat = flat
+        self.group = group
+        self.world = dist.get_world_size(group) if (dist.is_available() and dist.is_initialized()) else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        self.shard_size = flat.padded // self.world
+        lo = self.rank * self.shard_size
+        self.lo, self.hi = lo, lo + self.shard_size
+        self.master = flat.flat[lo:self.hi].to(torch.float32).clone()
+        self.m = torch.zeros_like(self.master)
+        self.v = torch.zeros_like(self.master)
+        self.grad_shard = torch.zeros_like(self.master)
+        self.wd_mask = flat.decay_mask[lo:self.hi].to(torch.float32)
+        self.sumsq = torch.zeros(1, dtype=torch.float32, device=self.master.device)
+        self.lr, self.min_lr, self.betas, self.eps = lr, min_lr, betas, eps
+        self.weight_decay, self.clip_grad = weight_decay, clip_grad
+        self.warmup_steps, self.decay_steps, self.decay_style = warmup_steps, decay_steps, decay_style
+        self.step_count = 0
+        self.stats = {"reduce_scatter_bytes": 0, "all_gather_bytes": 0}
+
+    # -------------------------------------------------------------- schedule
+    def current_lr(self, step: int) -> float:
+        if self.warmup_steps and step <= self.warmup_steps:
+            return self.lr * step / self.warmup_steps
+        if self.decay_style == "constant":
+            return self.lr
+        t = min(1.0, max(0.0, (step - self.warmup_steps) / max(1, self.decay_steps)))
+        if self.decay_style == "linear":
+            return self.min_lr + (self.lr - self.min_lr) * (1 - t)
+        return self.min_lr + 0.5 * (self.lr - self.min_lr) * (1 + math.cos(math.pi * t))
+
+    # -------------------------------------------------------------- collectives
+    def reduce_gradients(self):
+        g = self.flat.grad
+        if self.world > 1:
+            dist.reduce_scatter_tensor(self.grad_shard, g, op=dist.ReduceOp.SUM, group=self.group)
+            self.stats["reduce_scatter_bytes"] += g.numel() * 4
+        else:
+            self.grad_shard.copy_(g)
+
+    def gather_parameters(self):
+        shard = self.flat.flat[self.lo:self.hi]
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.flat.flat, shard.clone(), group=self.group)
+            self.stats["all_gather_bytes"] += self.flat.flat.numel() * self.flat.flat.element_size()
+
+    # -------------------------------------------------------------- update
+    def grad_norm_sq(self) -> torch.Tensor:
+        self.sumsq.zero_()
+        if is_cuda(self.grad_shard):
+            lib().sumsq_accumulate(self.grad_shard, self.sumsq)
+        else:
+            self.sumsq += self.grad_shard.pow(2).sum()
+        if self.world > 1:
+            dist.all_reduce(self.sumsq, op=dist.ReduceOp.SUM, group=self.group)
+        return self.sumsq
+
+    def step(self):
+        self.flat.fold_param_grads()
+        self.reduce_gradients()
+        self.grad_norm_sq()
+        self.step_count += 1
+        lr = self.current_lr(self.step_count)
+        b1, b2 = self.betas
+        bc1, bc2 = 1 - b1 ** self.step_count, 1 - b2 ** self.step_count
+        shard_bf16 = self.flat.flat[self.lo:self.hi]
+        if is_cuda(self.master):
+            # decoupled weight decay on matrices first (p *= 1 - lr*wd), then one fused
+            # AdamW launch that also writes the bf16 shard; a non-finite norm skips it
+            if self.weight_decay:
+                self.master.mul_(1.0 - lr * self.weight_decay * self.wd_mask)
+            lib().adamw_step(self.master, self.grad_shard, self.m, self.v, shard_bf16, self.sumsq, self.clip_grad,
+                             lr, b1, b2, self.eps, 0.0, bc1, bc2)
+        else:
+            ss = float(self.sumsq.item())
+            coef = min(1.0, self.clip_grad / (math.sqrt(ss) + 1e-6)) if self.clip_grad > 0 else 1.0
+            if math.isfinite(ss):
+                g = self.grad_shard * coef
+                self.master.mul_(1.0 - lr * self.weight_decay * self.wd_mask)
+                self.m.mul_(b1).add_(g, alpha=1 - b1)
+                self.v.mul_(b2).addcmul_(g, g, value=1 - b2)
+                self.master.sub_(lr * ((self.m / bc1) / ((self.v / bc2).sqrt() + self.eps)))
+                shard_bf16.copy_(self.master)
+        self.gather_parameters()
+        return lr
+
+    def state_dict(self):
+        return {"master": self.master, "m": self.m, "v": self.v, "step": self.step_count,
+                "rank": self.rank, "world": self.world, "lo": self.lo, "hi": self.hi}
+
+    def load_state_dict(self, state):
+        if state["world"] != self.world or state["lo"] != self.lo:
+            raise ValueError("optimizer shard layout differs from the checkpoint")
+        self.master.copy_(state["master"])
+        self.m.copy_(state["m"])
+        self.v.copy_(state["v"])
+        self.step_count = int(state["step"])
+        self.flat.flat[self.lo:self.hi].copy_(self.master)
+        self.gather_parameters()

@@ -1,0 +1,103 @@
+"""Training step over a plan: microbatch loop, gradient sync, AdamW, guards.
+
+``Trainer.train_step(batch, plan)`` is the public entry point: it copies each
+microbatch's inputs from (pinned) host memory, runs forward/backward through
+the plan-driven executor, accumulates fp32 gradients, reduce-scatters them,
+clips, applies the distributed AdamW and all-gathers the parameters, then
+returns a ``StepResult``. Guards follow the reference's contract
+(experiments/sequence_dynamic_cp/runtime.py:392-518): finite loss/grad check,
+HBM admission ``peak + external <= min(0.9 total, total - 8 GiB)`` agreed across
+ranks with an all-reduce MIN, and rank-max step time.
+"""
+
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+from ..planner.joint.ir import Plan
+from .batch import GlobalBatch, HostInputs, local_inputs
+from .executor import LayoutCache, MicrobatchRun
+from .optimizer import DistributedAdamW, FlatParameters
+
+
+def hbm_budget(total_bytes: int) -> int:
+    return min(int(0.9 * total_bytes), total_bytes - 8 * 1024 ** 3)
+
+
+@dataclass
+class StepResult:
+    loss: float
+    loss_tensor: torch.Tensor
+    tokens: int
+    microbatches: int
+    lr: float
+    elapsed_ms: float | None = None
+    grad_norm: float | None = None
+    peak_allocated: int | None = None
+    admitted: bool = True
+    extra: dict = field(default_factory=dict)
+
+
+class Trainer:
+    def __init__(self, model, teams, device, lr=3e-4, min_lr=3e-5, weight_decay=0.1, clip_grad=1.0,
+                 warmup_steps=0, decay_steps=1000, group=None, hbm_guard=True):
+        self.model, self.teams, self.device = model, teams, device
+        self.world = teams.world
+        self.rank = teams.rank
+        self.flat = FlatParameters(model, self.world)
+        self.optimizer = DistributedAdamW(self.flat, group=group, lr=lr, min_lr=min_lr,
+                                          weight_decay=weight_decay, clip_grad=clip_grad,
+                                          warmup_steps=warmup_steps, decay_steps=decay_steps)
+        self.cache = LayoutCache(self.world, self.rank, device, teams)
+        self.hbm_guard = hbm_guard and device.type == "cuda"
+        self.loss_acc = torch.zeros((), dtype=torch.float32, device=device)
+
+    # ------------------------------------------------------------------ inputs
+    def prepare(self, batch: GlobalBatch, plan: Plan, pin: bool = True) -> list[HostInputs]:
+        return [local_inputs(batch, mb.ingress, self.world, self.rank, pin=pin and self.device.type == "cuda")
+                for mb in plan.microbatches]
+
+    # ------------------------------------------------------------------ step
+    def forward_backward(self, batch_lengths: dict, plan: Plan, inputs: list):
+        self.loss_acc.zero_()
+        for mb, host in zip(plan.microbatches, inputs):
+            dev = host.to(self.device) if host.tokens.device != self.device else host
+            run = MicrobatchRun(mb, batch_lengths, self.cache)
+            loss, _ = run.forward(self.model, dev.tokens, dev.labels, dev.weights)
+            loss.backward()
+            self.loss_acc += loss.detach()
+        if self.world > 1:
+            dist.all_reduce(self.loss_acc, op=dist.ReduceOp.SUM)
+        return self.loss_acc
+
+    def train_step(self, batch: GlobalBatch, plan: Plan, inputs: list | None = None,
+                   read_loss: bool = True) -> StepResult:
+        if inputs is None:
+            inputs = self.prepare(batch, plan)
+        self.flat.zero_grad()
+        loss = self.forward_backward(batch.lengths, plan, inputs)
+        lr = self.optimizer.step()
+        value = float(loss.item()) if read_loss else float("nan")
+        if read_loss and not math.isfinite(value):
+            raise FloatingPointError("non-finite loss in training step")
+        return StepResult(value, loss, batch.total_tokens, len(plan.microbatches), lr)
+
+    # ------------------------------------------------------------------ guards
+    def admission(self) -> tuple[bool, dict]:
+        if not self.hbm_guard:
+            return True, {}
+        free, total = torch.cuda.mem_get_info(self.device)
+        peak = torch.cuda.max_memory_allocated(self.device)
+        reserved = torch.cuda.memory_reserved(self.device)
+        external = max(0, total - free - reserved)
+        required = peak + external
+        budget = hbm_budget(total)
+        ok = torch.tensor([1 if required <= budget else 0], dtype=torch.int32, device=self.device)
+        if self.world > 1:
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        return bool(ok.item()), dict(peak_allocated=peak, external=external, required=required, budget=budget)
