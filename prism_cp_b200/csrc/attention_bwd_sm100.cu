@@ -185,14 +185,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         dsum_s[r] = v ? p.dsum[(long)h * p.tq + q_seg + qq] : 0.f;
       }
       named_sync_compute();
-      if (!mbar_wait_bounded(s_full, it & 1, abort_flag, p.status, kTimeoutEpilogue)) {
-        ok = false;
-        break;
-      }
-      if (it > 0 && !mbar_wait_bounded(mma_done, (it - 1) & 1, abort_flag, p.status, kTimeoutEpilogue)) {
-        ok = false;
-        break;
-      }
+      bool waited = mbar_wait_bounded(s_full, it & 1, abort_flag, p.status, kTimeoutEpilogue);
+      if (waited && it > 0) waited = mbar_wait_bounded(mma_done, (it - 1) & 1, abort_flag, p.status, kTimeoutEpilogue);
+      ok = named_barrier_and(waited, 1, 128);
+      if (!ok) break;
       tc_fence_after();
       const bool row_ok = kk < k_len;
 #pragma unroll 1
@@ -230,14 +226,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_arrive(p_full);
     }
     if (ok && n_it > 0) ok = mbar_wait_bounded(acc_done, 0, abort_flag, p.status, kTimeoutEpilogue);
+    ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    if (kk < k_len) {
+    {
+      // every thread of the warp takes part in tcgen05.ld; only rows inside the sequence store
+      const bool store = kk < k_len;
+      const bool loaded = __all_sync(0xffffffffu, n_it > 0 && ok);
       __nv_bfloat16* dv_row = p.out2 + (long)(k_seg + kk) * p.out_stride + (long)kv_head * D;
       __nv_bfloat16* dk_row = p.out + (long)(k_seg + kk) * p.out_stride + (long)kv_head * D;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t a[32], b[32];
-        if (n_it > 0 && ok) {
+        if (loaded) {
           tmem_ld_32x32b_x32(lane_base + 256 + c * 32, a);
           tmem_ld_32x32b_x32(lane_base + 384 + c * 32, b);
           tmem_wait_ld();
@@ -245,6 +245,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) a[e] = b[e] = 0u;
         }
+        if (!store) continue;
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           reinterpret_cast<uint4*>(dv_row + c * 32)[v] = make_uint4(
@@ -379,10 +380,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const float dsum = row_ok ? p.dsum[(long)head * p.tq + q_seg + qq] : 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv && ok; ++j) {
-      if (!mbar_wait_bounded(s_full, j & 1, abort_flag, p.status, kTimeoutEpilogue)) {
-        ok = false;
-        break;
-      }
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(s_full, j & 1, abort_flag, p.status, kTimeoutEpilogue));
+      if (!ok) break;
       tc_fence_after();
       const int kbase = j * TILE;
 #pragma unroll 1
@@ -412,19 +411,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_arrive(ds_full);
     }
     if (ok && n_kv > 0) ok = mbar_wait_bounded(acc_done, 0, abort_flag, p.status, kTimeoutEpilogue);
+    ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    if (row_ok) {
+    {
+      const bool loaded = __all_sync(0xffffffffu, n_kv > 0 && ok);
       __nv_bfloat16* dq_row = p.out + (long)(q_seg + qq) * p.out_stride + (long)head * D;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t a[32];
-        if (n_kv > 0 && ok) {
+        if (loaded) {
           tmem_ld_32x32b_x32(lane_base + 256 + c * 32, a);
           tmem_wait_ld();
         } else {
 #pragma unroll
           for (int e = 0; e < 32; ++e) a[e] = 0u;
         }
+        if (!row_ok) continue;
 #pragma unroll
         for (int v = 0; v < 4; ++v)
           reinterpret_cast<uint4*>(dq_row + c * 32)[v] = make_uint4(

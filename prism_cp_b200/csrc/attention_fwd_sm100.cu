@@ -194,10 +194,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int j = 0; j < n_kv && ok; ++j) {
       const int s = j & 1;
       const uint32_t ph = (j >> 1) & 1;
-      if (!mbar_wait_bounded(&s_full[s], ph, abort_flag, p.status, kTimeoutEpilogue)) {
-        ok = false;
-        break;
-      }
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[s], ph, abort_flag, p.status, kTimeoutEpilogue));
+      if (!ok) break;
       tc_fence_after();
       float sv[128];
 #pragma unroll
@@ -233,9 +231,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float mm = (m == -INFINITY) ? 0.f : m;
       float rowsum = 0.f;
       // P_j may only be written after PV_{j-1} finished reading P_{j-1}
-      if (j > 0 && !mbar_wait_bounded(pv_done, (j - 1) & 1, abort_flag, p.status, kTimeoutEpilogue)) {
-        ok = false;
-        break;
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(pv_done, (j - 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
+        if (!ok) break;
       }
       if (j > 0 && alpha != 1.f) {
         tc_fence_after();
@@ -269,6 +267,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     // epilogue
     if (ok && n_kv > 0) ok = mbar_wait_bounded(pv_done, (n_kv - 1) & 1, abort_flag, p.status, kTimeoutEpilogue);
+    ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     const bool row_valid = q_idx < q_len;
     const float inv_l = (l > 0.f) ? 1.f / l : 0.f;

@@ -215,6 +215,21 @@ PRISM_DEVICE void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
 PRISM_DEVICE void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 PRISM_DEVICE void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// AND-reduction of a predicate across `count` threads at named barrier `id`
+// (keeps every participant on the same control path after a bounded wait gives up).
+PRISM_DEVICE bool named_barrier_and(bool v, int id, int count) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
 PRISM_DEVICE bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

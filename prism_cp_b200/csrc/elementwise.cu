@@ -334,6 +334,7 @@ void rope_inplace(at::Tensor& x, const at::Tensor& pos, int64_t heads, int64_t d
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "rope: bf16 CUDA rows");
   TORCH_CHECK(pos.scalar_type() == at::kInt && pos.numel() == x.size(0), "rope: int32 positions [T]");
   TORCH_CHECK(d % 16 == 0, "rope: head dim multiple of 16");
+  TORCH_CHECK(x.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0, "rope: aligned rows");
   const c10::cuda::CUDAGuard guard(x.device());
   const int T = x.size(0);
   const long total = (long)T * heads * (d / 16);
@@ -399,6 +400,7 @@ std::vector<at::Tensor> conv1d_silu_bwd(const at::Tensor& dy, const at::Tensor& 
 void swiglu_fwd(const at::Tensor& x, at::Tensor& y) {
   const int T = x.size(0), F = x.size(1) / 2;
   TORCH_CHECK(F % 8 == 0 && x.stride(1) == 1 && y.stride(1) == 1, "swiglu: F multiple of 8, unit stride");
+  TORCH_CHECK(x.stride(0) % 8 == 0 && y.stride(0) % 8 == 0, "swiglu: row strides multiple of 8");
   const c10::cuda::CUDAGuard guard(x.device());
   const long total = (long)T * (F / 8);
   if (total == 0) return;
@@ -425,7 +427,7 @@ void ce_fused(at::Tensor& logits, const at::Tensor& labels, const at::Tensor& we
   TORCH_CHECK(logits.scalar_type() == at::kBFloat16 && logits.stride(1) == 1, "ce: bf16 logits rows");
   TORCH_CHECK(labels.scalar_type() == at::kLong && weight.scalar_type() == at::kFloat, "ce: int64 labels, fp32 w");
   const int R = logits.size(0), V = logits.size(1);
-  TORCH_CHECK(V % 8 == 0, "ce: vocab multiple of 8");
+  TORCH_CHECK(V % 8 == 0 && logits.stride(0) % 8 == 0, "ce: vocab and row stride multiples of 8");
   const c10::cuda::CUDAGuard guard(logits.device());
   if (R == 0) return;
   ce_fused_kernel<<<R, kCeThreads, 0, at::cuda::getCurrentCUDAStream()>>>(

@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t tph = (local >> 1) & 1;
-      if (!mbar_wait_bounded(&tfull[buf], tph, abort_flag, p.status, kTimeoutEpilogue)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&tfull[buf], tph, abort_flag, p.status, kTimeoutEpilogue))) break;
       tc_fence_after();
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);

@@ -160,6 +160,7 @@ void check_rows(const at::Tensor& t, const char* name, int n) {
   TORCH_CHECK(t.stride(-1) == 1, name, ": unit inner stride required");
   TORCH_CHECK(n % 8 == 0, name, ": normalised length must be a multiple of 8");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, name, ": 16-byte alignment required");
+  TORCH_CHECK(t.dim() < 2 || (t.stride(0) % 8) == 0, name, ": row stride must be a multiple of 8 elements");
 }
 
 }  // namespace

@@ -55,8 +55,10 @@ class HybridConfig:
 
     @property
     def gdn_in_proj(self) -> int:
-        # q, k (qk dim each), v, output gate z (v dim each), beta and decay logits (heads each)
-        return 2 * self.gdn_qk_dim + 2 * self.gdn_v_dim + 2 * self.linear_num_key_heads
+        # q, k (qk dim each), v, output gate z (v dim each), beta and decay logits (heads
+        # each), rounded up to a multiple of 8 columns so every row starts 16-byte aligned
+        width = 2 * self.gdn_qk_dim + 2 * self.gdn_v_dim + 2 * self.linear_num_key_heads
+        return (width + 7) // 8 * 8
 
     @property
     def qkv_dim(self) -> int:

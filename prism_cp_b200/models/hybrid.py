@@ -107,7 +107,7 @@ class GDNMixer(nn.Module):
         v = qkv[:, 2 * self.qk_dim:].view(T, self.H, self.dv)
         z = p[:, c_end:c_end + self.v_dim]
         b = p[:, c_end + self.v_dim:c_end + self.v_dim + self.H].float()
-        a = p[:, c_end + self.v_dim + self.H:].float()
+        a = p[:, c_end + self.v_dim + self.H:c_end + self.v_dim + 2 * self.H].float()
         beta = torch.sigmoid(b)
         g = -self.A_log.exp() * F.softplus(a + self.dt_bias)
         o = ctx.delta_rule(q, k, v, g, beta)

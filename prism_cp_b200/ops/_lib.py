@@ -51,3 +51,11 @@ def check_status(device: torch.device) -> None:
 
 def is_cuda(*tensors) -> bool:
     return any(t is not None and t.is_cuda for t in tensors)
+
+
+def aligned_rows(t: torch.Tensor) -> torch.Tensor:
+    """``t`` if its rows are 16-byte aligned with unit inner stride, else a contiguous copy."""
+    if t.stride(-1) == 1 and t.data_ptr() % 16 == 0 and all(
+            (t.stride(d) * t.element_size()) % 16 == 0 for d in range(t.dim() - 1)):
+        return t
+    return t.contiguous()

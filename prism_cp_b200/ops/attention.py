@@ -113,7 +113,41 @@ class _FlashAttention(torch.autograd.Function):
         return dq, dk, dv, None, None
 
 
+def reference_attention_backward(q, k, v, out, lse, dout, meta: AttentionMeta, scale: float):
+    """fp32 oracle of the flash backward given the (possibly ring-merged) out and LSE."""
+    Tq, Hq, d = q.shape
+    Hkv = k.shape[1]
+    rep = Hq // Hkv
+    dq = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
+    dk = torch.zeros(k.shape, dtype=torch.float32, device=k.device)
+    dv = torch.zeros(v.shape, dtype=torch.float32, device=v.device)
+    oq = ok = 0
+    for lq, lk in zip(meta.q_lens, meta.k_lens):
+        qs = q[oq:oq + lq].float().transpose(0, 1)
+        ks = k[ok:ok + lk].float().transpose(0, 1).repeat_interleave(rep, 0)
+        vs = v[ok:ok + lk].float().transpose(0, 1).repeat_interleave(rep, 0)
+        do = dout[oq:oq + lq].float().transpose(0, 1)
+        o = out[oq:oq + lq].float().transpose(0, 1)
+        s = qs @ ks.transpose(1, 2) * scale
+        if meta.causal:
+            mask = torch.ones((lq, lk), dtype=torch.bool, device=q.device).tril()
+            s = s.masked_fill(~mask, float("-inf"))
+        p = torch.nan_to_num(torch.exp(s - lse[:, oq:oq + lq, None]), nan=0.0)
+        dvs = p.transpose(1, 2) @ do
+        dp = do @ vs.transpose(1, 2)
+        ds = p * (dp - (do * o).sum(-1, keepdim=True))
+        dq[oq:oq + lq] = (ds @ ks * scale).transpose(0, 1)
+        dk[ok:ok + lk] = (ds.transpose(1, 2) @ qs * scale).reshape(Hkv, rep, lk, d).sum(1).transpose(0, 1)
+        dv[ok:ok + lk] = dvs.reshape(Hkv, rep, lk, d).sum(1).transpose(0, 1)
+        oq += lq
+        ok += lk
+    return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
+
+
 def attention_backward(q, k, v, out, lse, dout, meta, scale):
+    """Flash backward from the (global) out/LSE; the tcgen05 kernels on CUDA."""
+    if not is_cuda(q):
+        return reference_attention_backward(q, k, v, out, lse, dout, meta, scale)
     dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
     dkv = torch.empty((k.shape[0], 2, k.shape[1], k.shape[2]), device=k.device, dtype=k.dtype)
     dk, dv = dkv[:, 0], dkv[:, 1]

@@ -15,7 +15,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from ._lib import is_cuda, lib
+from ._lib import aligned_rows, is_cuda, lib
 
 
 # ---------------------------------------------------------------- RoPE
@@ -35,7 +35,7 @@ def _ref_rope(x, pos, heads, d, base, inverse):
 class _Rope(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, pos, heads, d, base):
-        y = x.clone() if x.stride(-1) == 1 else x.contiguous()
+        y = x.contiguous().clone() if x.is_contiguous() else x.contiguous()
         lib().rope_inplace(y, pos, heads, d, base, False)
         ctx.save_for_backward(pos)
         ctx.cfg = (heads, d, base)
@@ -132,4 +132,4 @@ def swiglu(x: torch.Tensor) -> torch.Tensor:
     if not is_cuda(x):
         a, b = x.float().chunk(2, dim=-1)
         return (F.silu(a) * b).to(x.dtype)
-    return _SwiGLU.apply(x if x.stride(-1) == 1 else x.contiguous())
+    return _SwiGLU.apply(aligned_rows(x))

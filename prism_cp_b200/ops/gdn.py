@@ -156,6 +156,59 @@ class ChunkLayout:
         return flat.index_select(0, self.token_to_padded)
 
 
+def chunk_prep(q, k, v, g, beta, layout: ChunkLayout, scale: float | None = None) -> dict:
+    """Chunk-parallel part: everything that does not depend on the initial state."""
+    T, H, DK = q.shape
+    scale = DK ** -0.5 if scale is None else scale
+    f32 = torch.float32
+    Q = layout.pad(q.to(f32)).permute(0, 2, 1, 3) * scale     # [Nc, H, C, dk]
+    K = layout.pad(k.to(f32)).permute(0, 2, 1, 3)
+    V = layout.pad(v.to(f32)).permute(0, 2, 1, 3)
+    gl = layout.pad(g.to(f32)).permute(0, 2, 1)                # [Nc, H, C]
+    bt = layout.pad(beta.to(f32)).permute(0, 2, 1)
+    G = gl.cumsum(-1)
+    diff = G[..., :, None] - G[..., None, :]                   # G_i - G_j
+    lower = torch.ones((CHUNK, CHUNK), dtype=torch.bool, device=q.device).tril()
+    decay = torch.where(lower, diff, torch.zeros_like(diff)).exp() * lower
+    strict = decay * (~torch.eye(CHUNK, dtype=torch.bool, device=q.device))
+    A = torch.eye(CHUNK, dtype=f32, device=q.device) + bt[..., :, None] * (K @ K.transpose(-1, -2)) * strict
+    rhs = torch.cat([bt[..., None] * G.exp()[..., None] * K, bt[..., None] * V], dim=-1)
+    sol = torch.linalg.solve_triangular(A, rhs, upper=False, unitriangular=True)
+    G_last = G[..., -1:]
+    return {"Q": Q, "K": K, "G": G, "decay": decay, "W": sol[..., :DK], "U": sol[..., DK:],
+            "Kd": (G_last - G).exp()[..., None] * K, "gamma": G_last[..., 0].exp(), "layout": layout,
+            "dtype": v.dtype}
+
+
+def chunk_state(prep: dict, initial_state: torch.Tensor | None = None):
+    """Sequential state pass: returns (Delta, S_all, S_final)."""
+    layout = prep["layout"]
+    return _StatePass.apply(prep["W"], prep["U"], prep["Kd"], prep["gamma"], initial_state, layout.seq_chunks,
+                            layout.seq_chunks_dev)
+
+
+def chunk_output(prep: dict, Delta, S_all):
+    Q, K, G = prep["Q"], prep["K"], prep["G"]
+    QK = (Q @ K.transpose(-1, -2)) * prep["decay"]
+    O = (G.exp()[..., None] * Q) @ S_all + QK @ Delta          # [Nc, H, C, dv]
+    return prep["layout"].unpad(O.permute(0, 2, 1, 3)).to(prep["dtype"])
+
+
+def chunk_transition(prep: dict, seq: int) -> torch.Tensor:
+    """[H, dk, dk] linear map from the initial to the final state of sequence
+    ``seq`` (the recurrence with zero values, started from the identity)."""
+    layout = prep["layout"]
+    c0, c1 = layout.seq_chunks[seq], layout.seq_chunks[seq + 1]
+    W, Kd, gamma = prep["W"][c0:c1], prep["Kd"][c0:c1], prep["gamma"][c0:c1]
+    H, DK = W.shape[1], W.shape[-1]
+    eye = torch.eye(DK, dtype=W.dtype, device=W.device).expand(1, H, DK, DK).contiguous()
+    zeros = torch.zeros(W.shape[:-1] + (DK,), dtype=W.dtype, device=W.device)
+    local = [0, c1 - c0]
+    dev = torch.tensor(local, dtype=torch.int32, device=W.device)
+    _, _, M = _StatePass.apply(W, zeros, Kd, gamma, eye, local, dev)
+    return M[0]
+
+
 def chunk_gated_delta_rule(q, k, v, g, beta, layout: ChunkLayout, scale: float | None = None,
                            initial_state: torch.Tensor | None = None):
     """Return ``(o, final_state)``.
@@ -163,34 +216,9 @@ def chunk_gated_delta_rule(q, k, v, g, beta, layout: ChunkLayout, scale: float |
     q, k: [T, H, dk]; v: [T, H, dv]; g (log decay), beta: [T, H];
     initial_state / final_state: [nseq, H, dk, dv] fp32.
     """
-    T, H, DK = q.shape
-    scale = DK ** -0.5 if scale is None else scale
-    f32 = torch.float32
-    # [Nc, H, C, d]
-    Q = layout.pad(q.to(f32)).permute(0, 2, 1, 3) * scale
-    K = layout.pad(k.to(f32)).permute(0, 2, 1, 3)
-    V = layout.pad(v.to(f32)).permute(0, 2, 1, 3)
-    gl = layout.pad(g.to(f32)).permute(0, 2, 1)           # [Nc, H, C]
-    bt = layout.pad(beta.to(f32)).permute(0, 2, 1)        # [Nc, H, C]
-    G = gl.cumsum(-1)
-    diff = G[..., :, None] - G[..., None, :]              # G_i - G_j
-    lower = torch.ones((CHUNK, CHUNK), dtype=torch.bool, device=q.device).tril()
-    decay = torch.where(lower, diff, torch.zeros_like(diff)).exp() * lower
-    strict = decay * (~torch.eye(CHUNK, dtype=torch.bool, device=q.device))
-    KK = K @ K.transpose(-1, -2)
-    A = torch.eye(CHUNK, dtype=f32, device=q.device) + bt[..., :, None] * KK * strict
-    rhs = torch.cat([bt[..., None] * G.exp()[..., None] * K, bt[..., None] * V], dim=-1)
-    sol = torch.linalg.solve_triangular(A, rhs, upper=False, unitriangular=True)
-    W, U = sol[..., :DK], sol[..., DK:]
-    G_last = G[..., -1:]
-    Kd = (G_last - G).exp()[..., None] * K
-    gamma = G_last[..., 0].exp()
-    Delta, S_all, S_final = _StatePass.apply(W, U, Kd, gamma, initial_state, layout.seq_chunks,
-                                             layout.seq_chunks_dev)
-    QK = (Q @ K.transpose(-1, -2)) * decay
-    O = (G.exp()[..., None] * Q) @ S_all + QK @ Delta      # [Nc, H, C, dv]
-    o = layout.unpad(O.permute(0, 2, 1, 3))
-    return o.to(v.dtype), S_final
+    prep = chunk_prep(q, k, v, g, beta, layout, scale)
+    Delta, S_all, S_final = chunk_state(prep, initial_state)
+    return chunk_output(prep, Delta, S_all), S_final
 
 
 def naive_gated_delta_rule(q, k, v, g, beta, lengths, scale=None, initial_state=None):

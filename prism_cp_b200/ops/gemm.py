@@ -12,7 +12,7 @@ from __future__ import annotations
 
 import torch
 
-from ._lib import is_cuda, lib, status
+from ._lib import aligned_rows, is_cuda, lib, status
 
 
 def _torch_mm(a, b, a_mn, b_mn):
@@ -39,8 +39,7 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool =
         return out
     if out is None:
         out = torch.empty((M, N), device=a.device, dtype=out_dtype or torch.bfloat16)
-    a = a if a.stride(-1) == 1 else a.contiguous()
-    b = b if b.stride(-1) == 1 else b.contiguous()
+    a, b = aligned_rows(a), aligned_rows(b)
     lib().gemm(a, b, out, a_mn, b_mn, accumulate, row_scale, status(a.device))
     return out
 

@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import torch
 
-from ._lib import is_cuda, lib
+from ._lib import aligned_rows, is_cuda, lib
 
 
 def _ref_rownorm(x, w, z, heads, n, inv_n, eps):
@@ -58,10 +58,9 @@ class _RowNorm(torch.autograd.Function):
 def _rownorm(x, w, z, heads, n, inv_n, eps):
     if not is_cuda(x):
         return _ref_rownorm(x, w, z, heads, n, inv_n, eps)
-    if x.stride(-1) != 1:
-        x = x.contiguous()
-    if z is not None and z.stride(-1) != 1:
-        z = z.contiguous()
+    x = aligned_rows(x)
+    if z is not None:
+        z = aligned_rows(z)
     return _RowNorm.apply(x, w, z, heads, n, inv_n, eps)
 
 

@@ -26,11 +26,18 @@ from ..ops._lib import is_cuda, lib
 
 
 class FlatParameters:
-    def __init__(self, model: torch.nn.Module, world: int, dtype=torch.bfloat16):
+    def __init__(self, model: torch.nn.Module, world: int, dtype=None):
         params = [p for p in model.parameters() if p.requires_grad]
         self.params = params
         device = params[0].device
-        total = sum(p.numel() for p in params)
+        # the flat buffer keeps the model's compute dtype (bf16 on GPU, fp32 for CPU oracles)
+        if dtype is None:
+            dtype = torch.bfloat16 if any(p.dtype == torch.bfloat16 for p in params) else params[0].dtype
+        # every parameter starts on a 128-byte boundary (TMA and vector kernels need
+        # 16-byte aligned operands); the gaps are zero and never updated
+        def slot(n):
+            return (n + 63) // 64 * 64
+        total = sum(slot(p.numel()) for p in params)
         align = 128 * world
         self.padded = (total + align - 1) // align * align
         self.numel = total
@@ -45,7 +52,7 @@ class FlatParameters:
             p.data = view
             p.main_grad = self.grad[off:off + n].view_as(p)
             self.offsets.append((off, n))
-            off += n
+            off += slot(n)
         # decoupled weight decay only on matrices (Megatron excludes norms/biases/1-D)
         self.decay_mask = torch.zeros(self.padded, dtype=torch.bool, device=device)
         for p, (o, n) in zip(params, self.offsets):
@@ -67,10 +74,13 @@ class FlatParameters:
 
 class DistributedAdamW:
     def __init__(self, flat: FlatParameters, group=None, lr=3e-4, min_lr=3e-5, betas=(0.9, 0.95), eps=1e-8,
-                 weight_decay=0.1, clip_grad=1.0, warmup_steps=0, decay_steps=1000, decay_style="cosine"):
+                 weight_decay=0.1, clip_grad=1.0, warmup_steps=0, decay_steps=1000, decay_style="cosine",
+                 world: int | None = None):
         self.flat = flat
         self.group = group
-        self.world = dist.get_world_size(group) if (dist.is_available() and dist.is_initialized()) else 1
+        if world is None:
+            world = dist.get_world_size(group) if (dist.is_available() and dist.is_initialized()) else 1
+        self.world = world
         self.rank = dist.get_rank(group) if self.world > 1 else 0
         self.shard_size = flat.padded // self.world
         lo = self.rank * self.shard_size

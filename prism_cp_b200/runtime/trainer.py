@@ -52,7 +52,7 @@ class Trainer:
         self.flat = FlatParameters(model, self.world)
         self.optimizer = DistributedAdamW(self.flat, group=group, lr=lr, min_lr=min_lr,
                                           weight_decay=weight_decay, clip_grad=clip_grad,
-                                          warmup_steps=warmup_steps, decay_steps=decay_steps)
+                                          warmup_steps=warmup_steps, decay_steps=decay_steps, world=self.world)
         self.cache = LayoutCache(self.world, self.rank, device, teams)
         self.hbm_guard = hbm_guard and device.type == "cuda"
         self.loss_acc = torch.zeros((), dtype=torch.float32, device=device)
