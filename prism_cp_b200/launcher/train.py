@@ -1,0 +1,117 @@
+"""Training entry point (``python -m prism_cp_b200.launcher.train <Megatron-style flags>``).
+
+Run one process per GPU under ``torchrun`` (``--master-addr 127.0.0.1`` on one
+box). Every update: build or load the global batch, plan it with the selected
+scheduler, and run ``Trainer.train_step``:
+
+* ``--sequence-packing-scheduler default_dynamic_cp``: native N with per-rank
+  capacity ``--max-seqlen-per-dp-cp-rank`` and ``--min-dynamic-context-parallel-size``,
+  rounds coalesced into mixed-CP microbatches;
+* ``joint``: the frozen replay rows of ``--joint-replay`` (validated against the
+  world and layer pattern);
+* ``fixed``: one CP degree ``--context-parallel-size`` for every layer.
+
+Data: ``--packet-manifest`` (deterministic LCG64 content with the first-half
+loss mask), ``--varlen-mock-dataset-config-json`` (log-normal or explicit
+lengths) or fixed ``--global-batch-size x --seq-length`` documents.
+"""
+
+from __future__ import annotations
+
+import datetime
+import json
+import os
+import sys
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+from ..models.hybrid import HybridModel
+from ..parallel.teams import Teams
+from ..planner.fixed import uniform_plan
+from ..planner.joint.replay import validate_replay
+from ..planner.mixed import to_joint
+from ..planner.native import replay as native_replay
+from ..planner.onedim import from_rank_ids
+from ..runtime import checkpoint
+from ..runtime.batch import fixed_lengths, lognormal_lengths, make_batch, manifest_batch
+from ..runtime.trainer import Trainer
+from .args import build_parser, model_config, validate
+
+
+def global_batch(args, world: int, step: int, pin: bool):
+    if args.packet_manifest:
+        manifest = json.loads(Path(args.packet_manifest).read_text())
+        from ..planner.inputs import validate_manifest
+        validate_manifest(manifest)
+        return manifest_batch(manifest, pin=pin)
+    if args.varlen_mock_dataset_config_json:
+        cfg = json.loads(Path(args.varlen_mock_dataset_config_json).read_text())
+        if "lengths" in cfg:
+            lengths = list(cfg["lengths"])
+        else:
+            lengths = lognormal_lengths(cfg.get("total_tokens", 1 << 20), cfg.get("median", 4096),
+                                        cfg.get("sigma", 1.0), cfg.get("min", 512), cfg.get("max", 131072),
+                                        2 * world, args.seed + step)
+        return make_batch(lengths, args.vocab_size, args.seed + step, pin=pin)
+    return make_batch(fixed_lengths(args.global_batch_size, args.seq_length), args.vocab_size, args.seed + step,
+                      pin=pin)
+
+
+def plan_for(args, batch, world: int, pattern: str, step: int, replays):
+    if args.sequence_packing_scheduler == "joint":
+        row = replays[(step - 1) % len(replays)]
+        plan = validate_replay(row, world, pattern)
+        if list(batch.lengths.values()) != row["expected_lengths"]:
+            raise SystemExit("joint replay lengths differ from the batch")
+        return plan
+    if args.sequence_packing_scheduler == "fixed":
+        cp = args.context_parallel_size or world
+        return uniform_plan(batch.lengths, world, cp, args.max_seqlen_per_dp_cp_rank, pattern)
+    rounds = from_rank_ids(native_replay(list(batch.lengths.items()), world, args.max_seqlen_per_dp_cp_rank,
+                                         args.min_dynamic_context_parallel_size))
+    return to_joint(rounds, batch.lengths, world, pattern, token_cap=args.max_seqlen_per_dp_cp_rank)
+
+
+def main(argv=None) -> int:
+    args = build_parser().parse_args(argv)
+    validate(args)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cuda = args.device == "cuda"
+    device = torch.device("cuda", local) if cuda else torch.device("cpu")
+    if cuda:
+        torch.cuda.set_device(device)
+    if world > 1:
+        backend = args.distributed_backend if cuda else "gloo"
+        dist.init_process_group(backend, device_id=device if cuda else None,
+                                timeout=datetime.timedelta(minutes=args.distributed_timeout_minutes))
+    cfg = model_config(args)
+    dtype = torch.bfloat16 if (args.bf16 and cuda) else torch.float32
+    model = HybridModel(cfg, dtype=dtype, device=device, seed=args.seed)
+    trainer = Trainer(model, Teams(world), device, lr=args.lr, min_lr=args.min_lr, weight_decay=args.weight_decay,
+                      clip_grad=args.clip_grad, warmup_steps=args.lr_warmup_iters,
+                      decay_steps=args.lr_decay_iters or args.train_iters, records=args.records)
+    replays = json.loads(Path(args.joint_replay).read_text()) if args.joint_replay else None
+    start = 1
+    if args.load and checkpoint.latest(args.load) is not None:
+        start = checkpoint.load(trainer, checkpoint.latest(args.load)) + 1
+    for step in range(start, args.train_iters + 1):
+        batch = global_batch(args, world, step, pin=cuda)
+        plan = plan_for(args, batch, world, cfg.pattern, step, replays)
+        res = trainer.train_step(batch, plan)
+        if rank == 0 and step % args.log_interval == 0:
+            print(json.dumps({"step": step, "loss": res.loss, "lr": res.lr, "tokens": res.tokens,
+                              "microbatches": res.microbatches}), flush=True)
+        if args.save and args.save_interval and step % args.save_interval == 0:
+            checkpoint.save(trainer, args.save, plan_cursor=step)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

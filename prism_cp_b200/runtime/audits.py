@@ -1,0 +1,121 @@
+"""Run-time audits: collective inventory, accumulation ordering, input integrity.
+
+* ``CommunicationAudit`` records every torch.distributed collective issued
+  inside its context (name, shapes, bytes, group size, caller) - the
+  reference's one-step collective inventory (communication_audit.py:8-63).
+* ``AccumulationAudit`` checks the update contract the reference enforces
+  around Megatron's DDP (accumulation_audit.py:8-174): no gradient
+  reduce-scatter before the last backward of the update, exactly one
+  reduce-scatter, one optimizer step and one parameter all-gather per update,
+  and the loss-token count.
+* ``check_packet_inputs`` compares a rank's materialised tokens, labels,
+  positions and loss mask exactly with the deterministic content rule
+  (stream_integrity.py / mixed_packet_integrity.py).
+"""
+
+from __future__ import annotations
+
+import contextlib
+import traceback
+
+import torch
+import torch.distributed as dist
+
+_COLLECTIVES = ("all_reduce", "all_gather", "all_gather_into_tensor", "reduce_scatter_tensor", "all_to_all_single",
+                "broadcast", "barrier", "batch_isend_irecv", "send", "recv", "isend", "irecv")
+
+
+def _nbytes(obj) -> int:
+    if isinstance(obj, torch.Tensor):
+        return obj.numel() * obj.element_size()
+    if isinstance(obj, (list, tuple)):
+        return sum(_nbytes(x) for x in obj)
+    if isinstance(obj, dist.P2POp):
+        return _nbytes(obj.tensor)
+    return 0
+
+
+class CommunicationAudit(contextlib.AbstractContextManager):
+    def __init__(self, stacks: bool = False):
+        self.events: list[dict] = []
+        self.stacks = stacks
+        self._saved = {}
+
+    def __enter__(self):
+        for name in _COLLECTIVES:
+            fn = getattr(dist, name, None)
+            if fn is None:
+                continue
+            self._saved[name] = fn
+
+            def wrapper(*args, __fn=fn, __name=name, **kwargs):
+                group = kwargs.get("group")
+                size = dist.get_world_size(group) if dist.is_initialized() else 1
+                ev = {"op": __name, "bytes": sum(_nbytes(a) for a in args), "group_size": size,
+                      "shapes": [list(a.shape) for a in args if isinstance(a, torch.Tensor)]}
+                if self.stacks:
+                    ev["stack"] = traceback.format_stack(limit=6)[:-1]
+                self.events.append(ev)
+                return __fn(*args, **kwargs)
+
+            setattr(dist, name, wrapper)
+        return self
+
+    def __exit__(self, *exc):
+        for name, fn in self._saved.items():
+            setattr(dist, name, fn)
+        return False
+
+    def summary(self) -> dict:
+        out: dict = {}
+        for ev in self.events:
+            row = out.setdefault(ev["op"], {"calls": 0, "bytes": 0})
+            row["calls"] += 1
+            row["bytes"] += ev["bytes"]
+        return out
+
+
+class AccumulationAudit:
+    """Event log of one update with the ordering rules of a complete update."""
+
+    def __init__(self):
+        self.events: list[tuple] = []
+
+    def backward(self, microbatch: int):
+        self.events.append(("backward", microbatch))
+
+    def reduce_scatter(self, nbytes: int):
+        self.events.append(("reduce_scatter", nbytes))
+
+    def optimizer_step(self):
+        self.events.append(("optimizer_step",))
+
+    def all_gather(self, nbytes: int):
+        self.events.append(("all_gather", nbytes))
+
+    def check(self, microbatches: int, loss_tokens: int | None = None, observed_loss_tokens: int | None = None):
+        kinds = [e[0] for e in self.events]
+        backwards = [i for i, k in enumerate(kinds) if k == "backward"]
+        rs = [i for i, k in enumerate(kinds) if k == "reduce_scatter"]
+        if len(backwards) != microbatches:
+            raise AssertionError(f"expected {microbatches} backward passes, saw {len(backwards)}")
+        if len(rs) != 1 or rs[0] < backwards[-1]:
+            raise AssertionError("gradient reduce-scatter must run once, after the last backward")
+        if kinds.count("optimizer_step") != 1 or kinds.index("optimizer_step") < rs[0]:
+            raise AssertionError("exactly one optimizer step after the reduce-scatter")
+        if kinds.count("all_gather") != 1 or kinds.index("all_gather") < kinds.index("optimizer_step"):
+            raise AssertionError("exactly one parameter all-gather after the optimizer step")
+        if loss_tokens is not None and observed_loss_tokens != loss_tokens:
+            raise AssertionError(f"loss tokens {observed_loss_tokens} != {loss_tokens}")
+        return True
+
+
+def check_packet_inputs(source, update: int, ingress_layout, world: int, rank: int, tokens, labels, positions,
+                        weights) -> None:
+    """Exact comparison of one rank's inputs with the manifest's content rule."""
+    t, l, p, w = source.rank_inputs(update, ingress_layout, world, rank)
+    for name, a, b in (("tokens", tokens, t), ("labels", labels, l), ("positions", positions, p)):
+        if not torch.equal(a.cpu().to(b.dtype), b):
+            raise AssertionError(f"input integrity: {name} differ from the deterministic content rule")
+    if not torch.equal(weights.cpu().float() > 0, w > 0):
+        raise AssertionError("input integrity: loss mask differs from the content rule")

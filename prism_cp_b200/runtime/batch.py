@@ -27,6 +27,7 @@ class GlobalBatch:
     tokens: dict[int, torch.Tensor]     # host int64 [L] (pinned when built for CUDA)
     labels: dict[int, torch.Tensor]
     loss_tokens: int
+    masks: dict[int, torch.Tensor] | None = None   # optional per-token loss mask (1 = counted)
 
     @property
     def total_tokens(self) -> int:
@@ -86,7 +87,25 @@ def local_inputs(batch: GlobalBatch, ingress_layout, world: int, rank: int, pin:
     rows = spans(ingress_layout, batch.lengths, world)[rank]
     t = torch.cat([batch.tokens[s][b:b + c] for s, b, _, c in rows]) if rows else torch.empty(0, dtype=torch.int64)
     l = torch.cat([batch.labels[s][b:b + c] for s, b, _, c in rows]) if rows else torch.empty(0, dtype=torch.int64)
-    w = torch.full((t.numel(),), 1.0 / batch.loss_tokens, dtype=torch.float32)
+    if batch.masks is None:
+        w = torch.full((t.numel(),), 1.0 / batch.loss_tokens, dtype=torch.float32)
+    else:
+        m = torch.cat([batch.masks[s][b:b + c] for s, b, _, c in rows]) if rows else torch.empty(0)
+        w = m.float() / batch.loss_tokens
     if pin:
         t, l, w = t.pin_memory(), l.pin_memory(), w.pin_memory()
     return HostInputs(t, l, w)
+
+
+def manifest_batch(manifest: dict, pin: bool = False) -> GlobalBatch:
+    """Whole-update batch of a ``joint_cp_inputs_v1`` manifest (LCG64 content, first-half loss mask)."""
+    from ..planner.content import vector_fields
+    toks, labs, masks = {}, {}, {}
+    for s in manifest["samples"]:
+        f = vector_fields(manifest, s["sample_id"], torch.arange(s["length"]))
+        t, l, m = f["tokens"], f["labels"], f["loss_mask"] > 0
+        if pin:
+            t, l = t.pin_memory(), l.pin_memory()
+        toks[s["sample_id"]], labs[s["sample_id"]], masks[s["sample_id"]] = t, l, m
+    lengths = {s["sample_id"]: s["length"] for s in manifest["samples"]}
+    return GlobalBatch(lengths, toks, labs, manifest["loss_tokens"], masks)

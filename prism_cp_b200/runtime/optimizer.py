@@ -96,6 +96,7 @@ class DistributedAdamW:
         self.warmup_steps, self.decay_steps, self.decay_style = warmup_steps, decay_steps, decay_style
         self.step_count = 0
         self.stats = {"reduce_scatter_bytes": 0, "all_gather_bytes": 0}
+        self.audit = None
 
     # -------------------------------------------------------------- schedule
     def current_lr(self, step: int) -> float:
@@ -116,12 +117,16 @@ class DistributedAdamW:
             self.stats["reduce_scatter_bytes"] += g.numel() * 4
         else:
             self.grad_shard.copy_(g)
+        if self.audit is not None:
+            self.audit.reduce_scatter(g.numel() * 4)
 
     def gather_parameters(self):
         shard = self.flat.flat[self.lo:self.hi]
         if self.world > 1:
             dist.all_gather_into_tensor(self.flat.flat, shard.clone(), group=self.group)
             self.stats["all_gather_bytes"] += self.flat.flat.numel() * self.flat.flat.element_size()
+        if self.audit is not None:
+            self.audit.all_gather(self.flat.flat.numel() * self.flat.flat.element_size())
 
     # -------------------------------------------------------------- update
     def grad_norm_sq(self) -> torch.Tensor:
@@ -139,6 +144,8 @@ class DistributedAdamW:
         self.reduce_gradients()
         self.grad_norm_sq()
         self.step_count += 1
+        if self.audit is not None:
+            self.audit.optimizer_step()
         lr = self.current_lr(self.step_count)
         b1, b2 = self.betas
         bc1, bc2 = 1 - b1 ** self.step_count, 1 - b2 ** self.step_count

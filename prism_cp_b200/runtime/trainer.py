@@ -20,9 +20,11 @@ import torch
 import torch.distributed as dist
 
 from ..planner.joint.ir import Plan
+from .audits import AccumulationAudit
 from .batch import GlobalBatch, HostInputs, local_inputs
 from .executor import LayoutCache, MicrobatchRun
 from .optimizer import DistributedAdamW, FlatParameters
+from .records import StepRecorder, step_record
 
 
 def hbm_budget(total_bytes: int) -> int:
@@ -45,7 +47,8 @@ class StepResult:
 
 class Trainer:
     def __init__(self, model, teams, device, lr=3e-4, min_lr=3e-5, weight_decay=0.1, clip_grad=1.0,
-                 warmup_steps=0, decay_steps=1000, group=None, hbm_guard=True):
+                 warmup_steps=0, decay_steps=1000, group=None, hbm_guard=True, records: str | None = None,
+                 numerics=None, audit: bool = False):
         self.model, self.teams, self.device = model, teams, device
         self.world = teams.world
         self.rank = teams.rank
@@ -56,6 +59,10 @@ class Trainer:
         self.cache = LayoutCache(self.world, self.rank, device, teams)
         self.hbm_guard = hbm_guard and device.type == "cuda"
         self.loss_acc = torch.zeros((), dtype=torch.float32, device=device)
+        self.recorder = StepRecorder(records, self.rank) if records else None
+        self.numerics = numerics
+        self.audit = AccumulationAudit() if audit else None
+        self.step_index = 0
 
     # ------------------------------------------------------------------ inputs
     def prepare(self, batch: GlobalBatch, plan: Plan, pin: bool = True) -> list[HostInputs]:
@@ -70,6 +77,8 @@ class Trainer:
             run = MicrobatchRun(mb, batch_lengths, self.cache)
             loss, _ = run.forward(self.model, dev.tokens, dev.labels, dev.weights)
             loss.backward()
+            if self.audit is not None:
+                self.audit.backward(len(self.audit.events))
             self.loss_acc += loss.detach()
         if self.world > 1:
             dist.all_reduce(self.loss_acc, op=dist.ReduceOp.SUM)
@@ -79,13 +88,70 @@ class Trainer:
                    read_loss: bool = True) -> StepResult:
         if inputs is None:
             inputs = self.prepare(batch, plan)
+        track = self.recorder is not None or self.audit is not None
+        if track:
+            return self._tracked_step(batch, plan, inputs)
         self.flat.zero_grad()
         loss = self.forward_backward(batch.lengths, plan, inputs)
         lr = self.optimizer.step()
+        self.step_index += 1
         value = float(loss.item()) if read_loss else float("nan")
         if read_loss and not math.isfinite(value):
             raise FloatingPointError("non-finite loss in training step")
         return StepResult(value, loss, batch.total_tokens, len(plan.microbatches), lr)
+
+    def _tracked_step(self, batch: GlobalBatch, plan: Plan, inputs: list) -> StepResult:
+        """A step with records, audit and guards (reference: runtime.py:392-518)."""
+        cuda = self.device.type == "cuda"
+        if cuda:
+            torch.cuda.synchronize(self.device)
+            torch.cuda.reset_peak_memory_stats(self.device)
+        if self.world > 1:
+            dist.barrier()
+        external_before = self._external() if cuda else 0
+        t0 = time.perf_counter()
+        if self.audit is not None:
+            self.audit.events.clear()
+        self.flat.zero_grad()
+        loss = self.forward_backward(batch.lengths, plan, inputs)
+        if self.audit is not None:
+            self.optimizer.audit = self.audit
+        lr = self.optimizer.step()
+        self.step_index += 1
+        if cuda:
+            torch.cuda.synchronize(self.device)
+        local_ms = (time.perf_counter() - t0) * 1000
+        elapsed = torch.tensor([local_ms], dtype=torch.float64, device=self.device)
+        if self.world > 1:
+            dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
+        value = float(loss.item())
+        grad_norm = float(self.optimizer.sumsq.sqrt().item())
+        finite_ok = math.isfinite(value) and math.isfinite(grad_norm)
+        admitted, mem = self.admission()
+        if self.numerics is not None:
+            self.numerics.observe(self.step_index, self.optimizer)
+        if self.audit is not None:
+            self.audit.check(len(plan.microbatches))
+        if self.recorder is not None:
+            self.recorder.write(step_record(
+                self.step_index, value, grad_norm, float(elapsed.item()), local_ms, tokens=batch.total_tokens,
+                loss_tokens=batch.loss_tokens, samples=len(batch.lengths), microbatches=len(plan.microbatches),
+                peak_allocated=mem.get("peak_allocated", 0),
+                peak_reserved=torch.cuda.max_memory_reserved(self.device) if cuda else 0,
+                memory_budget=mem.get("budget", 0), memory_required=mem.get("required", 0), admitted=admitted,
+                external_before=external_before, external_after=mem.get("external", 0),
+                sync=dict(self.optimizer.stats), finite=finite_ok))
+        if not finite_ok:
+            raise FloatingPointError("non-finite loss or gradient norm in training step")
+        if not admitted:
+            raise RuntimeError(f"HBM admission rejected the step: {mem}")
+        return StepResult(value, loss, batch.total_tokens, len(plan.microbatches), lr,
+                          elapsed_ms=float(elapsed.item()), grad_norm=grad_norm,
+                          peak_allocated=mem.get("peak_allocated"), admitted=admitted, extra=mem)
+
+    def _external(self) -> int:
+        free, total = torch.cuda.mem_get_info(self.device)
+        return max(0, total - free - torch.cuda.memory_reserved(self.device))
 
     # ------------------------------------------------------------------ guards
     def admission(self) -> tuple[bool, dict]:

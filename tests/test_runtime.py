@@ -1,0 +1,102 @@
+"""Trainer records, audits, contracts and guards on CPU."""
+
+import json
+
+import pytest
+import torch
+
+from prism_cp_b200.models.config import hybrid_tiny
+from prism_cp_b200.models.hybrid import HybridModel
+from prism_cp_b200.parallel.teams import Teams
+from prism_cp_b200.planner.fixed import uniform_plan
+from prism_cp_b200.runtime import numerics, records
+from prism_cp_b200.runtime.audits import AccumulationAudit, CommunicationAudit
+from prism_cp_b200.runtime.batch import make_batch
+from prism_cp_b200.runtime.trainer import Trainer
+
+
+def _trainer(tmp_path, **kw):
+    cfg = hybrid_tiny()
+    model = HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0)
+    batch = make_batch([256, 128, 128], cfg.vocab_size, seed=1)
+    plan = uniform_plan(batch.lengths, 1, 1, 256, cfg.pattern)
+    return Trainer(model, Teams(1), torch.device("cpu"), **kw), batch, plan
+
+
+def test_records_audit_and_summary(tmp_path):
+    tr, batch, plan = _trainer(tmp_path, records=str(tmp_path), audit=True)
+    losses = [tr.train_step(batch, plan).loss for _ in range(3)]
+    assert losses[-1] < losses[0]
+    rows = [json.loads(x) for x in (tmp_path / "steps_rank0.jsonl").read_text().splitlines()]
+    assert [r["step"] for r in rows] == [1, 2, 3] and all(r["finite"] for r in rows)
+    records.compress(tmp_path, 1)
+    manifest = {"input_tokens": batch.total_tokens, "loss_tokens": batch.loss_tokens}
+    summary = records.summarize_records(tmp_path, manifest, 3, [2, 3], len(plan.microbatches), world=1)
+    assert summary["status"] == "complete" and len(summary["rankmax_seconds"]) == 2
+
+
+def test_accumulation_audit_rejects_early_reduce_scatter():
+    audit = AccumulationAudit()
+    audit.backward(0)
+    audit.reduce_scatter(10)
+    audit.backward(1)
+    audit.optimizer_step()
+    audit.all_gather(10)
+    with pytest.raises(AssertionError, match="after the last backward"):
+        audit.check(2)
+
+
+def test_communication_audit_counts_nothing_without_collectives(tmp_path):
+    tr, batch, plan = _trainer(tmp_path)
+    with CommunicationAudit() as audit:
+        tr.train_step(batch, plan)
+    assert audit.summary() == {}
+
+
+def test_contracts_are_frozen_and_gate_compares(tmp_path):
+    c = numerics.contract("cp_bf16_v2")
+    assert c["optimizer"]["gradients"]["relative"] == 0.06
+    path = tmp_path / "c.json"
+    path.write_text(json.dumps(c))
+    assert numerics.load_contract(path) == c
+    c["logical"]["decoder_Y"] = 0.5
+    path.write_text(json.dumps(c))
+    with pytest.raises(ValueError, match="frozen"):
+        numerics.load_contract(path)
+    tr, batch, plan = _trainer(tmp_path)
+    gate_w = numerics.TrainingNumerics(tmp_path / "ref", "write", steps=2)
+    for step in (1, 2):
+        tr.train_step(batch, plan)
+        gate_w.observe(step, tr.optimizer)
+    tr2, _, _ = _trainer(tmp_path)
+    gate_r = numerics.TrainingNumerics(tmp_path / "run", "read", reference=tmp_path / "ref", steps=2)
+    for step in (1, 2):
+        tr2.train_step(batch, plan)
+        gate_r.observe(step, tr2.optimizer)
+    assert not gate_r.failures
+    assert records.finite({"a": [1.0, torch.ones(2)]}) and not records.finite([float("nan")])
+
+
+def test_checkpoint_resume_restores_training_state(tmp_path):
+    from prism_cp_b200.runtime import checkpoint
+    tr, batch, plan = _trainer(tmp_path)
+    tr.train_step(batch, plan)
+    checkpoint.save(tr, tmp_path / "ck", plan_cursor=1)
+    after_save = tr.train_step(batch, plan).loss
+    tr2, _, _ = _trainer(tmp_path)
+    cursor = checkpoint.load(tr2, checkpoint.latest(tmp_path / "ck"))
+    assert cursor == 1 and tr2.optimizer.step_count == 1
+    assert abs(tr2.train_step(batch, plan).loss - after_save) < 1e-6
+
+
+def test_launcher_runs_native_and_fixed_schedulers(capsys):
+    from prism_cp_b200.launcher.train import main
+    common = ["--device", "cpu", "--num-layers", "4", "--hidden-size", "256", "--ffn-hidden-size", "512",
+              "--vocab-size", "4096", "--num-attention-heads", "4", "--num-query-groups", "2", "--kv-channels", "64",
+              "--linear-num-key-heads", "4", "--linear-num-value-heads", "4", "--linear-key-head-dim", "64",
+              "--linear-value-head-dim", "64", "--global-batch-size", "3", "--seq-length", "256",
+              "--max-seqlen-per-dp-cp-rank", "512", "--train-iters", "2"]
+    assert main(common) == 0
+    assert main(common + ["--sequence-packing-scheduler", "fixed", "--context-parallel-size", "1"]) == 0
+    lines = [json.loads(x) for x in capsys.readouterr().out.splitlines() if x.startswith("{")]
+    assert len(lines) == 4 and all(x["tokens"] == 768 for x in lines)
