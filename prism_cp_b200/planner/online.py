@@ -1,0 +1,146 @@
+"""Online per-batch CP selection (new capability; the reference left it unimplemented).
+
+For every global batch, before it runs, choose a CP degree separately for the
+GDN and the GQA layers from ``degrees`` (default {1, 2, 4, 8}) and pack the
+documents into microbatches, scoring each candidate plan with the joint cost
+and memory model (``joint.cost.Evaluator``, optionally calibrated by a B200
+response profile). Candidates:
+
+* ``(cp_gdn, cp_gqa)`` for every pair of degrees: documents are packed longest
+  first into microbatches whose per-rank tokens stay within the memory-derived
+  capacity at the larger degree; GDN layers use ``world / cp_gdn`` contiguous
+  teams, GQA layers ``world / cp_gqa`` zigzag teams over the same samples, so
+  every GDN<->GQA boundary with different degrees is a CP-transition reshard;
+* documents longer than a team can hold at a degree raise that degree for the
+  batch (the degree is the minimum that fits the longest document).
+
+The selection is deterministic (same lengths -> same plan on every rank), costs
+milliseconds of CPU per batch, and returns the plan with its predicted update
+time and the degree pair, so the executor can apply it without touching
+process groups (all dyadic teams exist from start-up).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+from .joint.cost import Evaluator, Model
+from .joint.ir import Group, Layout, Microbatch, Plan, validate_plan
+
+
+@dataclass(frozen=True)
+class Selection:
+    plan: Plan
+    cp_gdn: int
+    cp_gqa: int
+    predicted_update_ms: float
+    candidates: tuple
+
+
+def _pack(lengths: dict, order, capacity_tokens: int, groups: int):
+    """Greedy longest-first packing into microbatches of ``groups`` bins of
+    ``capacity_tokens`` tokens each (a bin = one team's share of the world)."""
+    batches = []
+    pending = list(order)
+    while pending:
+        bins = [[] for _ in range(groups)]
+        loads = [0] * groups
+        rest = []
+        for s in pending:
+            j = min(range(groups), key=lambda i: (loads[i], i))
+            if loads[j] + lengths[s] <= capacity_tokens or not bins[j]:
+                bins[j].append(s)
+                loads[j] += lengths[s]
+            else:
+                rest.append(s)
+        if any(not b for b in bins):
+            merged = sorted(s for b in bins for s in b)
+            bins = [merged]
+        batches.append([tuple(sorted(b)) for b in bins])
+        if len(rest) == len(pending):
+            raise ValueError("no progress while packing")
+        pending = rest
+    return batches
+
+
+def _split(samples, lengths, parts: int):
+    bins = [[] for _ in range(parts)]
+    loads = [0] * parts
+    for s in sorted(samples, key=lambda s: (-lengths[s], s)):
+        j = min(range(parts), key=lambda i: (loads[i], i))
+        bins[j].append(s)
+        loads[j] += lengths[s]
+    if any(not b for b in bins):
+        return None
+    return [tuple(sorted(b)) for b in bins]
+
+
+def candidate_plan(lengths: dict, world: int, pattern: str, cp_gdn: int, cp_gqa: int, capacity: int):
+    """Plan with GDN teams of ``cp_gdn`` and GQA teams of ``cp_gqa`` ranks, or None."""
+    coarse = max(cp_gdn, cp_gqa)
+    fine = min(cp_gdn, cp_gqa)
+    for n in lengths.values():
+        if coarse > 1 and n % (2 * coarse):
+            return None
+        if fine > 1 and n % (2 * fine):
+            return None
+    order = sorted(lengths, key=lambda s: (-lengths[s], s))
+    if max(lengths.values()) > capacity * coarse:
+        return None
+    mbs = []
+    for coarse_bins in _pack(lengths, order, capacity * coarse, world // coarse):
+        if len(coarse_bins) != world // coarse:
+            return None
+        fine_bins = []
+        ratio = coarse // fine
+        for b in coarse_bins:
+            parts = _split(b, lengths, ratio) if ratio > 1 else [b]
+            if parts is None or any(sum(lengths[s] for s in p) > capacity * fine for p in parts):
+                return None
+            fine_bins.extend(parts)
+        def lay(cp, bins, mode):
+            return Layout(tuple(Group(tuple(range(i * cp, (i + 1) * cp)), tuple(b)) for i, b in enumerate(bins)),
+                          mode)
+        g_bins = coarse_bins if cp_gdn == coarse else fine_bins
+        a_bins = coarse_bins if cp_gqa == coarse else fine_bins
+        gdn = lay(cp_gdn, g_bins, "contiguous")
+        gqa = lay(cp_gqa, a_bins, "zigzag")
+        layers = tuple((gdn, gdn) if c == "G" else (gqa, gqa) for c in pattern)
+        mbs.append(Microbatch(gqa, layers))
+    plan = Plan(world, pattern, tuple(mbs))
+    validate_plan(plan, lengths)
+    return plan
+
+
+def select(lengths: dict, world: int, pattern: str, model: Model, degrees=(1, 2, 4, 8),
+           capacity: int | None = None) -> Selection:
+    """Best (cp_gdn, cp_gqa) plan for this batch under ``model``."""
+    degrees = tuple(d for d in degrees if d <= world and world % d == 0)
+    if capacity is None:
+        capacity = max(1, model.token_capacity_upper_bound(pattern, world) // world)
+    ev = Evaluator(model, lengths, world, pattern)
+    rows = []
+    best = None
+    for cg in degrees:
+        for ca in degrees:
+            try:
+                plan = candidate_plan(lengths, world, pattern, cg, ca, capacity)
+            except ValueError:
+                plan = None
+            if plan is None:
+                continue
+            evid = [ev.evaluate(mb) for mb in plan.microbatches]
+            if not all(e["fits"] for e in evid):
+                rows.append({"cp_gdn": cg, "cp_gqa": ca, "fits": False})
+                continue
+            ms = sum(e["predicted_ms"] for e in evid) + model.update_ms
+            rows.append({"cp_gdn": cg, "cp_gqa": ca, "fits": True, "predicted_update_ms": ms,
+                         "microbatches": len(plan.microbatches)})
+            key = (ms, cg, ca)
+            if best is None or key < best[0]:
+                best = (key, plan, cg, ca, ms)
+    if best is None:
+        raise ValueError("no candidate CP pair fits this batch")
+    _, plan, cg, ca, ms = best
+    return Selection(plan, cg, ca, ms, tuple(rows))

@@ -1,0 +1,33 @@
+"""Online per-batch CP selection."""
+
+from prism_cp_b200.planner.joint import Model
+from prism_cp_b200.planner.joint.cost import model_from_config
+from prism_cp_b200.planner.joint.ir import validate_plan
+from prism_cp_b200.planner.online import candidate_plan, select
+from prism_cp_b200.runtime.batch import lognormal_lengths
+from prism_cp_b200.models.config import hybrid_1p3b
+
+
+def test_every_candidate_is_a_valid_plan():
+    lengths = dict(enumerate([4096, 2048, 1024, 1024, 512, 512, 8192, 256]))
+    for cg in (1, 2, 4, 8):
+        for ca in (1, 2, 4, 8):
+            plan = candidate_plan(lengths, 8, "GGG*GGG*", cg, ca, 8192)
+            if plan is not None:
+                validate_plan(plan, lengths)
+
+
+def test_selection_is_deterministic_and_prefers_cp1_for_short_documents():
+    model = Model()
+    short = dict(enumerate([2048] * 64))
+    sel = select(short, 8, "GGG*GGG*", model)
+    assert (sel.cp_gdn, sel.cp_gqa) == (1, 1)
+    assert select(short, 8, "GGG*GGG*", model).plan == sel.plan
+
+
+def test_long_documents_force_context_parallelism():
+    model = model_from_config(hybrid_1p3b(), device_bytes=180 * 1024 ** 3)
+    lengths = dict(enumerate(lognormal_lengths(1 << 20, 4096, 1.0, 512, 131072, 16, 3) + [131072]))
+    sel = select(lengths, 8, hybrid_1p3b().pattern, model, capacity=32768)
+    assert max(sel.cp_gdn, sel.cp_gqa) >= 4
+    assert any(r["fits"] for r in sel.candidates)
