@@ -236,7 +236,7 @@ def test_gdn_chunk_gradients_vs_cpu():
             torch.randn(T, H, dv), -torch.rand(T, H) * 0.2, torch.rand(T, H), torch.randn(2, H, dk, dv) * 0.1]
     grads = []
     for dev in ("cpu", DEV):
-        ts = [b.to(dev).requires_grad_(True) for b in base]
+        ts = [b.detach().clone().to(dev).requires_grad_(True) for b in base]
         layout = ChunkLayout(lens, torch.device(dev))
         o, fin = chunk_gated_delta_rule(*ts[:5], layout, initial_state=ts[5])
         (o.pow(2).sum() + fin.sum()).backward()
