@@ -35,6 +35,17 @@ void gdn_state_fwd(const at::Tensor& W, const at::Tensor& U, const at::Tensor& K
 void gdn_state_bwd(const at::Tensor& W, const at::Tensor& dDelta_ext, const at::Tensor& Kd, const at::Tensor& gamma,
                    const at::Tensor& dS_ext, const c10::optional<at::Tensor>& dS_final, const at::Tensor& seq_chunks,
                    at::Tensor& dDelta, at::Tensor& G_next, at::Tensor& dS0);
+int64_t symm_alloc(int64_t bytes);
+void symm_free(int64_t ptr);
+at::Tensor symm_handle(int64_t ptr);
+int64_t symm_open(const at::Tensor& handle);
+void symm_close(int64_t ptr);
+void symm_signal(const at::Tensor& peer_signal_bases, int64_t slot, int64_t value);
+void symm_wait(int64_t my_signal_base, int64_t first, int64_t count, int64_t value, at::Tensor& status);
+void symm_gather_rows(const at::Tensor& peer_bases, const at::Tensor& routes, const at::Tensor& block_route,
+                      const at::Tensor& block_row0, int64_t rows_per_block, int64_t row_bytes, at::Tensor& dst,
+                      at::Tensor& status);
+at::Tensor symm_tensor(int64_t ptr, std::vector<int64_t> sizes, int64_t dtype_code, int64_t device);
 }  // namespace prism
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -54,4 +65,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_bwd", &prism::attention_bwd_sm100, "tcgen05 varlen GQA flash attention backward");
   m.def("gdn_state_fwd", &prism::gdn_state_fwd);
   m.def("gdn_state_bwd", &prism::gdn_state_bwd);
+  m.def("symm_alloc", &prism::symm_alloc);
+  m.def("symm_free", &prism::symm_free);
+  m.def("symm_handle", &prism::symm_handle);
+  m.def("symm_open", &prism::symm_open);
+  m.def("symm_close", &prism::symm_close);
+  m.def("symm_signal", &prism::symm_signal);
+  m.def("symm_wait", &prism::symm_wait);
+  m.def("symm_gather_rows", &prism::symm_gather_rows, "P2P row gather over NVLink (CP-transition reshard)");
+  m.def("symm_tensor", &prism::symm_tensor);
 }

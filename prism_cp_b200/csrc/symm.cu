@@ -1,0 +1,163 @@
+// Symmetric memory over NVLink/NVSwitch: one device heap per rank, mapped into
+// every peer of the team through CUDA IPC, plus the P2P kernels that use it.
+//
+//  * symm_alloc / symm_handle / symm_open / symm_close: the heap itself. Each
+//    rank cudaMalloc's its heap once, exports an IPC handle, and opens every
+//    peer's handle; kernels then read and write peer memory with ordinary
+//    loads and stores (never through TMA multicast).
+//  * Signals: a small region of each heap holds 64-bit sequence words. A writer
+//    publishes with a system-scope release store to the peer's word; a reader
+//    spins with acquire loads for at most kPeerWaitNs and returns an error
+//    status instead of hanging if the peer never arrives.
+//  * p2p_gather_rows: the CP-transition reshard as one kernel - every
+//    destination row block is copied straight from the owning peer's heap
+//    (16-byte vector loads over NVLink) into the local layout, driven by a
+//    device route table, after a bounded wait for the sender's "ready" signal.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace prism {
+namespace symm {
+
+constexpr uint64_t kPeerWaitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Spin until *flag >= target; false (and an error code) after kPeerWaitNs.
+__device__ __forceinline__ bool wait_flag(const uint64_t* flag, uint64_t target, int* status) {
+  if (ld_acquire_sys(flag) >= target) return true;
+  const uint64_t t0 = globaltimer();
+  while (ld_acquire_sys(flag) < target) {
+    if (globaltimer() - t0 > kPeerWaitNs) {
+      record_error(status, kTimeoutPeer);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
+// Publish `value` into signal slot `slot` of every peer's heap.
+__global__ void signal_all_kernel(const int64_t* peer_signal_bases, int world, int slot, uint64_t value) {
+  const int r = threadIdx.x;
+  if (r < world) {
+    uint64_t* base = reinterpret_cast<uint64_t*>(peer_signal_bases[r]);
+    st_release_sys(base + slot, value);
+  }
+}
+
+// Wait until signal slots [first, first + count) of MY heap reach `value`.
+__global__ void wait_all_kernel(const uint64_t* my_signals, int first, int count, uint64_t value, int* status) {
+  const int i = threadIdx.x;
+  if (i < count) wait_flag(my_signals + first + i, value, status);
+}
+
+// Route entry: copy `rows` rows from peer `src` (heap byte offset src_off) to
+// local byte offset dst_off; rows are `row_bytes` long (multiple of 16).
+struct RouteEntry {
+  int64_t src_rank;
+  int64_t src_off;
+  int64_t dst_off;
+  int64_t rows;
+};
+
+__global__ void gather_rows_kernel(const int64_t* peer_bases, const RouteEntry* routes, int n_routes,
+                                   const int64_t* block_route, const int64_t* block_row0, int rows_per_block,
+                                   int64_t row_bytes, uint8_t* dst, int* status) {
+  const int b = blockIdx.x;
+  const RouteEntry e = routes[block_route[b]];
+  const int64_t r0 = block_row0[b];
+  const int64_t r1 = min(e.rows, r0 + rows_per_block);
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(peer_bases[e.src_rank]) + e.src_off;
+  const int64_t vec_per_row = row_bytes / 16;
+  const int64_t total = (r1 - r0) * vec_per_row;
+  for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
+    const int64_t row = r0 + i / vec_per_row, v = i % vec_per_row;
+    const uint4 val = *reinterpret_cast<const uint4*>(src + row * row_bytes + v * 16);
+    *reinterpret_cast<uint4*>(dst + e.dst_off + row * row_bytes + v * 16) = val;
+  }
+}
+
+}  // namespace symm
+
+// ---------------------------------------------------------------- host API
+int64_t symm_alloc(int64_t bytes) {
+  void* p = nullptr;
+  C10_CUDA_CHECK(cudaMalloc(&p, bytes));
+  C10_CUDA_CHECK(cudaMemset(p, 0, bytes));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void symm_free(int64_t ptr) { C10_CUDA_CHECK(cudaFree(reinterpret_cast<void*>(ptr))); }
+
+at::Tensor symm_handle(int64_t ptr) {
+  cudaIpcMemHandle_t h;
+  C10_CUDA_CHECK(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(ptr)));
+  at::Tensor out = at::empty({(int64_t)sizeof(h)}, at::TensorOptions().dtype(at::kByte));
+  memcpy(out.data_ptr(), &h, sizeof(h));
+  return out;
+}
+
+int64_t symm_open(const at::Tensor& handle) {
+  TORCH_CHECK(handle.numel() == sizeof(cudaIpcMemHandle_t), "symm_open: bad handle size");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle.data_ptr(), sizeof(h));
+  void* p = nullptr;
+  C10_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void symm_close(int64_t ptr) { C10_CUDA_CHECK(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr))); }
+
+// peer_signal_bases: int64 device tensor [world] of the signal-region base of every rank's heap.
+void symm_signal(const at::Tensor& peer_signal_bases, int64_t slot, int64_t value) {
+  const int world = peer_signal_bases.numel();
+  symm::signal_all_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      peer_signal_bases.data_ptr<int64_t>(), world, (int)slot, (uint64_t)value);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void symm_wait(int64_t my_signal_base, int64_t first, int64_t count, int64_t value, at::Tensor& status) {
+  TORCH_CHECK(count <= 32, "symm_wait: at most 32 slots");
+  symm::wait_all_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const uint64_t*>(my_signal_base), (int)first, (int)count, (uint64_t)value,
+      status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// routes: int64 [n, 4] (src_rank, src_off_bytes, dst_off_bytes, rows); block tables built on host.
+void symm_gather_rows(const at::Tensor& peer_bases, const at::Tensor& routes, const at::Tensor& block_route,
+                      const at::Tensor& block_row0, int64_t rows_per_block, int64_t row_bytes, at::Tensor& dst,
+                      at::Tensor& status) {
+  TORCH_CHECK(row_bytes % 16 == 0, "symm_gather_rows: rows must be multiples of 16 bytes");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(dst.data_ptr()) & 15) == 0, "symm_gather_rows: aligned destination");
+  const int blocks = block_route.numel();
+  if (blocks == 0) return;
+  const c10::cuda::CUDAGuard guard(dst.device());
+  symm::gather_rows_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      peer_bases.data_ptr<int64_t>(), reinterpret_cast<const symm::RouteEntry*>(routes.data_ptr<int64_t>()),
+      routes.size(0), block_route.data_ptr<int64_t>(), block_row0.data_ptr<int64_t>(), (int)rows_per_block,
+      row_bytes, reinterpret_cast<uint8_t*>(dst.data_ptr()), status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace prism
+
+namespace prism {
+// A tensor view of raw device memory inside a symmetric heap (no ownership).
+at::Tensor symm_tensor(int64_t ptr, std::vector<int64_t> sizes, int64_t dtype_code, int64_t device) {
+  const at::ScalarType dt = static_cast<at::ScalarType>(dtype_code);
+  return at::from_blob(reinterpret_cast<void*>(ptr), sizes, at::TensorOptions().dtype(dt).device(at::kCUDA, device));
+}
+}  // namespace prism

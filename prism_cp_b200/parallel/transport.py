@@ -64,6 +64,27 @@ class _Permute(torch.autograd.Function):
         return _exchange(g.contiguous(), ctx.bwd, ctx.group), None, None, None
 
 
+class _PermuteP2P(torch.autograd.Function):
+    """The same permutation over NVLink P2P loads from the symmetric heap."""
+
+    @staticmethod
+    def forward(ctx, x, edges, inverse, p2p):
+        ctx.inverse, ctx.p2p = inverse, p2p
+        return p2p.exchange(x.contiguous(), edges)
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.p2p.exchange(g.contiguous(), ctx.inverse), None, None, None
+
+
+_P2P = {"transport": None}
+
+
+def use_p2p(transport) -> None:
+    """Route every remote reshard through ``transport`` (a ``symm.P2PTransport``); None restores NCCL."""
+    _P2P["transport"] = transport
+
+
 @lru_cache(maxsize=512)
 def _compiled(source, target, lengths_key, world, rank, device_str):
     lengths = dict(lengths_key)
@@ -84,4 +105,8 @@ def move(x: torch.Tensor, source, target, group=None) -> torch.Tensor:
     if compiled is None:
         return x
     fwd, bwd = compiled
+    if _P2P["transport"] is not None and fwd.remote:
+        edges = route(source.layout, target.layout, source.lengths, source.world)
+        inverse = tuple((d, s, b, a, n) for s, d, a, b, n in edges)
+        return _PermuteP2P.apply(x, edges, inverse, _P2P["transport"])
     return _Permute.apply(x, fwd, bwd, group)
