@@ -1,0 +1,111 @@
+"""Planner CLI, catalogue cover, cost fit, profile builder and handoff self-check (CPU)."""
+
+import itertools
+import json
+import math
+
+import pytest
+
+from prism_cp_b200.planner import cli, costfit, handoff, profile_builder, studies
+from prism_cp_b200.planner.inputs import build_manifest
+from prism_cp_b200.planner.joint.cost import Model
+from prism_cp_b200.planner.joint.ir import Plan, validate_plan
+
+SMALL = Model(hidden=1024, ffn=4096, vocab=32000, q_heads=8, kv_heads=2, head_dim=128, gdn_heads=8, gdn_dim=128,
+              device_bytes=180 * 10 ** 9)
+
+
+def test_count_cover_matches_brute_force():
+    templates = [(1, 0, 5.0, "a"), (0, 2, 3.0, "b"), (1, 2, 7.5, "c"), (0, 1, 1.8, "d"), (2, 1, 9.0, "e")]
+    for n_long, n_short in [(2, 3), (3, 4), (1, 5)]:
+        best = math.inf
+        for counts in itertools.product(range(6), repeat=len(templates)):
+            h = sum(c * t[0] for c, t in zip(counts, templates))
+            s = sum(c * t[1] for c, t in zip(counts, templates))
+            if (h, s) == (n_long, n_short):
+                best = min(best, sum(c * t[2] for c, t in zip(counts, templates)))
+        score, chosen = studies.count_cover(templates, n_long, n_short)
+        assert math.isclose(score, best)
+        by_id = {t[3]: t for t in templates}
+        assert sum(by_id[i][0] for i in chosen) == n_long and sum(by_id[i][1] for i in chosen) == n_short
+
+
+def test_count_cover_rejects_uncoverable():
+    with pytest.raises(ValueError):
+        studies.count_cover([(2, 0, 1.0, 0)], 3, 0)
+
+
+def test_costfit_recovers_and_refuses():
+    s = [2048 * k for k in range(1, 11)]
+    t = [3e-4 * x + 0.2 for x in s]
+    f = costfit.fit("M", s, t, "linear", holdout_every=3)
+    assert abs(f.coefficients["S"] - 3e-4) < 1e-10 and abs(f.coefficients["1"] - 0.2) < 1e-8
+    assert math.isclose(f.query(8192), 3e-4 * 8192 + 0.2, rel_tol=1e-9)
+    with pytest.raises(ValueError, match="CP"):
+        f.query(8192, cp=4)
+    with pytest.raises(ValueError, match="outside"):
+        f.query(10 ** 7)
+
+
+def test_nnls_keeps_coefficients_nonnegative():
+    import numpy as np
+    A = np.array([[1.0, 1.0], [2.0, 1.0], [3.0, 1.0]])
+    b = np.array([3.0, 2.0, 1.0])  # decreasing: the unconstrained slope is negative
+    x = costfit.nnls_exact(A, b)
+    assert (x >= 0).all() and x[0] == 0.0 and math.isclose(x[1], 2.0)
+
+
+def test_profile_builder_medians_and_validates():
+    records = []
+    for module in ("GQA", "GDN"):
+        for cp, ms in ((1, 80.0), (2, 42.0), (4, 22.0), (8, 12.0)):
+            for rep in range(3):
+                records.append({"module": module, "cp": cp, "tokens": 65536, "fb_ms": ms + rep})
+    shape = (1024, 8, 2, 128, 8, 128)
+    prof = profile_builder.build(records, 65536, shape)
+    assert prof["anchors"]["GQA"]["milliseconds"]["4"] == 23.0
+    from dataclasses import replace
+    m = replace(SMALL, cp_response=prof)  # validates in __post_init__
+    assert m.cp_response["hardware"] == "B200"
+
+
+def test_handoff_self_check_passes():
+    report = handoff.run()
+    assert report["ok"], report
+
+
+def test_cli_search_writes_result_replay_executor(tmp_path):
+    manifest = build_manifest([8192, 4096, 2048, 2048], "cli", 2)
+    mpath = tmp_path / "m.json"
+    mpath.write_text(json.dumps(manifest))
+    prof = tmp_path / "model.json"
+    from dataclasses import asdict
+    prof.write_text(json.dumps(asdict(SMALL)))
+    out = tmp_path / "run"
+    rc = cli.main(["search", "--manifest", str(mpath), "--output", str(out), "--world", "2", "--pattern", "G*",
+                   "--model-profile", str(prof), "--updates", "2"])
+    assert rc == 0
+    result = json.loads((out / "result.json").read_text())
+    plan = Plan.from_dict(result["plan"])
+    validate_plan(plan, dict(enumerate([8192, 4096, 2048, 2048])))
+    assert len(json.loads((out / "replay.json").read_text())) == 2
+    assert json.loads((out / "executor.json").read_text())["mode"] == "joint"
+
+
+def test_cli_study_reports_alpha_selection(tmp_path):
+    manifest = build_manifest([16384, 4096, 4096, 2048, 2048, 1024, 1024], "study", 4)
+    mpath = tmp_path / "m.json"
+    mpath.write_text(json.dumps(manifest))
+    prof = tmp_path / "model.json"
+    from dataclasses import asdict
+    prof.write_text(json.dumps(asdict(SMALL)))
+    out = tmp_path / "study"
+    rc = cli.main(["study", "--manifest", str(mpath), "--output", str(out), "--world", "4", "--pattern", "GGG*",
+                   "--model-profile", str(prof), "--capacities", "4096", "8192", "16384",
+                   "--reference-capacity", "8192", "--beam", "4", "--layouts", "4"])
+    assert rc == 0
+    report = json.loads((out / "study.json").read_text())
+    ids = {c["id"] for c in report["candidates"]}
+    assert {"native_K4096", "native_K8192", "native_K16384", "joint"} <= ids
+    assert report["decision"]["selected"] in ids
+    assert (out / "REPORT.md").read_text().startswith("# Native N vs joint plan")
