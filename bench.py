@@ -101,6 +101,12 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.rows)}
 
 
+def progress(rank: int, msg: str) -> None:
+    """Phase markers on stderr (stdout carries only the JSON line)."""
+    if rank == 0:
+        print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -148,8 +154,10 @@ def main():
         if world > 1:
             dist.barrier()
 
+    progress(rank, f"model ready ({cfg.parameter_count() / 1e9:.2f}B params, {len(plan.microbatches)} microbatches)")
     for _ in range(args.warmup):
         trainer.train_step(batch, plan, dev_inputs, read_loss=False)
+    progress(rank, "warm-up done")
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
@@ -169,6 +177,7 @@ def main():
     tokens = batch.total_tokens
     value = tokens / (ms_step / 1000.0)
 
+    progress(rank, f"timed loop: {ms_step:.1f} ms/step")
     e2e = None
     if not args.no_e2e:
         torch.cuda.synchronize()
@@ -186,6 +195,7 @@ def main():
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "loss": res.loss,
                "api": "prism_cp_b200.runtime.trainer.Trainer.train_step"}
 
+    progress(rank, "end-to-end loop done")
     launches = count_launches(trainer, batch, plan, dev_inputs)
     mem_peak = torch.cuda.max_memory_allocated(device)
     if rank == 0:

@@ -27,7 +27,8 @@ import torch.distributed as dist
 import torch.distributed.nn.functional as distf
 
 from ..ops.elementwise import causal_conv1d_silu
-from ..ops.gdn import chunk_output, chunk_prep, chunk_state, chunk_transition
+from ..ops.gdn import (chunk_output, chunk_prep, chunk_state, chunk_transition, fused_gated_delta_rule,
+                       fused_supported)
 from ..planner.joint.ir import spans as layout_spans
 
 HALO = 3
@@ -131,11 +132,26 @@ def delta_rule_cp(ctx, q, k, v, g, beta):
     links = rank_links(ctx)
     i = ctx.index
     first_cont, last_cont, single = links[i]
-    prep = chunk_prep(q, k, v, g, beta, layout)
     H, DK, DV = q.shape[1], q.shape[2], v.shape[2]
     nseg = len(ctx.segment_lengths)
     f32 = torch.float32
-    if last_cont:
+    fused = fused_supported(q, v)
+    prep = None if fused else chunk_prep(q, k, v, g, beta, layout)
+    if fused and last_cont:
+        # tail state from zero, and (for a single continuing segment) the linear
+        # map of the incoming state: the recurrence with zero values from I
+        _, S_zero = fused_gated_delta_rule(q, k, v, g, beta, layout)
+        F_tail = S_zero[nseg - 1]
+        if first_cont and single:
+            eye = torch.eye(DK, dtype=f32, device=q.device).expand(nseg, H, DK, DK).contiguous()
+            _, M_all = fused_gated_delta_rule(q, k, torch.zeros_like(q), g, beta, layout, initial_state=eye)
+            M_tail = M_all[nseg - 1]
+        else:
+            M_tail = torch.zeros((H, DK, DK), dtype=f32, device=q.device)
+    elif fused:
+        F_tail = torch.zeros((H, DK, DV), dtype=f32, device=q.device)
+        M_tail = torch.zeros((H, DK, DK), dtype=f32, device=q.device)
+    elif last_cont:
         _, _, S_zero = chunk_state(prep, None)
         F_tail = S_zero[nseg - 1]
         if first_cont and single:
@@ -167,5 +183,8 @@ def delta_rule_cp(ctx, q, k, v, g, beta):
             state = M_r @ state + F_r
         rest = torch.zeros((nseg - 1, H, DK, DV), dtype=f32, device=q.device)
         initial = torch.cat([state[None], rest], 0)
+    if fused:
+        o, _ = fused_gated_delta_rule(q, k, v, g, beta, layout, initial_state=initial)
+        return tie(o, torch.stack(gathered))
     Delta, S_all, _ = chunk_state(prep, initial)
     return tie(chunk_output(prep, Delta, S_all), torch.stack(gathered))
