@@ -35,6 +35,26 @@ void gdn_state_fwd(const at::Tensor& W, const at::Tensor& U, const at::Tensor& K
 void gdn_state_bwd(const at::Tensor& W, const at::Tensor& dDelta_ext, const at::Tensor& Kd, const at::Tensor& gamma,
                    const at::Tensor& dS_ext, const c10::optional<at::Tensor>& dS_final, const at::Tensor& seq_chunks,
                    at::Tensor& dDelta, at::Tensor& G_next, at::Tensor& dS0);
+std::vector<at::Tensor> gdn_chunk_prep(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                       const at::Tensor& g, const at::Tensor& beta, const at::Tensor& tok0,
+                                       const at::Tensor& len, double scale);
+void gdn_chunk_fwd(const at::Tensor& Wn, const at::Tensor& U, const at::Tensor& Kd, const at::Tensor& Qg,
+                   const at::Tensor& Aqk, const at::Tensor& gam, const at::Tensor& tok0, const at::Tensor& len,
+                   const at::Tensor& seq_chunks, const c10::optional<at::Tensor>& S0,
+                   const c10::optional<at::Tensor>& out, const c10::optional<at::Tensor>& S_final,
+                   const c10::optional<at::Tensor>& states, const c10::optional<at::Tensor>& rows,
+                   at::Tensor& status);
+void gdn_chunk_bwd_state(const at::Tensor& Wn, const at::Tensor& Kd, const at::Tensor& Qg, const at::Tensor& Aqk,
+                         const at::Tensor& gam, const at::Tensor& dout, const at::Tensor& tok0, const at::Tensor& len,
+                         const at::Tensor& seq_chunks, const c10::optional<at::Tensor>& dS_final,
+                         const c10::optional<at::Tensor>& dS0, at::Tensor& states, at::Tensor& rows,
+                         at::Tensor& status);
+std::vector<at::Tensor> gdn_chunk_bwd_local(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                            const at::Tensor& g, const at::Tensor& beta, const at::Tensor& tok0,
+                                            const at::Tensor& len, const at::Tensor& Gc, const at::Tensor& states,
+                                            const at::Tensor& dstates, const at::Tensor& rows,
+                                            const at::Tensor& drows, const at::Tensor& dout, double scale,
+                                            at::Tensor& status);
 int64_t symm_alloc(int64_t bytes);
 void symm_free(int64_t ptr);
 at::Tensor symm_handle(int64_t ptr);
@@ -65,6 +85,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_bwd", &prism::attention_bwd_sm100, "tcgen05 varlen GQA flash attention backward");
   m.def("gdn_state_fwd", &prism::gdn_state_fwd);
   m.def("gdn_state_bwd", &prism::gdn_state_bwd);
+  m.def("gdn_chunk_prep", &prism::gdn_chunk_prep, "GDN chunk prep: WY form, decays, Aqk (CUDA cores)");
+  m.def("gdn_chunk_fwd", &prism::gdn_chunk_fwd, "GDN tcgen05 state pass with the output fused");
+  m.def("gdn_chunk_bwd_state", &prism::gdn_chunk_bwd_state, "GDN tcgen05 reverse state pass");
+  m.def("gdn_chunk_bwd_local", &prism::gdn_chunk_bwd_local, "GDN chunk-local backward (tcgen05 + CUDA cores)");
   m.def("symm_alloc", &prism::symm_alloc);
   m.def("symm_free", &prism::symm_free);
   m.def("symm_handle", &prism::symm_handle);

@@ -26,7 +26,7 @@ from __future__ import annotations
 
 import torch
 
-from ._lib import is_cuda, lib
+from ._lib import is_cuda, lib, status
 
 CHUNK = 64
 
@@ -140,6 +140,15 @@ class ChunkLayout:
         self.token_to_padded = torch.nonzero(self.valid).flatten().to(device)
         self.aligned = bool(self.valid.all())
         self.seq_chunks_dev = torch.tensor(self.seq_chunks, dtype=torch.int32, device=device)
+        tok0, valid_rows = [], []
+        offset = 0
+        for n, c in zip(self.lengths, chunks):
+            for j in range(c):
+                tok0.append(offset + j * CHUNK)
+                valid_rows.append(min(CHUNK, n - j * CHUNK))
+            offset += n
+        self.tok0_dev = torch.tensor(tok0, dtype=torch.int32, device=device)
+        self.len_dev = torch.tensor(valid_rows, dtype=torch.int32, device=device)
 
     def pad(self, x: torch.Tensor) -> torch.Tensor:
         """[T, ...] -> [Nc, C, ...] with zeros in padded slots."""
@@ -219,6 +228,77 @@ def chunk_gated_delta_rule(q, k, v, g, beta, layout: ChunkLayout, scale: float |
     prep = chunk_prep(q, k, v, g, beta, layout, scale)
     Delta, S_all, S_final = chunk_state(prep, initial_state)
     return chunk_output(prep, Delta, S_all), S_final
+
+
+# ---------------------------------------------------------------- fused sm_100a path
+def fused_supported(q: torch.Tensor, v: torch.Tensor) -> bool:
+    """Shapes the fused kernels of ``csrc/gdn_chunk.cu`` take: dk = 128, dv in {128, 256}."""
+    return is_cuda(q) and q.shape[-1] == 128 and v.shape[-1] in (128, 256) and q.shape[0] >= CHUNK
+
+
+class _FusedChunkRule(torch.autograd.Function):
+    """Chunked gated delta rule on the fused kernels.
+
+    Forward: prep (WY form, decays, Aqk) and one tcgen05 state pass that also
+    produces the output. Only the inputs are saved; the backward recomputes the
+    prep and the per-chunk states, runs the reverse state pass and the
+    chunk-local backward (dv contractions on tcgen05, WY/decay terms on CUDA
+    cores). Same recurrence as ``chunk_gated_delta_rule``.
+    """
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, layout, scale, S0):
+        L = lib()
+        bf = torch.bfloat16
+        qb, kb, vb = (t.to(bf).contiguous() for t in (q, k, v))
+        gf, bt = g.float().contiguous(), beta.float().contiguous()
+        st = status(q.device)
+        Wn, U, Kd, Qg, Aqk, gam, _ = L.gdn_chunk_prep(qb, kb, vb, gf, bt, layout.tok0_dev, layout.len_dev, scale)
+        T, H, DV = vb.shape
+        o = torch.empty_like(vb)
+        S_final = torch.empty((len(layout.lengths), H, qb.shape[-1], DV), dtype=torch.float32, device=q.device)
+        s0 = S0.float().contiguous() if S0 is not None else None
+        L.gdn_chunk_fwd(Wn, U, Kd, Qg, Aqk, gam, layout.tok0_dev, layout.len_dev, layout.seq_chunks_dev, s0, o,
+                        S_final, None, None, st)
+        ctx.save_for_backward(qb, kb, vb, gf, bt, s0)
+        ctx.layout, ctx.scale, ctx.has_s0 = layout, scale, S0 is not None
+        ctx.dtypes = (q.dtype, k.dtype, v.dtype, g.dtype, beta.dtype)
+        return o.to(v.dtype), S_final
+
+    @staticmethod
+    def backward(ctx, do, dS_final):
+        L = lib()
+        qb, kb, vb, gf, bt, s0 = ctx.saved_tensors
+        lay = ctx.layout
+        st = status(qb.device)
+        Wn, U, Kd, Qg, Aqk, gam, Gc = L.gdn_chunk_prep(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, ctx.scale)
+        Nc, H = Wn.shape[0], Wn.shape[1]
+        DV = vb.shape[-1]
+        states = torch.empty((Nc, H, DV, 128), dtype=torch.bfloat16, device=qb.device)
+        rows = torch.empty((Nc, H, DV, CHUNK), dtype=torch.bfloat16, device=qb.device)
+        L.gdn_chunk_fwd(Wn, U, Kd, Qg, Aqk, gam, lay.tok0_dev, lay.len_dev, lay.seq_chunks_dev, s0, None, None,
+                        states, rows, st)
+        dstates, drows = torch.empty_like(states), torch.empty_like(rows)
+        dS0 = torch.empty_like(s0) if ctx.has_s0 else None
+        if do is None:
+            do = torch.zeros_like(vb)
+        dob = do.to(torch.bfloat16).contiguous()
+        dsf = dS_final.float().contiguous() if dS_final is not None else None
+        L.gdn_chunk_bwd_state(Wn, Kd, Qg, Aqk, gam, dob, lay.tok0_dev, lay.len_dev, lay.seq_chunks_dev, dsf, dS0,
+                              dstates, drows, st)
+        dq, dk, dv, dg, dbeta = L.gdn_chunk_bwd_local(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, Gc, states,
+                                                      dstates, rows, drows, dob, ctx.scale, st)
+        tq, tk, tv, tg, tb = ctx.dtypes
+        return dq.to(tq), dk.to(tk), dv.to(tv), dg.to(tg), dbeta.to(tb), None, None, dS0
+
+
+def fused_gated_delta_rule(q, k, v, g, beta, layout: ChunkLayout, scale: float | None = None,
+                           initial_state: torch.Tensor | None = None):
+    """``(o, final_state)`` of the chunked gated delta rule on the fused sm_100a kernels."""
+    if not fused_supported(q, v):
+        raise ValueError("fused gated delta rule needs CUDA tensors with dk = 128 and dv in {128, 256}")
+    scale = q.shape[-1] ** -0.5 if scale is None else scale
+    return _FusedChunkRule.apply(q, k, v, g, beta, layout, scale, initial_state)
 
 
 def naive_gated_delta_rule(q, k, v, g, beta, lengths, scale=None, initial_state=None):

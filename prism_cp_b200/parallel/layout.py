@@ -23,7 +23,7 @@ import torch.utils.checkpoint
 
 from ..ops.attention import AttentionMeta, flash_attention
 from ..ops.elementwise import causal_conv1d_silu
-from ..ops.gdn import ChunkLayout, chunk_gated_delta_rule
+from ..ops.gdn import ChunkLayout, chunk_gated_delta_rule, fused_gated_delta_rule, fused_supported
 from ..planner.joint.ir import Layout, spans
 
 
@@ -85,6 +85,8 @@ class LocalLayout:
     def delta_rule(self, q, k, v, g, beta):
         if self.cp == 1:
             layout = self.chunk_layout()
+            if fused_supported(q, v):
+                return fused_gated_delta_rule(q, k, v, g, beta, layout)[0]
             if q.is_cuda and torch.is_grad_enabled():
                 # the fp32 chunk intermediates are recomputed in the backward
                 # (only the bf16 inputs stay alive between forward and backward)
