@@ -19,6 +19,9 @@
 
 #include "common.cuh"
 #include "tma_host.cuh"
+#include "attention_peer.cuh"
+
+#include <type_traits>
 
 namespace prism {
 namespace attnb {
@@ -63,10 +66,15 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int k) {
 }
 
 // ------------------------------------------------------------------ dK, dV
+// Src = PeerTiles: this rank's keys of a zigzag team; tiles hold (seq, global
+// position of the first key, its local row); Q / dO tiles and their LSE / D rows
+// are read from the rank that owns each query tile.
+template <class Src>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                       Params p) {
+                       Params p, const __grid_constant__ Src src) {
+  constexpr bool PEER = std::is_same<Src, PeerTiles>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
@@ -90,11 +98,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kv_head = blockIdx.y;
   const int rep = p.hq / p.hkv;
-  const int seq = p.tiles[2 * blockIdx.x];
-  const int ktile = p.tiles[2 * blockIdx.x + 1];
-  const int q_seg = p.cu_q[seq], q_len = p.cu_q[seq + 1] - q_seg;
-  const int k_seg = p.cu_k[seq], k_len = p.cu_k[seq + 1] - k_seg;
-  const int k0 = ktile * TILE;
+  int seq, k0, q_seg, q_len, k_seg, k_len;
+  if constexpr (PEER) {
+    seq = p.tiles[3 * blockIdx.x];
+    k0 = p.tiles[3 * blockIdx.x + 1];
+    k_seg = p.tiles[3 * blockIdx.x + 2] - k0;
+    q_len = k_len = src.seq_n[seq];
+    q_seg = 0;
+  } else {
+    seq = p.tiles[2 * blockIdx.x];
+    k0 = p.tiles[2 * blockIdx.x + 1] * TILE;
+    q_seg = p.cu_q[seq];
+    q_len = p.cu_q[seq + 1] - q_seg;
+    k_seg = p.cu_k[seq];
+    k_len = p.cu_k[seq + 1] - k_seg;
+  }
+  const int ktile = k0 / TILE;
   const int n_qt = (q_len + TILE - 1) / TILE;
   const int i_start = p.causal ? ktile : 0;
   const int per_head = max(0, n_qt - i_start);
@@ -131,11 +150,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int i = i_start + it % per_head;
         if (it > 0 && !mbar_wait_bounded(mma_done, (it - 1) & 1, abort_flag, p.status, kTimeoutProducer)) break;
         mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
-        const int qrow = q_seg + i * TILE;
-        tma_load_3d(sQ, &tmQ, q_full, 0, h, qrow);
-        tma_load_3d(sQ + HALF, &tmQ, q_full, 64, h, qrow);
-        tma_load_3d(sdO, &tmO, q_full, 0, h, qrow);
-        tma_load_3d(sdO + HALF, &tmO, q_full, 64, h, qrow);
+        int qrow = q_seg + i * TILE;
+        const CUtensorMap* mq = &tmQ;
+        const CUtensorMap* mo = &tmO;
+        if constexpr (PEER) {
+          int owner;
+          qrow = peer_row(src, seq, i * TILE, owner);
+          mq = &src.a[owner];
+          mo = &src.b[owner];
+        }
+        tma_load_3d(sQ, mq, q_full, 0, h, qrow);
+        tma_load_3d(sQ + HALF, mq, q_full, 64, h, qrow);
+        tma_load_3d(sdO, mo, q_full, 0, h, qrow);
+        tma_load_3d(sdO + HALF, mo, q_full, 64, h, qrow);
       }
     }
   } else if (warp == 5) {
@@ -181,8 +208,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       {
         const int qq = q0 + r;
         const bool v = qq < q_len;
-        lse_s[r] = v ? p.lse[(long)h * p.tq + q_seg + qq] * kLog2e : INFINITY;
-        dsum_s[r] = v ? p.dsum[(long)h * p.tq + q_seg + qq] : 0.f;
+        const float* lse_src = p.lse;
+        const float* dsum_src = p.dsum;
+        long row = q_seg + qq;
+        if constexpr (PEER) {
+          int owner;
+          row = peer_row(src, seq, q0, owner) + r;
+          lse_src = src.lse[owner];
+          dsum_src = src.dsum[owner];
+        }
+        lse_s[r] = v ? lse_src[(long)h * p.tq + row] * kLog2e : INFINITY;
+        dsum_s[r] = v ? dsum_src[(long)h * p.tq + row] : 0.f;
       }
       named_sync_compute();
       bool waited = mbar_wait_bounded(s_full, it & 1, abort_flag, p.status, kTimeoutEpilogue);
@@ -271,9 +307,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 // ------------------------------------------------------------------ dQ
+template <class Src>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     attn_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, Params p) {
+                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, Params p,
+                      const __grid_constant__ Src src) {
+  constexpr bool PEER = std::is_same<Src, PeerTiles>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
@@ -294,11 +333,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y;
   const int kv_head = head / (p.hq / p.hkv);
-  const int seq = p.tiles[2 * blockIdx.x];
-  const int qtile = p.tiles[2 * blockIdx.x + 1];
-  const int q_seg = p.cu_q[seq], q_len = p.cu_q[seq + 1] - q_seg;
-  const int k_seg = p.cu_k[seq], k_len = p.cu_k[seq + 1] - k_seg;
-  const int q0 = qtile * TILE;
+  int seq, q0, q_seg, q_len, k_seg, k_len;
+  if constexpr (PEER) {
+    seq = p.tiles[3 * blockIdx.x];
+    q0 = p.tiles[3 * blockIdx.x + 1];
+    q_seg = p.tiles[3 * blockIdx.x + 2] - q0;
+    q_len = k_len = src.seq_n[seq];
+    k_seg = 0;
+  } else {
+    seq = p.tiles[2 * blockIdx.x];
+    q0 = p.tiles[2 * blockIdx.x + 1] * TILE;
+    q_seg = p.cu_q[seq];
+    q_len = p.cu_q[seq + 1] - q_seg;
+    k_seg = p.cu_k[seq];
+    k_len = p.cu_k[seq + 1] - k_seg;
+  }
   const int kv_end = p.causal ? min(k_len, q0 + TILE) : k_len;
   const int n_kv = kv_end > 0 ? (kv_end + TILE - 1) / TILE : 0;
 
@@ -334,13 +383,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int s = j & 1;
         if (!mbar_wait_bounded(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.status, kTimeoutProducer)) break;
         mbar_arrive_expect_tx(&kv_full[s], 2 * TILE_BYTES);
-        const int krow = k_seg + j * TILE;
+        int krow = k_seg + j * TILE;
+        const CUtensorMap* mk = &tmK;
+        const CUtensorMap* mv = &tmV;
+        if constexpr (PEER) {
+          int owner;
+          krow = peer_row(src, seq, j * TILE, owner);
+          mk = &src.a[owner];
+          mv = &src.b[owner];
+        }
         uint8_t* kd = sK + s * TILE_BYTES;
         uint8_t* vd = sV + s * TILE_BYTES;
-        tma_load_3d(kd, &tmK, &kv_full[s], 0, kv_head, krow);
-        tma_load_3d(kd + HALF, &tmK, &kv_full[s], 64, kv_head, krow);
-        tma_load_3d(vd, &tmV, &kv_full[s], 0, kv_head, krow);
-        tma_load_3d(vd + HALF, &tmV, &kv_full[s], 64, kv_head, krow);
+        tma_load_3d(kd, mk, &kv_full[s], 0, kv_head, krow);
+        tma_load_3d(kd + HALF, mk, &kv_full[s], 64, kv_head, krow);
+        tma_load_3d(vd, mv, &kv_full[s], 0, kv_head, krow);
+        tma_load_3d(vd + HALF, mv, &kv_full[s], 64, kv_head, krow);
       }
     }
   } else if (warp == 5) {
@@ -504,8 +561,10 @@ void attention_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Ten
   p.status = status.data_ptr<int>();
   static bool configured = false;
   if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_KV));
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_Q));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kv_kernel<NoPeers>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        SMEM_KV));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_q_kernel<NoPeers>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        SMEM_Q));
     configured = true;
   }
   if (tiles_k.size(0) > 0) {
@@ -514,7 +573,8 @@ void attention_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Ten
     pk.out = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
     pk.out2 = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
     pk.out_stride = dk.stride(0);
-    attn_bwd_kv_kernel<<<dim3(tiles_k.size(0), hkv), NUM_THREADS, SMEM_KV, stream>>>(tq, tk, tv, tdo, pk);
+    attn_bwd_kv_kernel<NoPeers><<<dim3(tiles_k.size(0), hkv), NUM_THREADS, SMEM_KV, stream>>>(tq, tk, tv, tdo, pk,
+                                                                                             NoPeers{0});
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   if (tiles_q.size(0) > 0) {
@@ -523,9 +583,93 @@ void attention_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Ten
     pq.out = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
     pq.out2 = nullptr;
     pq.out_stride = dq.stride(0);
-    attn_bwd_q_kernel<<<dim3(tiles_q.size(0), hq), NUM_THREADS, SMEM_Q, stream>>>(tq, tk, tv, tdo, pq);
+    attn_bwd_q_kernel<NoPeers><<<dim3(tiles_q.size(0), hq), NUM_THREADS, SMEM_Q, stream>>>(tq, tk, tv, tdo, pq,
+                                                                                          NoPeers{0});
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
+}
+
+// Context-parallel backward over a zigzag team (causal). *_peers: the team's
+// buffers in symmetric memory, indexed by team rank: q/k/v/dout [T, H, 128]
+// views, lse/dsum [hq, T] fp32 (dsum = rowsum(dO * O), computed beforehand by
+// attention_bwd_dsum on every rank). tiles int32 [n, 3] = (seq, global position
+// of the tile's first row, its local row), the same list for keys and queries.
+void attention_bwd_peer(const std::vector<at::Tensor>& q_peers, const std::vector<at::Tensor>& k_peers,
+                        const std::vector<at::Tensor>& v_peers, const std::vector<at::Tensor>& do_peers,
+                        const std::vector<at::Tensor>& lse_peers, const std::vector<at::Tensor>& dsum_peers,
+                        int64_t rank, const at::Tensor& tiles, const at::Tensor& seq_n, const at::Tensor& seq_row0,
+                        at::Tensor& dq, at::Tensor& dk, at::Tensor& dv, double softmax_scale, at::Tensor& status) {
+  using namespace attnb;
+  const int cp = q_peers.size();
+  TORCH_CHECK(cp >= 1 && cp <= kMaxPeers && (int)k_peers.size() == cp && (int)v_peers.size() == cp &&
+                  (int)do_peers.size() == cp && (int)lse_peers.size() == cp && (int)dsum_peers.size() == cp,
+              "attention_bwd_peer: one buffer per team rank (1..8)");
+  TORCH_CHECK(dk.stride(0) == dv.stride(0), "attention bwd: dk/dv must share a row stride");
+  const at::Tensor& q = q_peers[rank];
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int Tq = q.size(0), hq = q.size(1), hkv = k_peers[rank].size(1);
+  const int ntiles = tiles.size(0);
+  if (ntiles == 0) return;
+  Params p;
+  p.cu_q = nullptr;
+  p.cu_k = nullptr;
+  p.hq = hq;
+  p.hkv = hkv;
+  p.causal = 1;
+  p.scale = (float)softmax_scale;
+  p.lse = lse_peers[rank].data_ptr<float>();
+  p.dsum = dsum_peers[rank].data_ptr<float>();
+  p.tq = Tq;
+  p.status = status.data_ptr<int>();
+  p.tiles = tiles.data_ptr<int>();
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kv_kernel<PeerTiles>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        SMEM_KV));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_q_kernel<PeerTiles>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        SMEM_Q));
+    configured = true;
+  }
+  CUtensorMap tq = make_head_map_128(q), tk = make_head_map_128(k_peers[rank]),
+              tv = make_head_map_128(v_peers[rank]), tdo = make_head_map_128(do_peers[rank]);
+  PeerTiles kv_src{}, q_src{};
+  for (int r = 0; r < cp; ++r) {
+    kv_src.a[r] = make_head_map_128(q_peers[r]);
+    kv_src.b[r] = make_head_map_128(do_peers[r]);
+    kv_src.lse[r] = lse_peers[r].data_ptr<float>();
+    kv_src.dsum[r] = dsum_peers[r].data_ptr<float>();
+    q_src.a[r] = make_head_map_128(k_peers[r]);
+    q_src.b[r] = make_head_map_128(v_peers[r]);
+  }
+  kv_src.seq_n = q_src.seq_n = seq_n.data_ptr<int>();
+  kv_src.seq_row0 = q_src.seq_row0 = seq_row0.data_ptr<int>();
+  kv_src.cp = q_src.cp = cp;
+  Params pk = p;
+  pk.out = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  pk.out2 = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  pk.out_stride = dk.stride(0);
+  attn_bwd_kv_kernel<PeerTiles><<<dim3(ntiles, hkv), NUM_THREADS, SMEM_KV, stream>>>(tq, tk, tv, tdo, pk, kv_src);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  Params pq = p;
+  pq.out = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
+  pq.out2 = nullptr;
+  pq.out_stride = dq.stride(0);
+  attn_bwd_q_kernel<PeerTiles><<<dim3(ntiles, hq), NUM_THREADS, SMEM_Q, stream>>>(tq, tk, tv, tdo, pq, q_src);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// D = rowsum(dO * O) per (query, head): [hq, T] fp32.
+void attention_bwd_dsum(const at::Tensor& out, const at::Tensor& dout, at::Tensor& dsum) {
+  using namespace attnb;
+  const c10::cuda::CUDAGuard guard(out.device());
+  const int Tq = out.size(0), hq = out.size(1);
+  const long warps = (long)Tq * hq;
+  if (warps > 0)
+    attn_bwd_dot_kernel<<<(warps * 32 + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), out.stride(0), dsum.data_ptr<float>(), Tq, hq);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 }  // namespace prism

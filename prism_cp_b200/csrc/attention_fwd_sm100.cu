@@ -23,6 +23,9 @@
 
 #include "common.cuh"
 #include "tma_host.cuh"
+#include "attention_peer.cuh"
+
+#include <type_traits>
 
 namespace prism {
 namespace attn {
@@ -66,9 +69,15 @@ __device__ __forceinline__ void write_p_chunk(uint8_t* p_base, int row, int chun
   *reinterpret_cast<uint4*>(addr) = val;
 }
 
+// Src = NoPeers: K/V of the sequence are local (tiles hold (seq, q tile)).
+// Src = PeerTiles: the sequence is spread over a zigzag team; tiles hold
+// (seq, global position of the first query, its local row) and every KV tile is
+// loaded from the rank that owns it.
+template <class Src>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, FwdParams p) {
+                    const __grid_constant__ CUtensorMap tmV, FwdParams p, const __grid_constant__ Src src) {
+  constexpr bool PEER = std::is_same<Src, PeerTiles>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SMEM_BAR);
@@ -85,11 +94,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y;
   const int kv_head = head / (p.hq / p.hkv);
-  const int seq = p.tiles[2 * blockIdx.x];
-  const int qtile = p.tiles[2 * blockIdx.x + 1];
-  const int q_seg = p.cu_q[seq], q_len = p.cu_q[seq + 1] - q_seg;
-  const int k_seg = p.cu_k[seq], k_len = p.cu_k[seq + 1] - k_seg;
-  const int q0 = qtile * BQ;  // within the sequence
+  int seq, q0, q_seg, q_len, k_seg, k_len;
+  if constexpr (PEER) {
+    seq = p.tiles[3 * blockIdx.x];
+    q0 = p.tiles[3 * blockIdx.x + 1];              // global position within the sequence
+    q_seg = p.tiles[3 * blockIdx.x + 2] - q0;      // local row = q_seg + position (this tile's rows)
+    q_len = k_len = src.seq_n[seq];
+    k_seg = 0;
+  } else {
+    seq = p.tiles[2 * blockIdx.x];
+    q0 = p.tiles[2 * blockIdx.x + 1] * BQ;         // within the sequence
+    q_seg = p.cu_q[seq];
+    q_len = p.cu_q[seq + 1] - q_seg;
+    k_seg = p.cu_k[seq];
+    k_len = p.cu_k[seq + 1] - k_seg;
+  }
   int kv_end = k_len;
   if (p.causal) kv_end = min(k_len, q0 + BQ);
   const int n_kv = kv_end > 0 ? (kv_end + BKV - 1) / BKV : 0;
@@ -130,13 +149,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait_bounded(&kv_empty[s], ph ^ 1, abort_flag, p.status, kTimeoutProducer)) break;
         mbar_arrive_expect_tx(&kv_full[s], 2 * TILE_BYTES);
-        const int krow = k_seg + j * BKV;
+        int krow = k_seg + j * BKV;
+        const CUtensorMap* mk = &tmK;
+        const CUtensorMap* mv = &tmV;
+        if constexpr (PEER) {
+          int owner;
+          krow = peer_row(src, seq, j * BKV, owner);
+          mk = &src.a[owner];
+          mv = &src.b[owner];
+        }
         uint8_t* kd = smem + SMEM_K + s * TILE_BYTES;
         uint8_t* vd = smem + SMEM_V + s * TILE_BYTES;
-        tma_load_3d(kd, &tmK, &kv_full[s], 0, kv_head, krow);
-        tma_load_3d(kd + TILE_BYTES / 2, &tmK, &kv_full[s], 64, kv_head, krow);
-        tma_load_3d(vd, &tmV, &kv_full[s], 0, kv_head, krow);
-        tma_load_3d(vd + TILE_BYTES / 2, &tmV, &kv_full[s], 64, kv_head, krow);
+        tma_load_3d(kd, mk, &kv_full[s], 0, kv_head, krow);
+        tma_load_3d(kd + TILE_BYTES / 2, mk, &kv_full[s], 64, kv_head, krow);
+        tma_load_3d(vd, mv, &kv_full[s], 0, kv_head, krow);
+        tma_load_3d(vd + TILE_BYTES / 2, mv, &kv_full[s], 64, kv_head, krow);
       }
     }
   } else if (warp == 5) {
@@ -341,11 +368,67 @@ void attention_fwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Ten
   p.status = status.data_ptr<int>();
   static bool configured = false;
   if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<NoPeers>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        SMEM_BYTES));
     configured = true;
   }
   dim3 grid(ntiles, hq);
-  attn_fwd_kernel<<<grid, NUM_THREADS, SMEM_BYTES, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
+  attn_fwd_kernel<NoPeers><<<grid, NUM_THREADS, SMEM_BYTES, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p,
+                                                                                                  NoPeers{0});
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Causal attention of this rank's zigzag query rows over a whole team's keys.
+// k_peers / v_peers: the team's K / V buffers ([Tk, Hkv, 128] views, this rank's
+// included, indexed by team rank) in symmetric memory; tiles int32 [n, 3] =
+// (seq, global position of the first query, local row); seq_n / seq_row0 int32 [nseq].
+void attention_fwd_peer(const at::Tensor& q, const std::vector<at::Tensor>& k_peers,
+                        const std::vector<at::Tensor>& v_peers, const at::Tensor& tiles, const at::Tensor& seq_n,
+                        const at::Tensor& seq_row0, at::Tensor& out, at::Tensor& lse, double softmax_scale,
+                        at::Tensor& status) {
+  using namespace attn;
+  const int cp = k_peers.size();
+  TORCH_CHECK(cp >= 1 && cp <= kMaxPeers && (int)v_peers.size() == cp, "attention_fwd_peer: 1..8 peers");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16, "attention: bf16");
+  TORCH_CHECK(out.dim() == 3 && out.stride(2) == 1 && out.stride(1) == D, "attention: out [T,H,128]");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.is_contiguous(), "attention: lse fp32 [H,T]");
+  const int hq = q.size(1), hkv = k_peers[0].size(1);
+  TORCH_CHECK(hq % hkv == 0, "attention: query heads must be a multiple of kv heads");
+  const int ntiles = tiles.size(0);
+  if (ntiles == 0) return;
+  const c10::cuda::CUDAGuard guard(q.device());
+  CUtensorMap tq = make_head_map_128(q);
+  PeerTiles src{};
+  for (int r = 0; r < cp; ++r) {
+    src.a[r] = make_head_map_128(k_peers[r]);
+    src.b[r] = make_head_map_128(v_peers[r]);
+  }
+  src.seq_n = seq_n.data_ptr<int>();
+  src.seq_row0 = seq_row0.data_ptr<int>();
+  src.cp = cp;
+  FwdParams p;
+  p.cu_q = nullptr;
+  p.cu_k = nullptr;
+  p.tiles = tiles.data_ptr<int>();
+  p.ntiles = ntiles;
+  p.hq = hq;
+  p.hkv = hkv;
+  p.causal = 1;
+  p.scale_log2 = (float)(softmax_scale * 1.4426950408889634);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.out_stride = out.stride(0);
+  p.lse = lse.data_ptr<float>();
+  p.tq = q.size(0);
+  p.status = status.data_ptr<int>();
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<PeerTiles>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        SMEM_BYTES));
+    configured = true;
+  }
+  dim3 grid(ntiles, hq);
+  attn_fwd_kernel<PeerTiles><<<grid, NUM_THREADS, SMEM_BYTES, at::cuda::getCurrentCUDAStream()>>>(
+      tq, src.a[0], src.b[0], p, src);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

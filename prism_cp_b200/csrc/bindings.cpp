@@ -55,6 +55,16 @@ std::vector<at::Tensor> gdn_chunk_bwd_local(const at::Tensor& q, const at::Tenso
                                             const at::Tensor& dstates, const at::Tensor& rows,
                                             const at::Tensor& drows, const at::Tensor& dout, double scale,
                                             at::Tensor& status);
+void attention_fwd_peer(const at::Tensor& q, const std::vector<at::Tensor>& k_peers,
+                        const std::vector<at::Tensor>& v_peers, const at::Tensor& tiles, const at::Tensor& seq_n,
+                        const at::Tensor& seq_row0, at::Tensor& out, at::Tensor& lse, double softmax_scale,
+                        at::Tensor& status);
+void attention_bwd_peer(const std::vector<at::Tensor>& q_peers, const std::vector<at::Tensor>& k_peers,
+                        const std::vector<at::Tensor>& v_peers, const std::vector<at::Tensor>& do_peers,
+                        const std::vector<at::Tensor>& lse_peers, const std::vector<at::Tensor>& dsum_peers,
+                        int64_t rank, const at::Tensor& tiles, const at::Tensor& seq_n, const at::Tensor& seq_row0,
+                        at::Tensor& dq, at::Tensor& dk, at::Tensor& dv, double softmax_scale, at::Tensor& status);
+void attention_bwd_dsum(const at::Tensor& out, const at::Tensor& dout, at::Tensor& dsum);
 int64_t symm_alloc(int64_t bytes);
 void symm_free(int64_t ptr);
 at::Tensor symm_handle(int64_t ptr);
@@ -89,6 +99,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_chunk_fwd", &prism::gdn_chunk_fwd, "GDN tcgen05 state pass with the output fused");
   m.def("gdn_chunk_bwd_state", &prism::gdn_chunk_bwd_state, "GDN tcgen05 reverse state pass");
   m.def("gdn_chunk_bwd_local", &prism::gdn_chunk_bwd_local, "GDN chunk-local backward (tcgen05 + CUDA cores)");
+  m.def("attention_fwd_peer", &prism::attention_fwd_peer,
+        "context-parallel attention forward reading every KV tile from its owner's symmetric buffer");
+  m.def("attention_bwd_peer", &prism::attention_bwd_peer,
+        "context-parallel attention backward reading peer Q/dO/K/V tiles and LSE/D rows");
+  m.def("attention_bwd_dsum", &prism::attention_bwd_dsum);
   m.def("symm_alloc", &prism::symm_alloc);
   m.def("symm_free", &prism::symm_free);
   m.def("symm_handle", &prism::symm_handle);

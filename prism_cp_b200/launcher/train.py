@@ -93,7 +93,9 @@ def main(argv=None) -> int:
     model = HybridModel(cfg, dtype=dtype, device=device, seed=args.seed)
     trainer = Trainer(model, Teams(world), device, lr=args.lr, min_lr=args.min_lr, weight_decay=args.weight_decay,
                       clip_grad=args.clip_grad, warmup_steps=args.lr_warmup_iters,
-                      decay_steps=args.lr_decay_iters or args.train_iters, records=args.records)
+                      decay_steps=args.lr_decay_iters or args.train_iters, records=args.records,
+                      overlap_grad_reduce=args.overlap_grad_reduce,
+                      bucket_bytes=(args.ddp_bucket_size or (64 << 20)) * 4)
     replays = json.loads(Path(args.joint_replay).read_text()) if args.joint_replay else None
     start = 1
     if args.load and checkpoint.latest(args.load) is not None:

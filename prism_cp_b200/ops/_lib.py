@@ -59,3 +59,18 @@ def aligned_rows(t: torch.Tensor) -> torch.Tensor:
             (t.stride(d) * t.element_size()) % 16 == 0 for d in range(t.dim() - 1)):
         return t
     return t.contiguous()
+
+
+# ---------------------------------------------------------------- gradient-ready notifications
+_GRAD_LISTENER = [None]
+
+
+def set_grad_listener(fn) -> None:
+    """Register ``fn(param)`` to be told when an op has accumulated into ``param.main_grad``."""
+    _GRAD_LISTENER[0] = fn
+
+
+def on_main_grad(param) -> None:
+    fn = _GRAD_LISTENER[0]
+    if fn is not None:
+        fn(param)

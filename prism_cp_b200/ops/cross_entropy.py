@@ -14,7 +14,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from ._lib import is_cuda, lib
+from ._lib import is_cuda, lib, on_main_grad
 from .gemm import matmul
 
 CHUNK_TOKENS = 8192
@@ -50,6 +50,7 @@ class _HeadCE(torch.autograd.Function):
         if main is not None:
             main.addcmul_(dw, g.to(torch.float32).reshape(1, 1))
             dweight = None
+            on_main_grad(weight)
         else:
             dweight = (dw * g).to(weight.dtype)
         return (dh * g.to(dh.dtype)), dweight, None, None, None

@@ -15,7 +15,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from ._lib import aligned_rows, is_cuda, lib
+from ._lib import aligned_rows, is_cuda, lib, on_main_grad
 
 
 # ---------------------------------------------------------------- RoPE
@@ -93,6 +93,7 @@ class _Conv(torch.autograd.Function):
         if main is not None:
             main.add_(dw)
             dw = None
+            on_main_grad(w)
         else:
             dw = dw.to(w.dtype)
         dhalo = res[1].to(halo.dtype) if halo is not None else None

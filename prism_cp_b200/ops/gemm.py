@@ -12,7 +12,7 @@ from __future__ import annotations
 
 import torch
 
-from ._lib import aligned_rows, is_cuda, lib, status
+from ._lib import aligned_rows, is_cuda, lib, status, on_main_grad
 
 
 def _torch_mm(a, b, a_mn, b_mn):
@@ -68,8 +68,10 @@ class _Linear(torch.autograd.Function):
             if main is not None and x2.is_cuda:
                 matmul(dy2, x2, a_mn=True, b_mn=True, out=main, accumulate=True)
                 dw = None
+                on_main_grad(weight)
             elif main is not None:
                 main.add_(_torch_mm(dy2, x2, True, True).to(main.dtype))
+                on_main_grad(weight)
             else:
                 dw = matmul(dy2, x2, a_mn=True, b_mn=True, out_dtype=weight.dtype)
         return dx, dw

@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import torch
 
-from ._lib import aligned_rows, is_cuda, lib
+from ._lib import aligned_rows, is_cuda, lib, on_main_grad
 
 
 def _ref_rownorm(x, w, z, heads, n, inv_n, eps):
@@ -50,6 +50,7 @@ class _RowNorm(torch.autograd.Function):
             if main is not None:
                 main.add_(dw)
                 dw = None
+                on_main_grad(w)
             else:
                 dw = dw.to(w.dtype)
         return dx, dw, dz, None, None, None, None

@@ -18,6 +18,8 @@ new per-layer CP degree never re-initialises process groups.
 
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.utils.checkpoint
 
@@ -25,6 +27,12 @@ from ..ops.attention import AttentionMeta, flash_attention
 from ..ops.elementwise import causal_conv1d_silu
 from ..ops.gdn import ChunkLayout, chunk_gated_delta_rule, fused_gated_delta_rule, fused_supported
 from ..planner.joint.ir import Layout, spans
+
+
+# "peer": kernels read the team's tiles from symmetric memory over NVLink
+# (layouts whose sequences split into whole 128-token chunks); "ring": NCCL
+# point-to-point ring with LSE merge. Override with PRISM_CP_ATTENTION.
+CP_ATTENTION = {"impl": os.environ.get("PRISM_CP_ATTENTION", "ring")}
 
 
 class LocalLayout:
@@ -65,9 +73,13 @@ class LocalLayout:
             return out
         if self.mode != "zigzag":
             raise ValueError("GQA context parallelism requires a zigzag layout")
-        from .cp_attention import ZigzagRing
         if self._cp_attn is None:
-            self._cp_attn = ZigzagRing(self)
+            from . import peer_attention
+            if q.is_cuda and CP_ATTENTION["impl"] == "peer" and peer_attention.supported(self):
+                self._cp_attn = peer_attention.PeerAttention(self)
+            else:
+                from .cp_attention import ZigzagRing
+                self._cp_attn = ZigzagRing(self)
         return self._cp_attn(q, k, v)
 
     # ------------------------------------------------------------ GDN pieces

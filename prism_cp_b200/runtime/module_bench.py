@@ -5,7 +5,10 @@ or under ``torch.distributed.run --nproc-per-node p`` for CP p (one team of all
 ranks: contiguous layout for GDN, zigzag for GQA). Before timing, the P0 gates
 of the reference bench run (experiments/performance_model/module_bench.py):
 
-* ``repeat``   - two runs on the same input give the same Y, dX and dW;
+* ``repeat``   - two runs on the same input give the same Y, dX and dW up to
+  summation order (the GDN backward reduces per-chunk decay/beta terms with
+  shared-memory atomics, so small parameters such as A_log can differ in the
+  last bits; the bound is the reference's 5e-3);
 * ``reference``- the module against an fp32 PyTorch evaluation of the same
   weights (attention / delta rule / MLP core on the CPU-reference code paths);
 * ``packed``   - a packed batch of two sequences equals the two run separately.
@@ -30,7 +33,7 @@ from pathlib import Path
 import torch
 import torch.distributed as dist
 
-THRESHOLDS = {"repeat": 1e-4, "reference": 3e-2, "packed": 1e-2}
+THRESHOLDS = {"repeat": 5e-3, "reference": 3e-2, "packed": 1e-2}
 
 
 def rel(a, b) -> float:

@@ -26,7 +26,16 @@ from ..ops._lib import is_cuda, lib
 
 
 class FlatParameters:
-    def __init__(self, model: torch.nn.Module, world: int, dtype=None):
+    """All trainable parameters as views into one flat buffer, grouped in gradient buckets.
+
+    Without ``bucket_bytes`` there is one bucket in module order. With it, the
+    parameters are laid out in backward order (last layers first) and cut into
+    buckets of at least ``bucket_bytes`` of fp32 gradient, each padded to a
+    multiple of 128 * world elements, so every bucket can be reduce-scattered on
+    its own as soon as the backward has produced all of its gradients.
+    """
+
+    def __init__(self, model: torch.nn.Module, world: int, dtype=None, bucket_bytes: int | None = None):
         params = [p for p in model.parameters() if p.requires_grad]
         self.params = params
         device = params[0].device
@@ -37,22 +46,42 @@ class FlatParameters:
         # 16-byte aligned operands); the gaps are zero and never updated
         def slot(n):
             return (n + 63) // 64 * 64
-        total = sum(slot(p.numel()) for p in params)
+
+        def pad(n):
+            return (n + align - 1) // align * align
+
         align = 128 * world
-        self.padded = (total + align - 1) // align * align
-        self.numel = total
+        order = list(range(len(params)))[::-1] if bucket_bytes else list(range(len(params)))
+        starts = [0] * len(params)
+        buckets, members, lo, off = [], [], 0, 0
+        for i in order:
+            starts[i] = off
+            off += slot(params[i].numel())
+            members.append(i)
+            if bucket_bytes and (off - lo) * 4 >= bucket_bytes:
+                off = pad(off)
+                buckets.append((lo, off, tuple(members)))
+                lo, members = off, []
+        if members or not buckets:
+            off = pad(off)
+            buckets.append((lo, off, tuple(members)))
+        self.buckets = buckets
+        self.padded = off
+        self.numel = off
         self.flat = torch.zeros(self.padded, dtype=dtype, device=device)
         self.grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
         self.offsets = []
-        off = 0
-        for p in params:
-            n = p.numel()
-            view = self.flat[off:off + n].view_as(p)
+        for i, p in enumerate(params):
+            o, n = starts[i], p.numel()
+            view = self.flat[o:o + n].view_as(p)
             view.copy_(p.detach().to(dtype))
             p.data = view
-            p.main_grad = self.grad[off:off + n].view_as(p)
-            self.offsets.append((off, n))
-            off += slot(n)
+            p.main_grad = self.grad[o:o + n].view_as(p)
+            self.offsets.append((o, n))
+        self.bucket_of = {}
+        for b, (_, _, mem) in enumerate(buckets):
+            for i in mem:
+                self.bucket_of[id(params[i])] = b
         # decoupled weight decay only on matrices (Megatron excludes norms/biases/1-D)
         self.decay_mask = torch.zeros(self.padded, dtype=torch.bool, device=device)
         for p, (o, n) in zip(params, self.offsets):
@@ -82,21 +111,37 @@ class DistributedAdamW:
             world = dist.get_world_size(group) if (dist.is_available() and dist.is_initialized()) else 1
         self.world = world
         self.rank = dist.get_rank(group) if self.world > 1 else 0
-        self.shard_size = flat.padded // self.world
-        lo = self.rank * self.shard_size
-        self.lo, self.hi = lo, lo + self.shard_size
-        self.master = flat.flat[lo:self.hi].to(torch.float32).clone()
+        # rank r owns slice r of every bucket; the optimizer state is their concatenation
+        self.slices = []
+        sh = 0
+        for lo, hi, _ in flat.buckets:
+            size = (hi - lo) // self.world
+            self.slices.append((lo, hi, lo + self.rank * size, size, sh))
+            sh += size
+        self.shard_size = sh
+        owned = [flat.flat[a:a + n] for _, _, a, n, _ in self.slices]
+        self.master = torch.cat(owned).to(torch.float32)
+        self.shard_bf16 = torch.cat(owned).clone()
         self.m = torch.zeros_like(self.master)
         self.v = torch.zeros_like(self.master)
         self.grad_shard = torch.zeros_like(self.master)
-        self.wd_mask = flat.decay_mask[lo:self.hi].to(torch.float32)
+        self.wd_mask = torch.cat([flat.decay_mask[a:a + n] for _, _, a, n, _ in self.slices]).to(torch.float32)
         self.sumsq = torch.zeros(1, dtype=torch.float32, device=self.master.device)
         self.lr, self.min_lr, self.betas, self.eps = lr, min_lr, betas, eps
         self.weight_decay, self.clip_grad = weight_decay, clip_grad
         self.warmup_steps, self.decay_steps, self.decay_style = warmup_steps, decay_steps, decay_style
         self.step_count = 0
-        self.stats = {"reduce_scatter_bytes": 0, "all_gather_bytes": 0}
+        self.stats = {"reduce_scatter_bytes": 0, "all_gather_bytes": 0, "overlapped_buckets": 0}
         self.audit = None
+        self._overlap = None
+
+    @property
+    def lo(self) -> int:
+        return self.slices[0][2]
+
+    @property
+    def hi(self) -> int:
+        return self.slices[-1][2] + self.slices[-1][3]
 
     # -------------------------------------------------------------- schedule
     def current_lr(self, step: int) -> float:
@@ -110,23 +155,40 @@ class DistributedAdamW:
         return self.min_lr + 0.5 * (self.lr - self.min_lr) * (1 + math.cos(math.pi * t))
 
     # -------------------------------------------------------------- collectives
-    def reduce_gradients(self):
-        g = self.flat.grad
+    def _reduce_bucket(self, b: int):
+        lo, hi, _, size, sh = self.slices[b]
+        g = self.flat.grad[lo:hi]
         if self.world > 1:
-            dist.reduce_scatter_tensor(self.grad_shard, g, op=dist.ReduceOp.SUM, group=self.group)
+            dist.reduce_scatter_tensor(self.grad_shard[sh:sh + size], g, op=dist.ReduceOp.SUM, group=self.group)
             self.stats["reduce_scatter_bytes"] += g.numel() * 4
         else:
-            self.grad_shard.copy_(g)
+            self.grad_shard[sh:sh + size].copy_(g)
         if self.audit is not None:
             self.audit.reduce_scatter(g.numel() * 4)
 
+    def reduce_gradients(self):
+        ov = self._overlap
+        done = ov.finish() if ov is not None else set()
+        for b in range(len(self.slices)):
+            if b not in done:
+                self._reduce_bucket(b)
+
     def gather_parameters(self):
-        shard = self.flat.flat[self.lo:self.hi]
-        if self.world > 1:
-            dist.all_gather_into_tensor(self.flat.flat, shard.clone(), group=self.group)
-            self.stats["all_gather_bytes"] += self.flat.flat.numel() * self.flat.flat.element_size()
-        if self.audit is not None:
-            self.audit.all_gather(self.flat.flat.numel() * self.flat.flat.element_size())
+        if self.world == 1:
+            self.flat.flat.copy_(self.shard_bf16)
+        for lo, hi, _, size, sh in self.slices:
+            if self.world > 1:
+                dist.all_gather_into_tensor(self.flat.flat[lo:hi], self.shard_bf16[sh:sh + size], group=self.group)
+                self.stats["all_gather_bytes"] += (hi - lo) * self.flat.flat.element_size()
+            if self.audit is not None:
+                self.audit.all_gather((hi - lo) * self.flat.flat.element_size())
+
+    # -------------------------------------------------------------- overlap
+    def enable_overlap(self):
+        """Reduce-scatter each gradient bucket on a side stream as soon as the backward
+        of the last microbatch has produced all of its gradients."""
+        self._overlap = _GradOverlap(self)
+        return self._overlap
 
     # -------------------------------------------------------------- update
     def grad_norm_sq(self) -> torch.Tensor:
@@ -149,7 +211,7 @@ class DistributedAdamW:
         lr = self.current_lr(self.step_count)
         b1, b2 = self.betas
         bc1, bc2 = 1 - b1 ** self.step_count, 1 - b2 ** self.step_count
-        shard_bf16 = self.flat.flat[self.lo:self.hi]
+        shard_bf16 = self.shard_bf16
         if is_cuda(self.master):
             # decoupled weight decay on matrices first (p *= 1 - lr*wd), then one fused
             # AdamW launch that also writes the bf16 shard; a non-finite norm skips it
@@ -181,5 +243,74 @@ class DistributedAdamW:
         self.m.copy_(state["m"])
         self.v.copy_(state["v"])
         self.step_count = int(state["step"])
-        self.flat.flat[self.lo:self.hi].copy_(self.master)
+        self.shard_bf16.copy_(self.master)
         self.gather_parameters()
+
+
+class _GradOverlap:
+    """Tracks which parameters of each bucket received their last gradient.
+
+    Kernels that accumulate straight into ``main_grad`` report through
+    ``ops._lib.on_main_grad``; every other parameter reports from a
+    post-accumulate-grad hook, which also folds its ``.grad`` into ``main_grad``.
+    While ``armed`` (the last microbatch's backward), a bucket whose parameters
+    have all reported is reduce-scattered on a side stream after an event on the
+    compute stream; ``finish`` makes the compute stream wait for those reduces.
+    """
+
+    def __init__(self, opt: DistributedAdamW):
+        from ..ops._lib import set_grad_listener
+        self.opt = opt
+        flat = opt.flat
+        self.need = [set(id(flat.params[i]) for i in mem) for _, _, mem in flat.buckets]
+        self.seen = [set() for _ in flat.buckets]
+        self.launched: set = set()
+        self.armed = False
+        dev = flat.grad.device
+        self.side = torch.cuda.Stream(device=dev) if flat.grad.is_cuda else None
+        self.handles = [p.register_post_accumulate_grad_hook(self._on_accumulated) for p in flat.params]
+        set_grad_listener(self._on_main_grad)
+
+    def arm(self, armed: bool = True):
+        self.armed = armed
+        if armed:
+            self.seen = [set() for _ in self.seen]
+            self.launched = set()
+
+    def _on_accumulated(self, p):
+        if p.grad is not None:
+            p.main_grad.add_(p.grad.to(torch.float32))
+            p.grad = None
+        self._on_main_grad(p)
+
+    def _on_main_grad(self, p):
+        if not self.armed:
+            return
+        b = self.opt.flat.bucket_of.get(id(p))
+        if b is None or b in self.launched:
+            return
+        self.seen[b].add(id(p))
+        if self.seen[b] >= self.need[b]:
+            self.launched.add(b)
+            if self.side is None:
+                self.opt._reduce_bucket(b)
+                return
+            ev = torch.cuda.Event()
+            ev.record()
+            with torch.cuda.stream(self.side):
+                self.side.wait_event(ev)
+                self.opt._reduce_bucket(b)
+            self.opt.stats["overlapped_buckets"] += 1
+
+    def finish(self) -> set:
+        done = set(self.launched)
+        if self.side is not None and done:
+            torch.cuda.current_stream().wait_stream(self.side)
+        self.armed = False
+        return done
+
+    def close(self):
+        from ..ops._lib import set_grad_listener
+        for h in self.handles:
+            h.remove()
+        set_grad_listener(None)

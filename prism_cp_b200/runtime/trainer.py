@@ -48,14 +48,16 @@ class StepResult:
 class Trainer:
     def __init__(self, model, teams, device, lr=3e-4, min_lr=3e-5, weight_decay=0.1, clip_grad=1.0,
                  warmup_steps=0, decay_steps=1000, group=None, hbm_guard=True, records: str | None = None,
-                 numerics=None, audit: bool = False):
+                 numerics=None, audit: bool = False, overlap_grad_reduce: bool = False,
+                 bucket_bytes: int = 256 << 20):
         self.model, self.teams, self.device = model, teams, device
         self.world = teams.world
         self.rank = teams.rank
-        self.flat = FlatParameters(model, self.world)
+        self.flat = FlatParameters(model, self.world, bucket_bytes=bucket_bytes if overlap_grad_reduce else None)
         self.optimizer = DistributedAdamW(self.flat, group=group, lr=lr, min_lr=min_lr,
                                           weight_decay=weight_decay, clip_grad=clip_grad,
                                           warmup_steps=warmup_steps, decay_steps=decay_steps, world=self.world)
+        self.overlap = self.optimizer.enable_overlap() if overlap_grad_reduce else None
         self.cache = LayoutCache(self.world, self.rank, device, teams)
         self.hbm_guard = hbm_guard and device.type == "cuda"
         self.loss_acc = torch.zeros((), dtype=torch.float32, device=device)
@@ -72,10 +74,14 @@ class Trainer:
     # ------------------------------------------------------------------ step
     def forward_backward(self, batch_lengths: dict, plan: Plan, inputs: list):
         self.loss_acc.zero_()
-        for mb, host in zip(plan.microbatches, inputs):
+        last = len(plan.microbatches) - 1
+        for index, (mb, host) in enumerate(zip(plan.microbatches, inputs)):
             dev = host.to(self.device) if host.tokens.device != self.device else host
             run = MicrobatchRun(mb, batch_lengths, self.cache)
             loss, _ = run.forward(self.model, dev.tokens, dev.labels, dev.weights)
+            if self.overlap is not None:
+                # the last backward reduce-scatters each finished bucket while it runs
+                self.overlap.arm(index == last)
             loss.backward()
             if self.audit is not None:
                 self.audit.backward(len(self.audit.events))

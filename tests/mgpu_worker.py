@@ -85,6 +85,25 @@ def main():
         err = rel(got, want)
         assert err < 3e-2, f"ring attention {name} rel err {err}"
 
+    # 2b. the same attention with the kernels reading peer tiles over NVLink
+    from prism_cp_b200.parallel import layout as layout_mod
+    layout_mod.CP_ATTENTION["impl"] = "peer"
+    pctx = LocalLayout(Layout((Group(ranks, (0, 1)),), "zigzag"), alen, world, rank, dev, teams)
+    qp, kp, vp = (t[rows].clone().requires_grad_(True) for t in (q, k, v))
+    for _ in range(3):  # repeated calls cycle both heap halves and the done/ready protocol
+        for t in (qp, kp, vp):
+            t.grad = None
+        outp = pctx.attention(qp, kp, vp)
+        (outp.float() * go[rows].float()).sum().backward()
+    torch.cuda.synchronize()
+    check_status(dev)
+    layout_mod.CP_ATTENTION["impl"] = "ring"
+    assert type(pctx._cp_attn).__name__ == "PeerAttention"
+    for name, got, want in (("out", outp, full[rows]), ("dq", qp.grad, qf.grad[rows]),
+                            ("dk", kp.grad, kf.grad[rows]), ("dv", vp.grad, vf.grad[rows])):
+        err = rel(got, want)
+        assert err < 3e-2, f"peer attention {name} rel err {err}"
+
     # 3. chunkwise GDN CP on the GPU state kernels vs one GPU
     glen = {0: 2560 * world // 2, 1: 640 * world // 2}
     gctx = LocalLayout(Layout((Group(ranks, (0, 1)),), "contiguous"), glen, world, rank, dev, teams)

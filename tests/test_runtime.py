@@ -100,3 +100,29 @@ def test_launcher_runs_native_and_fixed_schedulers(capsys):
     assert main(common + ["--sequence-packing-scheduler", "fixed", "--context-parallel-size", "1"]) == 0
     lines = [json.loads(x) for x in capsys.readouterr().out.splitlines() if x.startswith("{")]
     assert len(lines) == 4 and all(x["tokens"] == 768 for x in lines)
+
+
+def test_overlapped_bucket_reduce_matches_single_bucket():
+    """Bucketed ownership with overlapped reduce-scatter gives the same update as one bucket."""
+    import torch
+    from prism_cp_b200.models.config import hybrid_tiny
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.parallel.teams import Teams
+    from prism_cp_b200.planner.fixed import uniform_plan
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.trainer import Trainer
+    cfg = hybrid_tiny()
+    batch = make_batch([512, 256, 256], cfg.vocab_size, seed=3)
+    plan = uniform_plan(batch.lengths, 1, 1, 512, cfg.pattern)
+    results = []
+    for overlap in (False, True):
+        model = HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0)
+        tr = Trainer(model, Teams(1), torch.device("cpu"), overlap_grad_reduce=overlap, bucket_bytes=64 << 10)
+        if overlap:
+            assert len(tr.flat.buckets) > 2
+        losses = [tr.train_step(batch, plan).loss for _ in range(2)]
+        params = torch.cat([p.detach().reshape(-1) for p in model.parameters()])
+        results.append((losses, params))
+    (l0, p0), (l1, p1) = results
+    assert l0 == pytest.approx(l1, rel=1e-6)
+    assert torch.allclose(p0, p1, rtol=1e-5, atol=1e-6)
