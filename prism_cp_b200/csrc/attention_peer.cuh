@@ -5,7 +5,7 @@
 // the other in its local segment for that sequence (the same local row on every
 // rank). With every rank's Q/K/V/dO (and LSE, D) in a symmetric heap mapped into
 // all peers, an attention kernel reads the tile at global position `pos` straight
-// from its owner: tensor maps over the peers' buffers feed plain (non-multicast)
+// from its owner: tensor maps over the peers' buffers feed plain per-CTA
 // TMA loads, and LSE/D rows are read with ordinary loads over NVLink. The KV
 // exchange of a ring is thereby part of the attention tile loop itself.
 #pragma once

@@ -2,7 +2,7 @@
 //
 // Everything here is written for Blackwell (sm_100a): mbarrier waits are
 // bounded (a wait that runs out records an error code and returns false, it
-// never traps), TMA loads are plain tiled loads without cluster multicast, and
+// never traps), TMA loads are plain per-CTA tiled loads, and
 // the tcgen05 helpers wrap the PTX forms documented in the PTX ISA.
 #pragma once
 
@@ -99,7 +99,7 @@ PRISM_DEVICE void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled TMA load (no multicast) completing on an mbarrier transaction count.
+// 2-D tiled TMA load into this CTA only, completing on an mbarrier transaction count.
 PRISM_DEVICE void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
@@ -108,7 +108,7 @@ PRISM_DEVICE void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* 
       : "memory");
 }
 
-// 3-D tiled TMA load (no multicast).
+// 3-D tiled TMA load into this CTA only.
 PRISM_DEVICE void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y,
                               int32_t z) {
   asm volatile(

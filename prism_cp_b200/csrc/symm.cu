@@ -4,7 +4,7 @@
 //  * symm_alloc / symm_handle / symm_open / symm_close: the heap itself. Each
 //    rank cudaMalloc's its heap once, exports an IPC handle, and opens every
 //    peer's handle; kernels then read and write peer memory with ordinary
-//    loads and stores (never through TMA multicast).
+//    loads and stores.
 //  * Signals: a small region of each heap holds 64-bit sequence words. A writer
 //    publishes with a system-scope release store to the peer's word; a reader
 //    spins with acquire loads for at most kPeerWaitNs and returns an error
