@@ -160,6 +160,198 @@ __global__ void conv_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv
   }
 }
 
+// Vectorised forms: one thread owns 8 consecutive channels (16-byte loads) and
+// walks kConvTokV tokens with the last three inputs (forward) or pre-activation
+// gradients (backward) held in registers, so every x and dy element is read once
+// per pass instead of once per tap. Used when C % 8 == 0 and rows are 16-byte
+// aligned; dx[t] = sum_j w[j] dpre[t + 3 - j] is finalised when dpre[t + 3]
+// is known, or at a segment end with the missing terms zero.
+constexpr int kConvTokV = 256;
+
+__device__ __forceinline__ void ld8f(const __nv_bfloat16* p, float* f) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ void st8f(__nv_bfloat16* p, const float* f) {
+  *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                            pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+}
+
+// x value of token u for a sequence starting at `start` (halo rows before sequence 0)
+__device__ __forceinline__ void conv_x8(const __nv_bfloat16* x, long xs, const __nv_bfloat16* halo, int C, int c8,
+                                        int seg, int start, int u, float* f) {
+  if (u >= start) {
+    ld8f(x + (long)u * xs + c8, f);
+  } else if (seg == 0 && halo != nullptr && u - start + kConvK - 1 >= 0) {
+    ld8f(halo + (long)(u - start + kConvK - 1) * C + c8, f);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = 0.f;
+  }
+}
+
+__global__ void conv_fwd_vec_kernel(const __nv_bfloat16* __restrict__ x, long xs, const __nv_bfloat16* __restrict__ w,
+                                    const __nv_bfloat16* __restrict__ halo, const int* __restrict__ cu, int nseg,
+                                    int T, int C, __nv_bfloat16* __restrict__ y) {
+  const int c8 = 8 * (blockIdx.y * blockDim.x + threadIdx.x);
+  if (c8 >= C) return;
+  const int t0 = blockIdx.x * kConvTokV;
+  const int t1 = min(T, t0 + kConvTokV);
+  float wk[8][kConvK];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < kConvK; ++j) wk[i][j] = __bfloat162float(w[(c8 + i) * kConvK + j]);
+  int seg = find_segment(cu, nseg, t0);
+  int start = cu[seg], end = cu[seg + 1];
+  float xm3[8], xm2[8], xm1[8];
+  conv_x8(x, xs, halo, C, c8, seg, start, t0 - 3, xm3);
+  conv_x8(x, xs, halo, C, c8, seg, start, t0 - 2, xm2);
+  conv_x8(x, xs, halo, C, c8, seg, start, t0 - 1, xm1);
+  for (int t = t0; t < t1; ++t) {
+    if (t == end) {
+      while (seg + 1 < nseg && cu[seg + 1] <= t) ++seg;
+      start = cu[seg];
+      end = cu[seg + 1];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xm3[i] = xm2[i] = xm1[i] = 0.f;
+    }
+    float xt[8], out[8];
+    ld8f(x + (long)t * xs + c8, xt);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float acc = wk[i][0] * xm3[i] + wk[i][1] * xm2[i] + wk[i][2] * xm1[i] + wk[i][3] * xt[i];
+      out[i] = silu(acc);
+      xm3[i] = xm2[i];
+      xm2[i] = xm1[i];
+      xm1[i] = xt[i];
+    }
+    st8f(y + (long)t * C + c8, out);
+  }
+}
+
+__global__ void conv_bwd_vec_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                    long xs, const __nv_bfloat16* __restrict__ w,
+                                    const __nv_bfloat16* __restrict__ halo, const int* __restrict__ cu, int nseg,
+                                    int T, int C, __nv_bfloat16* __restrict__ dx, long dxs, float* __restrict__ dw,
+                                    float* __restrict__ dhalo) {
+  const int c8 = 8 * (blockIdx.y * blockDim.x + threadIdx.x);
+  if (c8 >= C) return;
+  const int t0 = blockIdx.x * kConvTokV;
+  const int t1 = min(T, t0 + kConvTokV);
+  const int s_end = min(T, t1 + kConvK - 1);
+  float wk[8][kConvK];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < kConvK; ++j) wk[i][j] = __bfloat162float(w[(c8 + i) * kConvK + j]);
+  int seg = find_segment(cu, nseg, t0);
+  int start = cu[seg], end = cu[seg + 1];
+  float xm3[8], xm2[8], xm1[8];
+  conv_x8(x, xs, halo, C, c8, seg, start, t0 - 3, xm3);
+  conv_x8(x, xs, halo, C, c8, seg, start, t0 - 2, xm2);
+  conv_x8(x, xs, halo, C, c8, seg, start, t0 - 1, xm1);
+  float dm3[8], dm2[8], dm1[8];
+  float dwa[8][kConvK], dha[8][kConvK - 1];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    dm3[i] = dm2[i] = dm1[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kConvK; ++j) dwa[i][j] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kConvK - 1; ++j) dha[i][j] = 0.f;
+  }
+  // dx of tokens [lo, s) whose later taps fall past the segment end (or the data)
+  auto flush = [&](int s, int lo) {
+    for (int t = max(lo, s - 3); t < min(s, t1); ++t) {
+      float out[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int k = s - t;  // 1..3 pending values: dpre[t..s-1]
+        float acc;
+        if (k == 3) acc = wk[i][3] * dm3[i] + wk[i][2] * dm2[i] + wk[i][1] * dm1[i];
+        else if (k == 2) acc = wk[i][3] * dm2[i] + wk[i][2] * dm1[i];
+        else acc = wk[i][3] * dm1[i];
+        out[i] = acc;
+      }
+      st8f(dx + (long)t * dxs + c8, out);
+    }
+  };
+  for (int s = t0; s < s_end; ++s) {
+    if (s == end) {
+      flush(s, max(t0, start));
+      while (seg + 1 < nseg && cu[seg + 1] <= s) ++seg;
+      start = cu[seg];
+      end = cu[seg + 1];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xm3[i] = xm2[i] = xm1[i] = dm3[i] = dm2[i] = dm1[i] = 0.f;
+    }
+    float xt[8], g[8], dp[8];
+    ld8f(x + (long)s * xs + c8, xt);
+    ld8f(dy + (long)s * C + c8, g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float acc = wk[i][0] * xm3[i] + wk[i][1] * xm2[i] + wk[i][2] * xm1[i] + wk[i][3] * xt[i];
+      const float sg = sigmoidf_(acc);
+      dp[i] = g[i] * sg * (1.f + acc * (1.f - sg));
+    }
+    if (s < t1) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        dwa[i][0] += dp[i] * xm3[i];
+        dwa[i][1] += dp[i] * xm2[i];
+        dwa[i][2] += dp[i] * xm1[i];
+        dwa[i][3] += dp[i] * xt[i];
+      }
+      if (seg == 0 && halo != nullptr && s - start < kConvK - 1) {
+        // taps j with s - 3 + j < start read halo row s - start + j
+#pragma unroll
+        for (int j = 0; j < kConvK - 1; ++j) {
+          const int hrow = s - start + j;
+          if (hrow < kConvK - 1) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dha[i][hrow] += wk[i][j] * dp[i];
+          }
+        }
+      }
+    }
+    if (s - 3 >= max(t0, start)) {
+      float out[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        out[i] = wk[i][3] * dm3[i] + wk[i][2] * dm2[i] + wk[i][1] * dm1[i] + wk[i][0] * dp[i];
+      st8f(dx + (long)(s - 3) * dxs + c8, out);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      xm3[i] = xm2[i];
+      xm2[i] = xm1[i];
+      xm1[i] = xt[i];
+      dm3[i] = dm2[i];
+      dm2[i] = dm1[i];
+      dm1[i] = dp[i];
+    }
+  }
+  if (s_end == T || s_end == end) flush(s_end, max(t0, start));
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < kConvK; ++j) atomicAdd(&dw[(c8 + i) * kConvK + j], dwa[i][j]);
+  if (dhalo != nullptr && halo != nullptr && t0 < cu[min(1, nseg)]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < kConvK - 1; ++j) atomicAdd(&dhalo[(long)j * C + c8 + i], dha[i][j]);
+  }
+}
+
 // ------------------------------------------------------------------ SwiGLU
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ x, long xs, __nv_bfloat16* __restrict__ y,
                                   long ys, int T, int F) {
@@ -359,6 +551,17 @@ at::Tensor conv1d_silu_fwd(const at::Tensor& x, const at::Tensor& w, const c10::
     TORCH_CHECK(halo->size(0) == kConvK - 1 && halo->size(1) == C && halo->is_contiguous(), "conv: halo [3,C]");
     hp = reinterpret_cast<const __nv_bfloat16*>(halo->data_ptr());
   }
+  const bool vec = C % 8 == 0 && x.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(w.data_ptr()) & 15) == 0;
+  if (vec) {
+    dim3 gv((T + kConvTokV - 1) / kConvTokV, (C / 8 + 127) / 128);
+    conv_fwd_vec_kernel<<<gv, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), hp, cu.data_ptr<int>(), (int)cu.numel() - 1, T, C,
+        reinterpret_cast<__nv_bfloat16*>(y.data_ptr()));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return y;
+  }
   dim3 grid((T + kConvTok - 1) / kConvTok, (C + 127) / 128);
   conv_fwd_kernel<<<grid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
@@ -384,7 +587,19 @@ std::vector<at::Tensor> conv1d_silu_bwd(const at::Tensor& dy, const at::Tensor& 
     dh = at::zeros({kConvK - 1, C}, x.options().dtype(at::kFloat));
     dhp = dh.data_ptr<float>();
   }
-  if (T > 0) {
+  const bool vec = C % 8 == 0 && x.stride(0) % 8 == 0 && dx.stride(0) % 8 == 0 &&
+                   (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(dx.data_ptr()) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(dy.data_ptr()) & 15) == 0;
+  if (T > 0 && vec) {
+    dim3 gv((T + kConvTokV - 1) / kConvTokV, (C / 8 + 127) / 128);
+    conv_bwd_vec_kernel<<<gv, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+        x.stride(0), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), hp, cu.data_ptr<int>(),
+        (int)cu.numel() - 1, T, C, reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dx.stride(0),
+        dw.data_ptr<float>(), dhp);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  } else if (T > 0) {
     dim3 grid((T + kConvTok - 1) / kConvTok, (C + 127) / 128);
     conv_bwd_kernel<<<grid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),

@@ -253,6 +253,266 @@ __global__ void __launch_bounds__(PREP_THREADS, 1) gdn_prep_kernel(PrepArgs a) {
   if (tid == 0) a.gam[ch] = __expf(GL);
 }
 
+// ============================================================================ prep (tcgen05)
+// One CTA (4 warps) per (chunk, head). K/Q/V tiles arrive by TMA; KK^T and
+// QK^T are one M = 128 MMA each (rows 64..127 of the A operand read the next
+// tile and land in TMEM lanes that are never read). Warps 0-1 (TMEM lanes =
+// chunk rows) form L and Aqk, then solve T = (I + L)^-1 one column per thread
+// and store T diag(beta e^G) and T diag(beta) in bf16 as A operands; the WY
+// products W = T diag(beta e^G) K and U = T diag(beta) V are two more MMAs.
+// Warps 2-3 write Kd and Qg meanwhile.
+constexpr int TP_THREADS = 128;
+constexpr int TP_TMEM_COLS = 512;  // [0,64) KK^T, [64,128) QK^T, [128,256) W, [256,256+DV) U
+
+struct PrepTcParams {
+  const float* g;
+  const float* beta;
+  const int* tok0;
+  const int* len;
+  __nv_bfloat16* Wn;
+  __nv_bfloat16* U;
+  __nv_bfloat16* Kd;
+  __nv_bfloat16* Qg;
+  __nv_bfloat16* Aqk;
+  float* gam;
+  float* Gc;
+  float scale;
+  int H, DV;
+  int* status;
+};
+
+__host__ __device__ constexpr int prep_tc_smem(int DV) { return (6 + DV / 64) * BLK + C * LP * 4 + 2 * C * 4 + 64 + 1024; }
+
+__global__ void __launch_bounds__(TP_THREADS, 1)
+    gdn_prep_tc_kernel(const __grid_constant__ CUtensorMap mQ, const __grid_constant__ CUtensorMap mK,
+                       const __grid_constant__ CUtensorMap mV, PrepTcParams a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  const int DV = a.DV, H = a.H, nvb = DV / 64;
+  uint8_t* sK = smem;
+  uint8_t* sQ = sK + 2 * BLK;
+  uint8_t* sV = sQ + 2 * BLK;
+  uint8_t* sTk = sV + nvb * BLK;
+  uint8_t* sTv = sTk + BLK;
+  float* Ls = reinterpret_cast<float*>(sTv + BLK);
+  float* Gs = Ls + C * LP;
+  float* Bs = Gs + C;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(Bs + C);
+  uint64_t* full = bars;
+  uint64_t* mma1 = bars + 1;
+  uint64_t* mma2 = bars + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+  const int ch = blockIdx.x, c = ch / H, h = ch % H;
+  const int t0 = a.tok0[c], n = a.len[c];
+  const int tid = threadIdx.x, warp = tid >> 5;
+
+  if (tid == 0) {
+    mbar_init(full, 1);
+    mbar_init(mma1, 1);
+    mbar_init(mma2, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, TP_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (tid == 0) {
+    mbar_arrive_expect_tx(full, (4 + nvb) * BLK);
+    tma_load_2d(sK, &mK, full, h * DK, t0);
+    tma_load_2d(sK + BLK, &mK, full, h * DK + 64, t0);
+    tma_load_2d(sQ, &mQ, full, h * DK, t0);
+    tma_load_2d(sQ + BLK, &mQ, full, h * DK + 64, t0);
+    for (int b = 0; b < nvb; ++b) tma_load_2d(sV + b * BLK, &mV, full, h * DV + b * 64, t0);
+  }
+  if (warp == 0) {
+    const int l = tid;
+    float x0 = l < n ? a.g[(long)(t0 + l) * H + h] : 0.f;
+    float x1 = l + 32 < n ? a.g[(long)(t0 + l + 32) * H + h] : 0.f;
+    Bs[l] = l < n ? a.beta[(long)(t0 + l) * H + h] : 0.f;
+    Bs[l + 32] = l + 32 < n ? a.beta[(long)(t0 + l + 32) * H + h] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
+      const float y1 = __shfl_up_sync(0xffffffffu, x1, o);
+      if (l >= o) {
+        x0 += y0;
+        x1 += y1;
+      }
+    }
+    x1 += __shfl_sync(0xffffffffu, x0, 31);
+    Gs[l] = x0;
+    Gs[l + 32] = x1;
+  }
+  bool ok = __syncthreads_and(mbar_wait_bounded(full, 0, nullptr, a.status, kTimeoutProducer));
+  if (ok) {
+    if (n < C) {
+      // rows past the end of the sequence hold the next sequence's tokens: zero them
+      const int nblk = 4 + nvb;
+      const int per = (C - n) * 8;
+      for (int e = tid; e < nblk * per; e += TP_THREADS) {
+        const int b = e / per, rem = e % per;
+        const int r = n + rem / 8, cc = rem % 8;
+        *reinterpret_cast<uint4*>(smem + b * BLK + swz(r, cc)) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    fence_proxy_async();
+  }
+  __syncthreads();
+  if (ok && tid == 0) {
+    tc_fence_after();
+    const uint32_t k_addr = smem_u32(sK), q_addr = smem_u32(sQ);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t off = (k >> 2) * BLK + (k & 3) * 32;
+      umma_bf16_ss(tmem, make_smem_desc_sw128(k_addr + off, 16, 1024), make_smem_desc_sw128(k_addr + off, 16, 1024),
+                   make_idesc_bf16(128, 64, 0, 0), k > 0);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t off = (k >> 2) * BLK + (k & 3) * 32;
+      umma_bf16_ss(tmem + 64, make_smem_desc_sw128(q_addr + off, 16, 1024),
+                   make_smem_desc_sw128(k_addr + off, 16, 1024), make_idesc_bf16(128, 64, 0, 0), k > 0);
+    }
+    umma_commit(mma1);
+  }
+  const float GL = Gs[C - 1];
+  if (ok && warp >= 2) {
+    // Kd = e^(G_last - G) k and Qg = e^G s q, one row per thread
+    const int r = tid - 64;
+    const float eg = __expf(Gs[r]) * a.scale, ed = __expf(GL - Gs[r]);
+    __nv_bfloat16* kd = a.Kd + ((long)ch * C + r) * DK;
+    __nv_bfloat16* qg = a.Qg + ((long)ch * C + r) * DK;
+#pragma unroll 4
+    for (int cc = 0; cc < 16; ++cc) {
+      float fk[8], fq[8];
+      unpack8(*reinterpret_cast<const uint4*>(sK + (cc >> 3) * BLK + swz(r, cc & 7)), fk);
+      unpack8(*reinterpret_cast<const uint4*>(sQ + (cc >> 3) * BLK + swz(r, cc & 7)), fq);
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        fk[m] *= ed;
+        fq[m] *= eg;
+      }
+      reinterpret_cast<uint4*>(kd)[cc] = pack8(fk);
+      reinterpret_cast<uint4*>(qg)[cc] = pack8(fq);
+    }
+  }
+  if (warp < 2) {
+    const bool waited = __all_sync(0xffffffffu, ok && mbar_wait_bounded(mma1, 0, nullptr, a.status, kTimeoutEpilogue));
+    if (waited) {
+      tc_fence_after();
+      const int i = tid;
+      const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+      uint32_t kk[64], qk[64];
+      tmem_ld_32x32b_x32(tl, *reinterpret_cast<uint32_t(*)[32]>(kk));
+      tmem_ld_32x32b_x32(tl + 32, *reinterpret_cast<uint32_t(*)[32]>(kk + 32));
+      tmem_ld_32x32b_x32(tl + 64, *reinterpret_cast<uint32_t(*)[32]>(qk));
+      tmem_ld_32x32b_x32(tl + 96, *reinterpret_cast<uint32_t(*)[32]>(qk + 32));
+      tmem_wait_ld();
+      const float gi = Gs[i], bi = Bs[i];
+      float aq[64];
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        const float e = j <= i ? __expf(gi - Gs[j]) : 0.f;
+        Ls[i * LP + j] = j < i ? bi * e * __uint_as_float(kk[j]) : 0.f;
+        aq[j] = j <= i ? a.scale * e * __uint_as_float(qk[j]) : 0.f;
+      }
+      uint4* dst = reinterpret_cast<uint4*>(a.Aqk + ((long)ch * C + i) * C);
+#pragma unroll
+      for (int m = 0; m < 8; ++m) dst[m] = pack8(aq + 8 * m);
+    }
+  }
+  ok = __syncthreads_and(ok);
+  if (ok && tid < C) {
+    // column j of T = (I + L)^-1 by forward substitution (four partial sums per row)
+    const int j = tid;
+    float x[C];
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+      for (int l4 = 0; l4 < i / 4; ++l4) {
+        const float4 lv = *reinterpret_cast<const float4*>(Ls + i * LP + 4 * l4);
+        s0 = fmaf(lv.x, x[4 * l4], s0);
+        s1 = fmaf(lv.y, x[4 * l4 + 1], s1);
+        s2 = fmaf(lv.z, x[4 * l4 + 2], s2);
+        s3 = fmaf(lv.w, x[4 * l4 + 3], s3);
+      }
+#pragma unroll
+      for (int l = (i / 4) * 4; l < i; ++l) s0 = fmaf(Ls[i * LP + l], x[l], s0);
+      x[i] = i < j ? 0.f : (i == j ? 1.f : -((s0 + s1) + (s2 + s3)));
+    }
+    const float sk = Bs[j] * __expf(Gs[j]), sv = Bs[j];
+    const int cb = ((j >> 3)), cw = (j & 7) * 2;
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int off = i * 128 + (((cb ^ (i & 7))) << 4) + cw;
+      *reinterpret_cast<__nv_bfloat16*>(sTk + off) = __float2bfloat16(x[i] * sk);
+      *reinterpret_cast<__nv_bfloat16*>(sTv + off) = __float2bfloat16(x[i] * sv);
+    }
+  }
+  fence_proxy_async();
+  __syncthreads();
+  if (ok && tid == 0) {
+    tc_fence_after();
+    const uint32_t tk = smem_u32(sTk), tv = smem_u32(sTv), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      umma_bf16_ss(tmem + 128, make_smem_desc_sw128(tk + k * 32, 16, 1024),
+                   make_smem_desc_sw128(k_addr + k * 2048, BLK, 1024), make_idesc_bf16(128, 128, 0, 1), k > 0);
+    const uint32_t idu = make_idesc_bf16(128, DV, 0, 1);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      umma_bf16_ss(tmem + 256, make_smem_desc_sw128(tv + k * 32, 16, 1024),
+                   make_smem_desc_sw128(v_addr + k * 2048, BLK, 1024), idu, k > 0);
+    umma_commit(mma2);
+  }
+  if (warp < 2) {
+    const bool waited = __all_sync(0xffffffffu, ok && mbar_wait_bounded(mma2, 0, nullptr, a.status, kTimeoutEpilogue));
+    if (waited) {
+      tc_fence_after();
+      const int i = tid;
+      const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+      uint4* wd = reinterpret_cast<uint4*>(a.Wn + ((long)ch * C + i) * DK);
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tl + 128 + q4 * 32, r);
+        tmem_wait_ld();
+        float f[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) f[e] = -__uint_as_float(r[e]);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) wd[q4 * 4 + m] = pack8(f + 8 * m);
+      }
+      uint4* ud = reinterpret_cast<uint4*>(a.U + ((long)ch * C + i) * DV);
+#pragma unroll 1
+      for (int q4 = 0; q4 < DV / 32; ++q4) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tl + 256 + q4 * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int m = 0; m < 4; ++m) ud[q4 * 4 + m] = pack8u(r + 8 * m);
+      }
+    }
+  }
+  if (tid < C) a.Gc[(long)ch * C + tid] = Gs[tid];
+  if (tid == 0) {
+    a.gam[ch] = __expf(GL);
+    if (!ok) mbar_wait_bounded(full, 0, nullptr, nullptr, 0);  // no TMA copy may outlive the CTA
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TP_TMEM_COLS);
+  }
+}
+
 // ============================================================================ state passes (tcgen05)
 constexpr int ST_THREADS = 192;  // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 one TMEM lane each
 constexpr int VS = 128;          // value columns per CTA
@@ -1205,7 +1465,7 @@ void check_f32(const at::Tensor& t, const char* name) {
 // q, k [T, H, 128], v [T, H, DV] bf16; g, beta [T, H] fp32; tok0/len [Nc] int32.
 std::vector<at::Tensor> gdn_chunk_prep(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                        const at::Tensor& g, const at::Tensor& beta, const at::Tensor& tok0,
-                                       const at::Tensor& len, double scale) {
+                                       const at::Tensor& len, double scale, at::Tensor& status) {
   using namespace gdnc;
   check_bf16(q, "q");
   check_bf16(k, "k");
@@ -1225,18 +1485,22 @@ std::vector<at::Tensor> gdn_chunk_prep(const at::Tensor& q, const at::Tensor& k,
   at::Tensor Aqk = at::empty({Nc, H, C, C}, bf);
   at::Tensor gam = at::empty({Nc, H}, f32), Gc = at::empty({Nc, H, C}, f32);
   if (Nc == 0) return {Wn, U, Kd, Qg, Aqk, gam, Gc};
-  PrepArgs a{reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k.data_ptr()),
-             reinterpret_cast<const __nv_bfloat16*>(v.data_ptr()), g.data_ptr<float>(), beta.data_ptr<float>(),
-             tok0.data_ptr<int>(), len.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(Wn.data_ptr()),
-             reinterpret_cast<__nv_bfloat16*>(U.data_ptr()), reinterpret_cast<__nv_bfloat16*>(Kd.data_ptr()),
-             reinterpret_cast<__nv_bfloat16*>(Qg.data_ptr()), reinterpret_cast<__nv_bfloat16*>(Aqk.data_ptr()),
-             gam.data_ptr<float>(), Gc.data_ptr<float>(), (float)scale, H, DV};
-  static bool attr = false;
-  if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM));
-    attr = true;
+  const int64_t T = q.size(0);
+  TORCH_CHECK(T >= C, "gdn: at least 64 tokens");
+  CUtensorMap mQ = map2d(q, T, (int64_t)H * DK, (int64_t)H * DK), mK = map2d(k, T, (int64_t)H * DK, (int64_t)H * DK);
+  CUtensorMap mV = map2d(v, T, (int64_t)H * DV, (int64_t)H * DV);
+  PrepTcParams a{g.data_ptr<float>(), beta.data_ptr<float>(), tok0.data_ptr<int>(), len.data_ptr<int>(),
+                 reinterpret_cast<__nv_bfloat16*>(Wn.data_ptr()), reinterpret_cast<__nv_bfloat16*>(U.data_ptr()),
+                 reinterpret_cast<__nv_bfloat16*>(Kd.data_ptr()), reinterpret_cast<__nv_bfloat16*>(Qg.data_ptr()),
+                 reinterpret_cast<__nv_bfloat16*>(Aqk.data_ptr()), gam.data_ptr<float>(), Gc.data_ptr<float>(),
+                 (float)scale, H, DV, status.data_ptr<int>()};
+  const int smem = prep_tc_smem(DV);
+  static int attr = 0;
+  if (attr < smem) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gdn_prep_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = smem;
   }
-  gdn_prep_kernel<<<Nc * H, PREP_THREADS, PREP_SMEM, at::cuda::getCurrentCUDAStream()>>>(a);
+  gdn_prep_tc_kernel<<<Nc * H, TP_THREADS, smem, at::cuda::getCurrentCUDAStream()>>>(mQ, mK, mV, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {Wn, U, Kd, Qg, Aqk, gam, Gc};
 }

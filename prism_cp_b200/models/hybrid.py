@@ -28,6 +28,7 @@ from ..ops.cross_entropy import head_cross_entropy
 from ..ops.elementwise import causal_conv1d_silu, rope, swiglu
 from ..ops.gemm import linear
 from ..ops.norms import gated_rms_norm, l2_norm, rms_norm
+from ..ops.split import split_columns
 from .config import HybridConfig
 
 
@@ -68,9 +69,10 @@ class GQAMixer(nn.Module):
         y = rms_norm(x, self.norm, self.eps)
         qkv = linear(y, self.qkv)
         qd, kd = self.hq * self.d, self.hkv * self.d
-        q = rope(qkv[:, :qd], ctx.positions, self.hq, self.d, self.base).view(T, self.hq, self.d)
-        k = rope(qkv[:, qd:qd + kd], ctx.positions, self.hkv, self.d, self.base).view(T, self.hkv, self.d)
-        v = qkv[:, qd + kd:].view(T, self.hkv, self.d)
+        qs, ks, vs = split_columns(qkv, (qd, kd, kd))
+        q = rope(qs, ctx.positions, self.hq, self.d, self.base).view(T, self.hq, self.d)
+        k = rope(ks, ctx.positions, self.hkv, self.d, self.base).view(T, self.hkv, self.d)
+        v = vs.view(T, self.hkv, self.d)
         o = ctx.attention(q, k, v)
         return linear(o.reshape(T, qd), self.proj)
 
@@ -101,13 +103,13 @@ class GDNMixer(nn.Module):
         y = rms_norm(x, self.norm, self.eps)
         p = linear(y, self.in_proj)
         c_end = 2 * self.qk_dim + self.v_dim
-        qkv = ctx.conv(p[:, :c_end], self.conv)
-        q = l2_norm(qkv[:, :self.qk_dim], self.H).view(T, self.H, self.dk)
-        k = l2_norm(qkv[:, self.qk_dim:2 * self.qk_dim], self.H).view(T, self.H, self.dk)
-        v = qkv[:, 2 * self.qk_dim:].view(T, self.H, self.dv)
-        z = p[:, c_end:c_end + self.v_dim]
-        b = p[:, c_end + self.v_dim:c_end + self.v_dim + self.H].float()
-        a = p[:, c_end + self.v_dim + self.H:c_end + self.v_dim + 2 * self.H].float()
+        conv_in, z, b, a = split_columns(p, (c_end, self.v_dim, self.H, self.H))
+        qkv = ctx.conv(conv_in, self.conv)
+        qs, ks, vs = split_columns(qkv, (self.qk_dim, self.qk_dim, self.v_dim))
+        q = l2_norm(qs, self.H).view(T, self.H, self.dk)
+        k = l2_norm(ks, self.H).view(T, self.H, self.dk)
+        v = vs.view(T, self.H, self.dv)
+        b, a = b.float(), a.float()
         beta = torch.sigmoid(b)
         g = -self.A_log.exp() * F.softplus(a + self.dt_bias)
         o = ctx.delta_rule(q, k, v, g, beta)

@@ -253,7 +253,8 @@ class _FusedChunkRule(torch.autograd.Function):
         qb, kb, vb = (t.to(bf).contiguous() for t in (q, k, v))
         gf, bt = g.float().contiguous(), beta.float().contiguous()
         st = status(q.device)
-        Wn, U, Kd, Qg, Aqk, gam, _ = L.gdn_chunk_prep(qb, kb, vb, gf, bt, layout.tok0_dev, layout.len_dev, scale)
+        Wn, U, Kd, Qg, Aqk, gam, _ = L.gdn_chunk_prep(qb, kb, vb, gf, bt, layout.tok0_dev, layout.len_dev, scale,
+                                                     st)
         T, H, DV = vb.shape
         o = torch.empty_like(vb)
         S_final = torch.empty((len(layout.lengths), H, qb.shape[-1], DV), dtype=torch.float32, device=q.device)
@@ -271,7 +272,7 @@ class _FusedChunkRule(torch.autograd.Function):
         qb, kb, vb, gf, bt, s0 = ctx.saved_tensors
         lay = ctx.layout
         st = status(qb.device)
-        Wn, U, Kd, Qg, Aqk, gam, Gc = L.gdn_chunk_prep(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, ctx.scale)
+        Wn, U, Kd, Qg, Aqk, gam, Gc = L.gdn_chunk_prep(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, ctx.scale, st)
         Nc, H = Wn.shape[0], Wn.shape[1]
         DV = vb.shape[-1]
         states = torch.empty((Nc, H, DV, 128), dtype=torch.bfloat16, device=qb.device)
