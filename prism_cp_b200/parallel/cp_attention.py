@@ -54,7 +54,7 @@ class Ring:
     def __init__(self, ctx):
         self.c, self.i = ctx.cp, ctx.index
         self.team = ctx.team
-        self.ranks = ctx.group_ranks
+        self.ranks = ctx.global_ranks
         lens = [ctx.lengths[s] for s in ctx.samples]
         self.half = [n // (2 * self.c) for n in lens]
         dev = ctx.device

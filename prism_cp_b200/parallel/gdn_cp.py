@@ -24,7 +24,6 @@ from __future__ import annotations
 
 import torch
 import torch.distributed as dist
-import torch.distributed.nn.functional as distf
 
 from ..ops.elementwise import causal_conv1d_silu
 from ..ops.gdn import (chunk_output, chunk_prep, chunk_state, chunk_transition, fused_gated_delta_rule,
@@ -55,6 +54,30 @@ class _Tie(torch.autograd.Function):
 
 def tie(x, anchor):
     return _Tie.apply(x, anchor)
+
+
+class _AllGather(torch.autograd.Function):
+    """All-gather of equal-size flat tensors over a team; the backward sums every
+    rank's gradient of the stacked result and keeps this rank's row (group-relative
+    ranks throughout, so it works for teams of any global ranks)."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        n = dist.get_world_size(group)
+        out = [torch.empty_like(x) for _ in range(n)]
+        dist.all_gather(out, x.contiguous(), group=group)
+        return torch.stack(out)
+
+    @staticmethod
+    def backward(ctx, g):
+        g = g.contiguous()
+        dist.all_reduce(g, group=ctx.group)
+        return g[dist.get_rank(ctx.group)], None
+
+
+def all_gather_rows(x, group):
+    return _AllGather.apply(x, group)
 
 
 def rank_links(ctx):
@@ -114,8 +137,8 @@ def conv_with_halo(ctx, x, weight):
         tail = x[-HALO:]
     else:
         tail = torch.cat([x.new_zeros((HALO - x.shape[0], x.shape[1])), x], 0)
-    prev_rank = ctx.group_ranks[i - 1] if i > 0 else -1
-    next_rank = ctx.group_ranks[i + 1] if i + 1 < c else -1
+    prev_rank = ctx.global_ranks[i - 1] if i > 0 else -1
+    next_rank = ctx.global_ranks[i + 1] if i + 1 < c else -1
     halo = _HaloExchange.apply(tail, prev_rank, next_rank, first_cont, has_next, ctx.team)
     if not first_cont:
         return tie(causal_conv1d_silu(x, weight, ctx.cu_segments), halo)
@@ -166,7 +189,7 @@ def delta_rule_cp(ctx, q, k, v, g, beta):
         # a rank whose contribution is a constant must still own an all-gather
         # backward node, or the team's backward collectives would not match
         packed = packed.detach().requires_grad_(True)
-    gathered = distf.all_gather(packed, group=ctx.team)
+    gathered = all_gather_rows(packed, ctx.team)
     initial = None
     if first_cont:
         chain = [i - 1]
@@ -185,6 +208,6 @@ def delta_rule_cp(ctx, q, k, v, g, beta):
         initial = torch.cat([state[None], rest], 0)
     if fused:
         o, _ = fused_gated_delta_rule(q, k, v, g, beta, layout, initial_state=initial)
-        return tie(o, torch.stack(gathered))
+        return tie(o, gathered)
     Delta, S_all, _ = chunk_state(prep, initial)
-    return tie(chunk_output(prep, Delta, S_all), torch.stack(gathered))
+    return tie(chunk_output(prep, Delta, S_all), gathered)

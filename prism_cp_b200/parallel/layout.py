@@ -48,6 +48,10 @@ class LocalLayout:
         self.tokens = sum(c for _, _, _, c in self.spans)
         self.device = device
         self.team = teams.team(group.ranks) if (teams is not None and self.cp > 1) else None
+        self.world_group = getattr(teams, "world_group", None)
+        # point-to-point peers are addressed by global rank
+        to_global = getattr(teams, "global_rank", None)
+        self.global_ranks = tuple(to_global(r) for r in group.ranks) if to_global is not None else group.ranks
         pos = []
         for _, begin, _, count in self.spans:
             pos.extend(range(begin, begin + count))

@@ -23,21 +23,43 @@ def dyadic_intervals(world: int) -> list[tuple[int, ...]]:
 
 
 class Teams:
-    def __init__(self, world: int | None = None, backend: str | None = None):
+    """Dyadic CP teams over logical ranks.
+
+    Without tensor parallelism a logical rank is a global rank. With a
+    ``TPContext`` of size tp, logical rank l of TP index i is global rank
+    l * tp + i; every TP index gets its own teams (all ranks take part in all
+    ``new_group`` calls) and this rank keeps the teams of its own index.
+    """
+
+    def __init__(self, world: int | None = None, backend: str | None = None, tp=None):
         self.initialized = dist.is_available() and dist.is_initialized()
-        self.world = world if world is not None else (dist.get_world_size() if self.initialized else 1)
-        self.rank = dist.get_rank() if self.initialized else 0
+        tp_on = tp is not None and tp.enabled
+        if tp_on:
+            self.world, self.rank = tp.logical_world, tp.logical_rank
+            self.rank_map = tp.rank_map()
+            indices = range(tp.tp)
+        else:
+            self.world = world if world is not None else (dist.get_world_size() if self.initialized else 1)
+            self.rank = dist.get_rank() if self.initialized else 0
+            self.rank_map = list(range(self.world))
+            indices = [0]
         self.groups: dict[tuple[int, ...], object] = {}
+        self._world_group = dist.group.WORLD if (self.initialized and not tp_on) else None
         if self.initialized and self.world > 1:
             for ranks in dyadic_intervals(self.world):
-                if len(ranks) == self.world:
-                    group = dist.group.WORLD
-                elif len(ranks) == 1:
-                    group = None
-                else:
-                    group = dist.new_group(list(ranks), backend=backend)
-                if self.rank in ranks:
-                    self.groups[ranks] = group
+                for index in indices:
+                    members = [l * tp.tp + index for l in ranks] if tp_on else list(ranks)
+                    if len(ranks) == 1:
+                        group = None
+                    elif len(ranks) == self.world and not tp_on:
+                        group = dist.group.WORLD
+                    else:
+                        group = dist.new_group(members, backend=backend)
+                    mine = (not tp_on or index == tp.index) and self.rank in ranks
+                    if mine:
+                        self.groups[ranks] = group
+                        if len(ranks) == self.world:
+                            self._world_group = group
 
     def team(self, ranks: tuple[int, ...]):
         if len(ranks) == 1:
@@ -46,6 +68,10 @@ class Teams:
             raise KeyError(f"rank {self.rank} is not a member of team {ranks}")
         return self.groups[ranks]
 
+    def global_rank(self, logical: int) -> int:
+        return self.rank_map[logical]
+
     @property
     def world_group(self):
-        return dist.group.WORLD if self.initialized else None
+        """Group of all logical ranks of this rank's TP index (the whole world without TP)."""
+        return self._world_group

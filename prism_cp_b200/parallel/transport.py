@@ -100,6 +100,8 @@ def move(x: torch.Tensor, source, target, group=None) -> torch.Tensor:
     """Reshard rows of ``x`` from LocalLayout ``source`` to LocalLayout ``target``."""
     if source.layout == target.layout:
         return x
+    if group is None:
+        group = getattr(source, "world_group", None)
     lengths_key = tuple(sorted(source.lengths.items()))
     compiled = _compiled(source.layout, target.layout, lengths_key, source.world, source.rank, str(x.device))
     if compiled is None:

@@ -104,9 +104,10 @@ class FlatParameters:
 class DistributedAdamW:
     def __init__(self, flat: FlatParameters, group=None, lr=3e-4, min_lr=3e-5, betas=(0.9, 0.95), eps=1e-8,
                  weight_decay=0.1, clip_grad=1.0, warmup_steps=0, decay_steps=1000, decay_style="cosine",
-                 world: int | None = None):
+                 world: int | None = None, tp_group=None):
         self.flat = flat
         self.group = group
+        self.tp_group = tp_group
         if world is None:
             world = dist.get_world_size(group) if (dist.is_available() and dist.is_initialized()) else 1
         self.world = world
@@ -126,6 +127,14 @@ class DistributedAdamW:
         self.v = torch.zeros_like(self.master)
         self.grad_shard = torch.zeros_like(self.master)
         self.wd_mask = torch.cat([flat.decay_mask[a:a + n] for _, _, a, n, _ in self.slices]).to(torch.float32)
+        # elements of tensor-parallel shards: their squared norms add up across the TP group
+        self.tp_mask = None
+        if tp_group is not None:
+            shard = torch.zeros(flat.padded, dtype=torch.bool, device=flat.flat.device)
+            for p, (o, n) in zip(flat.params, flat.offsets):
+                if not getattr(p, "tp_replicated", False):
+                    shard[o:o + n] = True
+            self.tp_mask = torch.cat([shard[a:a + n] for _, _, a, n, _ in self.slices]).to(torch.float32)
         self.sumsq = torch.zeros(1, dtype=torch.float32, device=self.master.device)
         self.lr, self.min_lr, self.betas, self.eps = lr, min_lr, betas, eps
         self.weight_decay, self.clip_grad = weight_decay, clip_grad
@@ -193,6 +202,15 @@ class DistributedAdamW:
     # -------------------------------------------------------------- update
     def grad_norm_sq(self) -> torch.Tensor:
         self.sumsq.zero_()
+        if self.tp_mask is not None:
+            sq = self.grad_shard.float().pow(2)
+            parts = torch.stack([(sq * self.tp_mask).sum(), (sq * (1 - self.tp_mask)).sum()])
+            if self.world > 1:
+                dist.all_reduce(parts, op=dist.ReduceOp.SUM, group=self.group)
+            shard_part = parts[:1].clone()
+            dist.all_reduce(shard_part, op=dist.ReduceOp.SUM, group=self.tp_group)
+            self.sumsq.copy_(shard_part + parts[1:])
+            return self.sumsq
         if is_cuda(self.grad_shard):
             lib().sumsq_accumulate(self.grad_shard, self.sumsq)
         else:

@@ -53,10 +53,17 @@ class Trainer:
         self.model, self.teams, self.device = model, teams, device
         self.world = teams.world
         self.rank = teams.rank
+        tp = getattr(model, "tp", None)
+        self.tp = tp if (tp is not None and tp.enabled) else None
+        if group is None and self.tp is not None:
+            # every TP index updates its own copy of the model; shards never mix across indices
+            group = teams.world_group
+        self.group = group
         self.flat = FlatParameters(model, self.world, bucket_bytes=bucket_bytes if overlap_grad_reduce else None)
         self.optimizer = DistributedAdamW(self.flat, group=group, lr=lr, min_lr=min_lr,
                                           weight_decay=weight_decay, clip_grad=clip_grad,
-                                          warmup_steps=warmup_steps, decay_steps=decay_steps, world=self.world)
+                                          warmup_steps=warmup_steps, decay_steps=decay_steps, world=self.world,
+                                          tp_group=self.tp.group if self.tp is not None else None)
         self.overlap = self.optimizer.enable_overlap() if overlap_grad_reduce else None
         self.cache = LayoutCache(self.world, self.rank, device, teams)
         self.hbm_guard = hbm_guard and device.type == "cuda"
@@ -87,7 +94,7 @@ class Trainer:
                 self.audit.backward(len(self.audit.events))
             self.loss_acc += loss.detach()
         if self.world > 1:
-            dist.all_reduce(self.loss_acc, op=dist.ReduceOp.SUM)
+            dist.all_reduce(self.loss_acc, op=dist.ReduceOp.SUM, group=self.group)
         return self.loss_acc
 
     def train_step(self, batch: GlobalBatch, plan: Plan, inputs: list | None = None,

@@ -249,3 +249,64 @@ def _tiny_model_case(rank, world, steps):
 
 def test_tiny_hybrid_cp2_matches_cp1_over_two_steps():
     run_ranks(_tiny_model_case, 2, 2, timeout=600)
+
+
+# ------------------------------------------------------------------ tensor parallel
+def _tp_case(rank, world, tp, steps):
+    from prism_cp_b200.models.config import hybrid_tiny
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.parallel.teams import Teams
+    from prism_cp_b200.parallel.tensor import make_tp
+    from prism_cp_b200.planner.joint.ir import Group, Layout, Microbatch, Plan
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.trainer import Trainer
+    cfg = hybrid_tiny()
+    lengths = [1280, 768]
+    batch = make_batch(lengths, cfg.vocab_size, seed=1)
+    tpc = make_tp(tp)
+    L = world // tp
+    if L == 2:
+        gdn = Layout((Group((0, 1), (0, 1)),), "contiguous")
+        gqa = Layout((Group((0,), (0,)), Group((1,), (1,))), "zigzag")
+    else:
+        gdn = Layout((Group((0,), (0, 1)),), "contiguous")
+        gqa = Layout((Group((0,), (0, 1)),), "zigzag")
+    layers = tuple((gdn, gdn) if c == "G" else (gqa, gqa) for c in cfg.pattern)
+    plan = Plan(L, cfg.pattern, (Microbatch(gqa, layers),))
+    model = HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0, tp=tpc)
+    trainer = Trainer(model, Teams(tp=tpc), torch.device("cpu"), lr=1e-3, weight_decay=0.1)
+    losses, norms = [], []
+    for _ in range(steps):
+        res = trainer.train_step(batch, plan)
+        losses.append(res.loss)
+        norms.append(float(trainer.optimizer.sumsq.sqrt()))
+    if rank == 0:
+        ref_model = HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0)
+        one = Layout((Group((0,), (0, 1)),), "zigzag")
+        ref_plan = Plan(1, cfg.pattern, (Microbatch(one, tuple((one.with_mode("contiguous"),) * 2 if c == "G"
+                                                                  else (one, one) for c in cfg.pattern)),))
+
+        class Solo:
+            world, rank, initialized = 1, 0, False
+
+            def team(self, ranks):
+                return None
+
+        ref_tr = Trainer(ref_model, Solo(), torch.device("cpu"), lr=1e-3, weight_decay=0.1)
+        ref_losses, ref_norms = [], []
+        for _ in range(steps):
+            r = ref_tr.train_step(batch, ref_plan)
+            ref_losses.append(r.loss)
+            ref_norms.append(float(ref_tr.optimizer.sumsq.sqrt()))
+        for a, b in zip(losses, ref_losses):
+            assert abs(a - b) <= 1e-4 * abs(b), (losses, ref_losses)
+        for a, b in zip(norms, ref_norms):
+            assert abs(a - b) <= 1e-4 * abs(b), (norms, ref_norms)
+
+
+def test_tensor_parallel_tp2_matches_single_process():
+    run_ranks(_tp_case, 2, 2, 2, timeout=600)
+
+
+def test_tensor_parallel_tp2_cp2_matches_single_process():
+    run_ranks(_tp_case, 4, 2, 2, timeout=900)
