@@ -310,3 +310,57 @@ def test_tensor_parallel_tp2_matches_single_process():
 
 def test_tensor_parallel_tp2_cp2_matches_single_process():
     run_ranks(_tp_case, 4, 2, 2, timeout=900)
+
+
+# ------------------------------------------------------------------ pipeline parallel (1F1B)
+def _pp_case(rank, world, pp, steps):
+    from prism_cp_b200.models.config import hybrid_tiny
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.planner.fixed import uniform_plan
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.pipeline import PipelineTrainer, make_stage
+    from prism_cp_b200.runtime.trainer import Trainer
+    cfg = hybrid_tiny()
+    ws = world // pp
+    batch = make_batch([1024, 512, 512, 256, 256], cfg.vocab_size, seed=2)
+    plan = uniform_plan(batch.lengths, ws, ws, 1024 // ws, cfg.pattern)
+    assert len(plan.microbatches) >= 2
+    info = make_stage(pp, cfg.num_layers)
+    model = HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0,
+                        layers=range(info.first_layer, info.first_layer + info.num_layers),
+                        pre_process=info.stage == 0, post_process=info.stage == pp - 1)
+    trainer = PipelineTrainer(model, info, torch.device("cpu"), lr=1e-3, weight_decay=0.1)
+    losses, norms = [], []
+    for _ in range(steps):
+        res = trainer.train_step(batch, plan)
+        losses.append(res.loss)
+        norms.append(float(trainer.optimizer.sumsq.sqrt()))
+        assert 0.0 <= res.extra["bubble_fraction"] <= 1.0
+    if rank == 0:
+        ref_model = HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0)
+        ref_plan = uniform_plan(batch.lengths, 1, 1, 1024, cfg.pattern)
+
+        class Solo:
+            world, rank, initialized = 1, 0, False
+
+            def team(self, ranks):
+                return None
+
+        ref_tr = Trainer(ref_model, Solo(), torch.device("cpu"), lr=1e-3, weight_decay=0.1)
+        ref_losses, ref_norms = [], []
+        for _ in range(steps):
+            r = ref_tr.train_step(batch, ref_plan)
+            ref_losses.append(r.loss)
+            ref_norms.append(float(ref_tr.optimizer.sumsq.sqrt()))
+        for a, b in zip(losses, ref_losses):
+            assert abs(a - b) <= 1e-4 * abs(b), (losses, ref_losses)
+        for a, b in zip(norms, ref_norms):
+            assert abs(a - b) <= 1e-4 * abs(b), (norms, ref_norms)
+
+
+def test_pipeline_1f1b_pp2_matches_single_process():
+    run_ranks(_pp_case, 2, 2, 2, timeout=600)
+
+
+def test_pipeline_1f1b_pp2_cp2_matches_single_process():
+    run_ranks(_pp_case, 4, 2, 2, timeout=900)
