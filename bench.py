@@ -76,7 +76,13 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+            self.rows.append((time.monotonic(), [x.strip() for x in line.split(",")]))
+
+    def mark_start(self):
+        self.t0 = time.monotonic()
+
+    def mark_end(self):
+        self.t1 = time.monotonic()
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -87,6 +93,10 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        self.__exit__()
+        t0, t1 = getattr(self, "t0", 0.0), getattr(self, "t1", float("inf"))
+        window = [r for t, r in self.rows if t0 <= t <= t1]
+        self.rows = window or [r for _, r in self.rows]
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
@@ -155,6 +165,8 @@ def main():
             dist.barrier()
 
     progress(rank, f"model ready ({cfg.parameter_count() / 1e9:.2f}B params, {len(plan.microbatches)} microbatches)")
+    # the clock sampler's process starts before any GPU work, its samples are cut to the timed region
+    clocks = ClockSampler(local).__enter__()
     for _ in range(args.warmup):
         trainer.train_step(batch, plan, dev_inputs, read_loss=False)
     progress(rank, "warm-up done")
@@ -162,12 +174,14 @@ def main():
     barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        start.record()
-        for _ in range(args.steps):
-            trainer.train_step(batch, plan, dev_inputs, read_loss=False)
-        end.record()
-        torch.cuda.synchronize()
+    clocks.mark_start()
+    start.record()
+    for i in range(args.steps):
+        trainer.train_step(batch, plan, dev_inputs, read_loss=False)
+        progress(rank, f"timed step {i + 1}/{args.steps} queued")
+    end.record()
+    torch.cuda.synchronize()
+    clocks.mark_end()
     barrier()
     torch.cuda.synchronize()
     ms = torch.tensor([start.elapsed_time(end) / args.steps], dtype=torch.float64, device=device)
