@@ -66,9 +66,26 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int k) {
 }
 
 // ------------------------------------------------------------------ dK, dV
+// One CTA per (128-key tile, kv head). Query tiles of 64 rows stream through a
+// two-stage TMA ring; S^T / dP^T for the next query tile are computed into the
+// other half of a double-buffered TMEM region while the compute warps turn the
+// current one into P^T and dS^T, so TMA, tensor cores and the softmax-gradient
+// math overlap.
+//   TMEM: S^T [0,64) / [64,128), dP^T [128,192) / [192,256), dV [256,384), dK [384,512)
 // Src = PeerTiles: this rank's keys of a zigzag team; tiles hold (seq, global
 // position of the first key, its local row); Q / dO tiles and their LSE / D rows
 // are read from the rank that owns each query tile.
+constexpr int KV_QT = 64;                    // query rows per iteration
+constexpr int KV_QBYTES = KV_QT * D * 2;     // 16 KiB: 64 rows x 128 dims (two 64-dim boxes)
+constexpr int KV_QHALF = KV_QBYTES / 2;
+constexpr int KV_PBYTES = 128 * KV_QT * 2;   // 16 KiB: 128 keys x 64 queries
+constexpr int KV_OFF_Q = 2 * TILE_BYTES;                 // Q[2]
+constexpr int KV_OFF_DO = KV_OFF_Q + 2 * KV_QBYTES;      // dO[2]
+constexpr int KV_OFF_PT = KV_OFF_DO + 2 * KV_QBYTES;
+constexpr int KV_OFF_DST = KV_OFF_PT + KV_PBYTES;
+constexpr int KV_OFF_STAT = KV_OFF_DST + KV_PBYTES;      // lse[2][64], dsum[2][64]
+constexpr int KV_OFF_BAR = KV_OFF_STAT + 4 * KV_QT * 4;
+
 template <class Src>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -79,21 +96,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
   uint8_t* sV = smem + TILE_BYTES;
-  uint8_t* sQ = smem + 2 * TILE_BYTES;
-  uint8_t* sdO = smem + 3 * TILE_BYTES;
-  uint8_t* sPT = smem + 4 * TILE_BYTES;
-  uint8_t* sdST = smem + 5 * TILE_BYTES;
-  float* lse_s = reinterpret_cast<float*>(smem + 6 * TILE_BYTES);
-  float* dsum_s = lse_s + 128;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(dsum_s + 128);
+  uint8_t* sPT = smem + KV_OFF_PT;
+  uint8_t* sdST = smem + KV_OFF_DST;
+  float* lse_s = reinterpret_cast<float*>(smem + KV_OFF_STAT);   // [2][64]
+  float* dsum_s = lse_s + 2 * KV_QT;                             // [2][64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + KV_OFF_BAR);
   uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;
-  uint64_t* s_full = bars + 2;
-  uint64_t* p_full = bars + 3;
-  uint64_t* mma_done = bars + 4;
-  uint64_t* acc_done = bars + 5;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 7);
+  uint64_t* q_full = bars + 1;    // [2]
+  uint64_t* q_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_free = bars + 7;    // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* mma_done = bars + 10;
+  uint64_t* acc_done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 13);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kv_head = blockIdx.y;
@@ -113,16 +130,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_seg = p.cu_k[seq];
     k_len = p.cu_k[seq + 1] - k_seg;
   }
-  const int ktile = k0 / TILE;
-  const int n_qt = (q_len + TILE - 1) / TILE;
-  const int i_start = p.causal ? ktile : 0;
+  const int n_qt = (q_len + KV_QT - 1) / KV_QT;
+  const int i_start = p.causal ? k0 / KV_QT : 0;
   const int per_head = max(0, n_qt - i_start);
   const int n_it = rep * per_head;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(q_full, 1);
-    mbar_init(s_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&q_full[b], 1);
+      mbar_init(&q_empty[b], 1);
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_free[b], 128);
+    }
     mbar_init(p_full, 128);
     mbar_init(mma_done, 1);
     mbar_init(acc_done, 1);
@@ -139,73 +159,106 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 4) {
+    // ---------------------------------------------------------------- producer
     if (lane == 0 && n_it > 0) {
       mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
       tma_load_3d(sK, &tmK, kv_full, 0, kv_head, k_seg + k0);
       tma_load_3d(sK + HALF, &tmK, kv_full, 64, kv_head, k_seg + k0);
       tma_load_3d(sV, &tmV, kv_full, 0, kv_head, k_seg + k0);
       tma_load_3d(sV + HALF, &tmV, kv_full, 64, kv_head, k_seg + k0);
+      int issued = 0;
       for (int it = 0; it < n_it; ++it) {
+        const int s = it & 1;
+        if (it >= 2 && !mbar_wait_bounded(&q_empty[s], ((it >> 1) - 1) & 1, abort_flag, p.status, kTimeoutProducer))
+          break;
         const int h = kv_head * rep + it / per_head;
         const int i = i_start + it % per_head;
-        if (it > 0 && !mbar_wait_bounded(mma_done, (it - 1) & 1, abort_flag, p.status, kTimeoutProducer)) break;
-        mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
-        int qrow = q_seg + i * TILE;
+        int qrow = q_seg + i * KV_QT;
         const CUtensorMap* mq = &tmQ;
         const CUtensorMap* mo = &tmO;
         if constexpr (PEER) {
           int owner;
-          qrow = peer_row(src, seq, i * TILE, owner);
+          qrow = peer_row(src, seq, i * KV_QT, owner);
           mq = &src.a[owner];
           mo = &src.b[owner];
         }
-        tma_load_3d(sQ, mq, q_full, 0, h, qrow);
-        tma_load_3d(sQ + HALF, mq, q_full, 64, h, qrow);
-        tma_load_3d(sdO, mo, q_full, 0, h, qrow);
-        tma_load_3d(sdO + HALF, mo, q_full, 64, h, qrow);
+        uint8_t* dq = smem + KV_OFF_Q + s * KV_QBYTES;
+        uint8_t* dd = smem + KV_OFF_DO + s * KV_QBYTES;
+        mbar_arrive_expect_tx(&q_full[s], 2 * KV_QBYTES);
+        tma_load_3d(dq, mq, &q_full[s], 0, h, qrow);
+        tma_load_3d(dq + KV_QHALF, mq, &q_full[s], 64, h, qrow);
+        tma_load_3d(dd, mo, &q_full[s], 0, h, qrow);
+        tma_load_3d(dd + KV_QHALF, mo, &q_full[s], 64, h, qrow);
+        issued = it + 1;
       }
+      // copies still in flight after an abort land before the CTA exits
+      mbar_wait_bounded(kv_full, 0, nullptr, nullptr, 0);
+      for (int it = issued > 2 ? issued - 2 : 0; it < issued; ++it)
+        mbar_wait_bounded(&q_full[it & 1], (it >> 1) & 1, nullptr, nullptr, 0);
     }
   } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer
     if (lane == 0 && n_it > 0) {
-      constexpr uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);
-      constexpr uint32_t idesc_km = make_idesc_bf16(128, 128, 0, 1);
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), adO = smem_u32(sdO);
-      const uint32_t aPT = smem_u32(sPT), adST = smem_u32(sdST);
+      constexpr uint32_t idesc_s = make_idesc_bf16(128, KV_QT, 0, 0);   // K/V K-major x Q/dO K-major
+      constexpr uint32_t idesc_g = make_idesc_bf16(128, 128, 0, 1);     // P^T/dS^T K-major x dO/Q MN-major
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aPT = smem_u32(sPT), adST = smem_u32(sdST);
       bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, p.status, kTimeoutMma);
-      for (int it = 0; ok && it < n_it; ++it) {
-        if (!mbar_wait_bounded(q_full, it & 1, abort_flag, p.status, kTimeoutMma)) break;
-        tc_fence_after();
+      for (int it = 0; ok && it <= n_it; ++it) {
+        if (it < n_it) {
+          const int s = it & 1, b = it & 1;
+          if (!mbar_wait_bounded(&q_full[s], (it >> 1) & 1, abort_flag, p.status, kTimeoutMma)) break;
+          if (it >= 2 && !mbar_wait_bounded(&s_free[b], ((it >> 1) - 1) & 1, abort_flag, p.status, kTimeoutMma)) break;
+          tc_fence_after();
+          const uint32_t aQ = smem_u32(smem + KV_OFF_Q + s * KV_QBYTES);
+          const uint32_t adO = smem_u32(smem + KV_OFF_DO + s * KV_QBYTES);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_bf16_ss(tmem + 0, desc_kmajor(aK, k), desc_kmajor(aQ, k), idesc_kk, k > 0);
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t bo = (k >> 2) * KV_QHALF + (k & 3) * 32;
+            umma_bf16_ss(tmem + b * KV_QT, desc_kmajor(aK, k), make_smem_desc_sw128(aQ + bo, 16, 1024), idesc_s,
+                         k > 0);
+          }
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_bf16_ss(tmem + 128, desc_kmajor(aV, k), desc_kmajor(adO, k), idesc_kk, k > 0);
-        umma_commit(s_full);
-        if (!mbar_wait_bounded(p_full, it & 1, abort_flag, p.status, kTimeoutMma)) break;
-        tc_fence_after();
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t bo = (k >> 2) * KV_QHALF + (k & 3) * 32;
+            umma_bf16_ss(tmem + 128 + b * KV_QT, desc_kmajor(aV, k), make_smem_desc_sw128(adO + bo, 16, 1024),
+                         idesc_s, k > 0);
+          }
+          umma_commit(&s_full[b]);
+        }
+        if (it >= 1) {
+          const int jt = it - 1, s = jt & 1;
+          if (!mbar_wait_bounded(p_full, jt & 1, abort_flag, p.status, kTimeoutMma)) break;
+          tc_fence_after();
+          const uint32_t aQ = smem_u32(smem + KV_OFF_Q + s * KV_QBYTES);
+          const uint32_t adO = smem_u32(smem + KV_OFF_DO + s * KV_QBYTES);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_bf16_ss(tmem + 256, desc_kmajor(aPT, k), desc_mnmajor(adO, k), idesc_km, (it > 0 || k > 0));
+          for (int k = 0; k < KV_QT / 16; ++k)
+            umma_bf16_ss(tmem + 256, make_smem_desc_sw128(aPT + k * 32, 16, 1024),
+                         make_smem_desc_sw128(adO + k * 2048, KV_QHALF, 1024), idesc_g, (jt > 0 || k > 0));
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_bf16_ss(tmem + 384, desc_kmajor(adST, k), desc_mnmajor(aQ, k), idesc_km, (it > 0 || k > 0));
-        umma_commit(mma_done);
+          for (int k = 0; k < KV_QT / 16; ++k)
+            umma_bf16_ss(tmem + 384, make_smem_desc_sw128(adST + k * 32, 16, 1024),
+                         make_smem_desc_sw128(aQ + k * 2048, KV_QHALF, 1024), idesc_g, (jt > 0 || k > 0));
+          umma_commit(mma_done);
+          umma_commit(&q_empty[s]);
+        }
       }
       umma_commit(acc_done);
     }
   } else {
-    const int r = threadIdx.x;
+    // ---------------------------------------------------------------- P^T / dS^T rows
+    const int r = threadIdx.x;  // key row == TMEM lane
     const int kk = k0 + r;
     const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
     const float c_log2 = p.scale * kLog2e;
+    const bool row_ok = kk < k_len;
     bool ok = true;
     for (int it = 0; it < n_it && ok; ++it) {
+      const int b = it & 1;
       const int h = kv_head * rep + it / per_head;
       const int i = i_start + it % per_head;
-      const int q0 = i * TILE;
-      if (it > 0) named_sync_compute();
-      {
+      const int q0 = i * KV_QT;
+      if (r < KV_QT) {
         const int qq = q0 + r;
         const bool v = qq < q_len;
         const float* lse_src = p.lse;
@@ -217,45 +270,48 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           lse_src = src.lse[owner];
           dsum_src = src.dsum[owner];
         }
-        lse_s[r] = v ? lse_src[(long)h * p.tq + row] * kLog2e : INFINITY;
-        dsum_s[r] = v ? dsum_src[(long)h * p.tq + row] : 0.f;
+        lse_s[b * KV_QT + r] = v ? lse_src[(long)h * p.tq + row] * kLog2e : INFINITY;
+        dsum_s[b * KV_QT + r] = v ? dsum_src[(long)h * p.tq + row] : 0.f;
       }
       named_sync_compute();
-      bool waited = mbar_wait_bounded(s_full, it & 1, abort_flag, p.status, kTimeoutEpilogue);
-      if (waited && it > 0) waited = mbar_wait_bounded(mma_done, (it - 1) & 1, abort_flag, p.status, kTimeoutEpilogue);
-      ok = named_barrier_and(waited, 1, 128);
+      ok = named_barrier_and(mbar_wait_bounded(&s_full[b], (it >> 1) & 1, abort_flag, p.status, kTimeoutEpilogue),
+                             1, 128);
       if (!ok) break;
       tc_fence_after();
-      const bool row_ok = kk < k_len;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t s_raw[32], dp_raw[32];
-        tmem_ld_32x32b_x32(lane_base + c * 32, s_raw);
-        tmem_ld_32x32b_x32(lane_base + 128 + c * 32, dp_raw);
-        tmem_wait_ld();
-        float pv[32], dsv[32];
+      uint32_t s_raw[64], dp_raw[64];
+      tmem_ld_32x32b_x32(lane_base + b * KV_QT, *reinterpret_cast<uint32_t(*)[32]>(s_raw));
+      tmem_ld_32x32b_x32(lane_base + b * KV_QT + 32, *reinterpret_cast<uint32_t(*)[32]>(s_raw + 32));
+      tmem_ld_32x32b_x32(lane_base + 128 + b * KV_QT, *reinterpret_cast<uint32_t(*)[32]>(dp_raw));
+      tmem_ld_32x32b_x32(lane_base + 128 + b * KV_QT + 32, *reinterpret_cast<uint32_t(*)[32]>(dp_raw + 32));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_free[b]);
+      // P^T and dS^T overwrite the loaded S^T / dP^T values in place (keeps register use flat)
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int col = c * 32 + e;
-          const int qq = q0 + col;
-          const bool valid = row_ok && qq < q_len && (!p.causal || kk <= qq);
-          const float pe = valid ? exp2f(__uint_as_float(s_raw[e]) * c_log2 - lse_s[col]) : 0.f;
-          pv[e] = pe;
-          dsv[e] = pe * (__uint_as_float(dp_raw[e]) - dsum_s[col]);
-        }
+      for (int e = 0; e < KV_QT; ++e) {
+        const int qq = q0 + e;
+        const bool valid = row_ok && qq < q_len && (!p.causal || kk <= qq);
+        const float pe = valid ? exp2f(__uint_as_float(s_raw[e]) * c_log2 - lse_s[b * KV_QT + e]) : 0.f;
+        s_raw[e] = __float_as_uint(pe);
+        dp_raw[e] = __float_as_uint(pe * (__uint_as_float(dp_raw[e]) - dsum_s[b * KV_QT + e]));
+      }
+      const float* pv = reinterpret_cast<const float*>(s_raw);
+      const float* dsv = reinterpret_cast<const float*>(dp_raw);
+      // P^T / dS^T of the previous query tile must have been consumed
+      if (it > 0) {
+        ok = named_barrier_and(mbar_wait_bounded(mma_done, (it - 1) & 1, abort_flag, p.status, kTimeoutEpilogue),
+                               1, 128);
+        if (!ok) break;
+      }
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int chunk = c * 4 + g;
-          write_chunk_sw128(sPT, r, chunk,
-                            make_uint4(pack_bf16x2(pv[8 * g], pv[8 * g + 1]), pack_bf16x2(pv[8 * g + 2], pv[8 * g + 3]),
-                                       pack_bf16x2(pv[8 * g + 4], pv[8 * g + 5]),
-                                       pack_bf16x2(pv[8 * g + 6], pv[8 * g + 7])));
-          write_chunk_sw128(sdST, r, chunk,
-                            make_uint4(pack_bf16x2(dsv[8 * g], dsv[8 * g + 1]),
-                                       pack_bf16x2(dsv[8 * g + 2], dsv[8 * g + 3]),
-                                       pack_bf16x2(dsv[8 * g + 4], dsv[8 * g + 5]),
-                                       pack_bf16x2(dsv[8 * g + 6], dsv[8 * g + 7])));
-        }
+      for (int g = 0; g < 8; ++g) {
+        const int off = r * 128 + ((g ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(sPT + off) =
+            make_uint4(pack_bf16x2(pv[8 * g], pv[8 * g + 1]), pack_bf16x2(pv[8 * g + 2], pv[8 * g + 3]),
+                       pack_bf16x2(pv[8 * g + 4], pv[8 * g + 5]), pack_bf16x2(pv[8 * g + 6], pv[8 * g + 7]));
+        *reinterpret_cast<uint4*>(sdST + off) =
+            make_uint4(pack_bf16x2(dsv[8 * g], dsv[8 * g + 1]), pack_bf16x2(dsv[8 * g + 2], dsv[8 * g + 3]),
+                       pack_bf16x2(dsv[8 * g + 4], dsv[8 * g + 5]), pack_bf16x2(dsv[8 * g + 6], dsv[8 * g + 7]));
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
@@ -272,14 +328,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __nv_bfloat16* dk_row = p.out + (long)(k_seg + kk) * p.out_stride + (long)kv_head * D;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
-        uint32_t a[32], b[32];
+        uint32_t a[32], bb[32];
         if (loaded) {
           tmem_ld_32x32b_x32(lane_base + 256 + c * 32, a);
-          tmem_ld_32x32b_x32(lane_base + 384 + c * 32, b);
+          tmem_ld_32x32b_x32(lane_base + 384 + c * 32, bb);
           tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) a[e] = b[e] = 0u;
+          for (int e = 0; e < 32; ++e) a[e] = bb[e] = 0u;
         }
         if (!store) continue;
 #pragma unroll
@@ -290,10 +346,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               pack_bf16x2(__uint_as_float(a[8 * v + 4]), __uint_as_float(a[8 * v + 5])),
               pack_bf16x2(__uint_as_float(a[8 * v + 6]), __uint_as_float(a[8 * v + 7])));
           reinterpret_cast<uint4*>(dk_row + c * 32)[v] = make_uint4(
-              pack_bf16x2(__uint_as_float(b[8 * v]) * p.scale, __uint_as_float(b[8 * v + 1]) * p.scale),
-              pack_bf16x2(__uint_as_float(b[8 * v + 2]) * p.scale, __uint_as_float(b[8 * v + 3]) * p.scale),
-              pack_bf16x2(__uint_as_float(b[8 * v + 4]) * p.scale, __uint_as_float(b[8 * v + 5]) * p.scale),
-              pack_bf16x2(__uint_as_float(b[8 * v + 6]) * p.scale, __uint_as_float(b[8 * v + 7]) * p.scale));
+              pack_bf16x2(__uint_as_float(bb[8 * v]) * p.scale, __uint_as_float(bb[8 * v + 1]) * p.scale),
+              pack_bf16x2(__uint_as_float(bb[8 * v + 2]) * p.scale, __uint_as_float(bb[8 * v + 3]) * p.scale),
+              pack_bf16x2(__uint_as_float(bb[8 * v + 4]) * p.scale, __uint_as_float(bb[8 * v + 5]) * p.scale),
+              pack_bf16x2(__uint_as_float(bb[8 * v + 6]) * p.scale, __uint_as_float(bb[8 * v + 7]) * p.scale));
         }
       }
     }
@@ -523,7 +579,7 @@ __global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ dO, long d
   if (lane == 0) out[(long)h * T + t] = acc;
 }
 
-constexpr int SMEM_KV = 6 * TILE_BYTES + 1024 + 256 + 1024;
+constexpr int SMEM_KV = KV_OFF_BAR + 256 + 1024;
 constexpr int SMEM_Q = 7 * TILE_BYTES + 256 + 1024;
 
 }  // namespace attnb
@@ -548,6 +604,8 @@ void attention_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Ten
   }
   CUtensorMap tq = make_head_map_128(q), tk = make_head_map_128(k), tv = make_head_map_128(v),
               tdo = make_head_map_128(dout);
+  // the dK/dV kernel streams query tiles of KV_QT rows
+  CUtensorMap tq64 = make_head_map(q, KV_QT), tdo64 = make_head_map(dout, KV_QT);
   Params p;
   p.cu_q = cu_q.data_ptr<int>();
   p.cu_k = cu_k.data_ptr<int>();
@@ -573,8 +631,8 @@ void attention_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Ten
     pk.out = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
     pk.out2 = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
     pk.out_stride = dk.stride(0);
-    attn_bwd_kv_kernel<NoPeers><<<dim3(tiles_k.size(0), hkv), NUM_THREADS, SMEM_KV, stream>>>(tq, tk, tv, tdo, pk,
-                                                                                             NoPeers{0});
+    attn_bwd_kv_kernel<NoPeers><<<dim3(tiles_k.size(0), hkv), NUM_THREADS, SMEM_KV, stream>>>(tq64, tk, tv, tdo64,
+                                                                                             pk, NoPeers{0});
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   if (tiles_q.size(0) > 0) {
@@ -635,8 +693,8 @@ void attention_bwd_peer(const std::vector<at::Tensor>& q_peers, const std::vecto
               tv = make_head_map_128(v_peers[rank]), tdo = make_head_map_128(do_peers[rank]);
   PeerTiles kv_src{}, q_src{};
   for (int r = 0; r < cp; ++r) {
-    kv_src.a[r] = make_head_map_128(q_peers[r]);
-    kv_src.b[r] = make_head_map_128(do_peers[r]);
+    kv_src.a[r] = make_head_map(q_peers[r], KV_QT);
+    kv_src.b[r] = make_head_map(do_peers[r], KV_QT);
     kv_src.lse[r] = lse_peers[r].data_ptr<float>();
     kv_src.dsum[r] = dsum_peers[r].data_ptr<float>();
     q_src.a[r] = make_head_map_128(k_peers[r]);
@@ -649,7 +707,9 @@ void attention_bwd_peer(const std::vector<at::Tensor>& q_peers, const std::vecto
   pk.out = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
   pk.out2 = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
   pk.out_stride = dk.stride(0);
-  attn_bwd_kv_kernel<PeerTiles><<<dim3(ntiles, hkv), NUM_THREADS, SMEM_KV, stream>>>(tq, tk, tv, tdo, pk, kv_src);
+  CUtensorMap tq64 = make_head_map(q, KV_QT), tdo64 = make_head_map(do_peers[rank], KV_QT);
+  attn_bwd_kv_kernel<PeerTiles><<<dim3(ntiles, hkv), NUM_THREADS, SMEM_KV, stream>>>(tq64, tk, tv, tdo64, pk,
+                                                                                     kv_src);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   Params pq = p;
   pq.out = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());

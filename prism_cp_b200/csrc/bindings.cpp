@@ -37,7 +37,7 @@ void gdn_state_bwd(const at::Tensor& W, const at::Tensor& dDelta_ext, const at::
                    at::Tensor& dDelta, at::Tensor& G_next, at::Tensor& dS0);
 std::vector<at::Tensor> gdn_chunk_prep(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                        const at::Tensor& g, const at::Tensor& beta, const at::Tensor& tok0,
-                                       const at::Tensor& len, double scale, at::Tensor& status);
+                                       const at::Tensor& len, double scale, bool with_aux, at::Tensor& status);
 void gdn_chunk_fwd(const at::Tensor& Wn, const at::Tensor& U, const at::Tensor& Kd, const at::Tensor& Qg,
                    const at::Tensor& Aqk, const at::Tensor& gam, const at::Tensor& tok0, const at::Tensor& len,
                    const at::Tensor& seq_chunks, const c10::optional<at::Tensor>& S0,
@@ -51,7 +51,8 @@ void gdn_chunk_bwd_state(const at::Tensor& Wn, const at::Tensor& Kd, const at::T
                          at::Tensor& status);
 std::vector<at::Tensor> gdn_chunk_bwd_local(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                             const at::Tensor& g, const at::Tensor& beta, const at::Tensor& tok0,
-                                            const at::Tensor& len, const at::Tensor& Gc, const at::Tensor& states,
+                                            const at::Tensor& len, const at::Tensor& Gc, const at::Tensor& aux,
+                                            const at::Tensor& states,
                                             const at::Tensor& dstates, const at::Tensor& rows,
                                             const at::Tensor& drows, const at::Tensor& dout, double scale,
                                             at::Tensor& status);

@@ -10,8 +10,9 @@
 //   O_c     = Qg_c S_c + Aqk_c Delta_c
 //
 // Kernels (one launch each, in this order):
-//   gdn_prep_kernel        CUDA cores, one CTA per (chunk, head): G, KK^T, QK^T,
-//                          forward substitution for [W | U], Kd, Qg, Aqk.
+//   gdn_prep_tc_kernel     tcgen05, one CTA per (chunk, head): G, KK^T and QK^T on
+//                          the tensor cores, T = (I + L)^-1 by forward substitution,
+//                          W and U as T-products on the tensor cores, Kd, Qg, Aqk.
 //   gdn_state_tc_kernel<0> tcgen05, one CTA per (sequence, head, 128 columns of dv):
 //                          the sequential state pass with the output fused in. The
 //                          state is held TRANSPOSED in tensor memory (lane = value
@@ -77,30 +78,9 @@ PRISM_DEVICE uint4 pack8u(const uint32_t* r) {
                     pack_bf16x2(__uint_as_float(r[6]), __uint_as_float(r[7])));
 }
 
-// ============================================================================ prep
-constexpr int PREP_THREADS = 256;
+// ============================================================================ shared loaders
 constexpr int KP = DK + 1;  // fp32 row pitch of the k/q tiles (odd: conflict-free column reads)
 constexpr int LP = 68;      // fp32 row pitch of L (multiple of 4: float4 row reads)
-constexpr int PREP_SMEM = (2 * C * KP + C * LP + 2 * C) * 4;
-
-struct PrepArgs {
-  const __nv_bfloat16* q;  // [T, H, DK]
-  const __nv_bfloat16* k;  // [T, H, DK]
-  const __nv_bfloat16* v;  // [T, H, DV]
-  const float* g;          // [T, H]
-  const float* beta;       // [T, H]
-  const int* tok0;         // [Nc]
-  const int* len;          // [Nc]
-  __nv_bfloat16* Wn;       // [Nc, H, C, DK]
-  __nv_bfloat16* U;        // [Nc, H, C, DV]
-  __nv_bfloat16* Kd;       // [Nc, H, C, DK]
-  __nv_bfloat16* Qg;       // [Nc, H, C, DK]
-  __nv_bfloat16* Aqk;      // [Nc, H, C, C]
-  float* gam;              // [Nc, H]
-  float* Gc;               // [Nc, H, C]
-  float scale;
-  int H, DV;
-};
 
 // Loads k (and q * scale) of one chunk as fp32 rows, zero rows past the end, plus
 // g/beta; returns after the in-chunk cumulative sum G is in Gs.
@@ -146,113 +126,6 @@ PRISM_DEVICE void load_chunk_kq(const __nv_bfloat16* q, const __nv_bfloat16* k, 
   __syncthreads();
 }
 
-// 64x64 register-tiled products over the DK columns of two fp32 row tiles:
-// out1[x][y] = a1_i . b_j, out2[x][y] = a2_i . b_j with i = ti + 16x, j = tj + 16y.
-PRISM_DEVICE void gram64(const float* a1, const float* a2, const float* b, int ti, int tj, float (&o1)[4][4],
-                         float (&o2)[4][4]) {
-#pragma unroll
-  for (int x = 0; x < 4; ++x)
-#pragma unroll
-    for (int y = 0; y < 4; ++y) o1[x][y] = o2[x][y] = 0.f;
-#pragma unroll 4
-  for (int d = 0; d < DK; ++d) {
-    float u1[4], u2[4], w[4];
-#pragma unroll
-    for (int x = 0; x < 4; ++x) {
-      u1[x] = a1[(ti + 16 * x) * KP + d];
-      u2[x] = a2[(ti + 16 * x) * KP + d];
-      w[x] = b[(tj + 16 * x) * KP + d];
-    }
-#pragma unroll
-    for (int x = 0; x < 4; ++x)
-#pragma unroll
-      for (int y = 0; y < 4; ++y) {
-        o1[x][y] = fmaf(u1[x], w[y], o1[x][y]);
-        o2[x][y] = fmaf(u2[x], w[y], o2[x][y]);
-      }
-  }
-}
-
-__global__ void __launch_bounds__(PREP_THREADS, 1) gdn_prep_kernel(PrepArgs a) {
-  extern __shared__ float sm[];
-  float* ks = sm;
-  float* qs = ks + C * KP;
-  float* Ls = qs + C * KP;
-  float* Gs = Ls + C * LP;
-  float* Bs = Gs + C;
-  const int H = a.H, DV = a.DV;
-  const int ch = blockIdx.x, c = ch / H, h = ch % H;
-  const int t0 = a.tok0[c], n = a.len[c];
-  const int tid = threadIdx.x;
-  load_chunk_kq(a.q, a.k, a.g, a.beta, t0, n, h, H, a.scale, ks, qs, Gs, Bs);
-
-  const int ti = tid >> 4, tj = tid & 15;
-  float kk[4][4], qk[4][4];
-  gram64(ks, qs, ks, ti, tj, kk, qk);
-#pragma unroll
-  for (int x = 0; x < 4; ++x) {
-    const int i = ti + 16 * x;
-#pragma unroll
-    for (int y = 0; y < 4; ++y) {
-      const int j = tj + 16 * y;
-      const float e = j <= i ? __expf(Gs[i] - Gs[j]) : 0.f;
-      Ls[i * LP + j] = j < i ? Bs[i] * e * kk[x][y] : 0.f;
-      a.Aqk[((long)ch * C + i) * C + j] = __float2bfloat16(j <= i ? qk[x][y] * e : 0.f);
-    }
-  }
-  __syncthreads();
-
-  // (I + L) X = [beta e^G K | beta V], one right-hand-side column per thread.
-  for (int col = tid; col < DK + DV; col += PREP_THREADS) {
-    float x[C];
-    if (col < DK) {
-#pragma unroll
-      for (int i = 0; i < C; ++i) x[i] = Bs[i] * __expf(Gs[i]) * ks[i * KP + col];
-    } else {
-      const __nv_bfloat16* vp = a.v + (long)h * DV + (col - DK);
-#pragma unroll
-      for (int i = 0; i < C; ++i) x[i] = i < n ? Bs[i] * bf2f(vp[(long)(t0 + i) * H * DV]) : 0.f;
-    }
-#pragma unroll
-    for (int i = 1; i < C; ++i) {
-      float acc = x[i];
-#pragma unroll
-      for (int j4 = 0; j4 < (i + 3) / 4; ++j4) {
-        const float4 l = *reinterpret_cast<const float4*>(Ls + i * LP + 4 * j4);
-        acc = fmaf(-l.x, x[4 * j4], acc);
-        if (4 * j4 + 1 < i) acc = fmaf(-l.y, x[4 * j4 + 1], acc);
-        if (4 * j4 + 2 < i) acc = fmaf(-l.z, x[4 * j4 + 2], acc);
-        if (4 * j4 + 3 < i) acc = fmaf(-l.w, x[4 * j4 + 3], acc);
-      }
-      x[i] = acc;
-    }
-    if (col < DK) {
-#pragma unroll
-      for (int i = 0; i < C; ++i) a.Wn[((long)ch * C + i) * DK + col] = __float2bfloat16(-x[i]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < C; ++i) a.U[((long)ch * C + i) * DV + (col - DK)] = __float2bfloat16(x[i]);
-    }
-  }
-
-  const float GL = Gs[C - 1];
-  for (int e = tid; e < C * (DK / 8); e += PREP_THREADS) {
-    const int i = e / (DK / 8), a8 = (e % (DK / 8)) * 8;
-    const float eg = __expf(Gs[i]), ed = __expf(GL - Gs[i]);
-    float fq[8], fk[8];
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      fq[m] = qs[i * KP + a8 + m] * eg;
-      fk[m] = ks[i * KP + a8 + m] * ed;
-    }
-    const long off = ((long)ch * C + i) * DK + a8;
-    *reinterpret_cast<uint4*>(a.Qg + off) = pack8(fq);
-    *reinterpret_cast<uint4*>(a.Kd + off) = pack8(fk);
-  }
-  if (tid < C) a.Gc[(long)ch * C + tid] = Gs[tid];
-  if (tid == 0) a.gam[ch] = __expf(GL);
-}
-
 // ============================================================================ prep (tcgen05)
 // One CTA (4 warps) per (chunk, head). K/Q/V tiles arrive by TMA; KK^T and
 // QK^T are one M = 128 MMA each (rows 64..127 of the A operand read the next
@@ -276,6 +149,7 @@ struct PrepTcParams {
   __nv_bfloat16* Aqk;
   float* gam;
   float* Gc;
+  float* aux;  // optional [Nc * H, 3, C, C] fp32: k_i.k_j, s q_i.k_j and T, for the backward
   float scale;
   int H, DV;
   int* status;
@@ -424,6 +298,17 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
       uint4* dst = reinterpret_cast<uint4*>(a.Aqk + ((long)ch * C + i) * C);
 #pragma unroll
       for (int m = 0; m < 8; ++m) dst[m] = pack8(aq + 8 * m);
+      if (a.aux != nullptr) {
+        float4* kr = reinterpret_cast<float4*>(a.aux + ((long)ch * 3 * C + i) * C);
+        float4* qr = reinterpret_cast<float4*>(a.aux + ((long)ch * 3 * C + C + i) * C);
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+          kr[m] = make_float4(__uint_as_float(kk[4 * m]), __uint_as_float(kk[4 * m + 1]),
+                              __uint_as_float(kk[4 * m + 2]), __uint_as_float(kk[4 * m + 3]));
+          qr[m] = make_float4(a.scale * __uint_as_float(qk[4 * m]), a.scale * __uint_as_float(qk[4 * m + 1]),
+                              a.scale * __uint_as_float(qk[4 * m + 2]), a.scale * __uint_as_float(qk[4 * m + 3]));
+        }
+      }
     }
   }
   ok = __syncthreads_and(ok);
@@ -445,6 +330,11 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
 #pragma unroll
       for (int l = (i / 4) * 4; l < i; ++l) s0 = fmaf(Ls[i * LP + l], x[l], s0);
       x[i] = i < j ? 0.f : (i == j ? 1.f : -((s0 + s1) + (s2 + s3)));
+    }
+    if (a.aux != nullptr) {
+      float* tcol = a.aux + ((long)ch * 3 * C + 2 * C) * C + j;
+#pragma unroll
+      for (int i = 0; i < C; ++i) tcol[i * C] = x[i];
     }
     const float sk = Bs[j] * __expf(Gs[j]), sv = Bs[j];
     const int cb = ((j >> 3)), cw = (j & 7) * 2;
@@ -1044,6 +934,7 @@ struct LocalArgs {
   const int* tok0;
   const int* len;
   const float* Gc;      // [Nc, H, C]
+  const float* aux;     // [Nc * H, 3, C, C]: k.k, s q.k, T (from the prep recompute)
   const float* dWnT;    // [Nc, H, DK, C]
   const float* dQgT;
   const float* dKdT;
@@ -1095,32 +986,14 @@ __global__ void __launch_bounds__(LB_THREADS, 1) gdn_bwd_local_kernel(LocalArgs 
   }
   load_chunk_kq(a.q, a.k, a.g, a.beta, t0, n, h, H, a.scale, ks, qs, Gs, Bs);
   {
-    float kk[4][4], qk[4][4];
-    gram64(ks, qs, ks, ti, tj, kk, qk);
-#pragma unroll
-    for (int x = 0; x < 4; ++x)
-#pragma unroll
-      for (int y = 0; y < 4; ++y) {
-        const int i = ti + 16 * x, j = tj + 16 * y;
-        KK[i * P65 + j] = kk[x][y];
-        QK[i * P65 + j] = qk[x][y];
-        X1[i * P65 + j] = j < i ? Bs[i] * __expf(Gs[i] - Gs[j]) * kk[x][y] : 0.f;  // L
-      }
-  }
-  __syncthreads();
-  // T = (I + L)^-1 by forward substitution, one column per thread
-  if (tid < C) {
-    const int j = tid;
-    float x[C];
-#pragma unroll
-    for (int i = 0; i < C; ++i) {
-      float acc = (i == j) ? 1.f : 0.f;
-#pragma unroll
-      for (int l = 0; l < i; ++l) acc = fmaf(-X1[i * P65 + l], x[l], acc);
-      x[i] = acc;
+    // k.k, s q.k and T = (I + L)^-1 come from the prep recompute
+    const float* src = a.aux + ch * 3 * C * C;
+    for (int e = tid; e < C * C; e += LB_THREADS) {
+      const int i = e / C, j = e % C;
+      KK[i * P65 + j] = src[e];
+      QK[i * P65 + j] = src[C * C + e];
+      Ts[i * P65 + j] = src[2 * C * C + e];
     }
-#pragma unroll
-    for (int i = 0; i < C; ++i) Ts[i * P65 + j] = x[i];
   }
   // dW = -dWn, stored [i][a]
   for (int e = tid; e < DK * C; e += LB_THREADS) {
@@ -1465,7 +1338,7 @@ void check_f32(const at::Tensor& t, const char* name) {
 // q, k [T, H, 128], v [T, H, DV] bf16; g, beta [T, H] fp32; tok0/len [Nc] int32.
 std::vector<at::Tensor> gdn_chunk_prep(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                        const at::Tensor& g, const at::Tensor& beta, const at::Tensor& tok0,
-                                       const at::Tensor& len, double scale, at::Tensor& status) {
+                                       const at::Tensor& len, double scale, bool with_aux, at::Tensor& status) {
   using namespace gdnc;
   check_bf16(q, "q");
   check_bf16(k, "k");
@@ -1484,7 +1357,8 @@ std::vector<at::Tensor> gdn_chunk_prep(const at::Tensor& q, const at::Tensor& k,
   at::Tensor Kd = at::empty({Nc, H, C, DK}, bf), Qg = at::empty({Nc, H, C, DK}, bf);
   at::Tensor Aqk = at::empty({Nc, H, C, C}, bf);
   at::Tensor gam = at::empty({Nc, H}, f32), Gc = at::empty({Nc, H, C}, f32);
-  if (Nc == 0) return {Wn, U, Kd, Qg, Aqk, gam, Gc};
+  at::Tensor aux = with_aux ? at::empty({Nc, H, 3, C, C}, f32) : at::empty({0}, f32);
+  if (Nc == 0) return {Wn, U, Kd, Qg, Aqk, gam, Gc, aux};
   const int64_t T = q.size(0);
   TORCH_CHECK(T >= C, "gdn: at least 64 tokens");
   CUtensorMap mQ = map2d(q, T, (int64_t)H * DK, (int64_t)H * DK), mK = map2d(k, T, (int64_t)H * DK, (int64_t)H * DK);
@@ -1493,7 +1367,7 @@ std::vector<at::Tensor> gdn_chunk_prep(const at::Tensor& q, const at::Tensor& k,
                  reinterpret_cast<__nv_bfloat16*>(Wn.data_ptr()), reinterpret_cast<__nv_bfloat16*>(U.data_ptr()),
                  reinterpret_cast<__nv_bfloat16*>(Kd.data_ptr()), reinterpret_cast<__nv_bfloat16*>(Qg.data_ptr()),
                  reinterpret_cast<__nv_bfloat16*>(Aqk.data_ptr()), gam.data_ptr<float>(), Gc.data_ptr<float>(),
-                 (float)scale, H, DV, status.data_ptr<int>()};
+                 with_aux ? aux.data_ptr<float>() : nullptr, (float)scale, H, DV, status.data_ptr<int>()};
   const int smem = prep_tc_smem(DV);
   static int attr = 0;
   if (attr < smem) {
@@ -1502,7 +1376,7 @@ std::vector<at::Tensor> gdn_chunk_prep(const at::Tensor& q, const at::Tensor& k,
   }
   gdn_prep_tc_kernel<<<Nc * H, TP_THREADS, smem, at::cuda::getCurrentCUDAStream()>>>(mQ, mK, mV, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return {Wn, U, Kd, Qg, Aqk, gam, Gc};
+  return {Wn, U, Kd, Qg, Aqk, gam, Gc, aux};
 }
 
 namespace gdnc {
@@ -1595,7 +1469,8 @@ void gdn_chunk_bwd_state(const at::Tensor& Wn, const at::Tensor& Kd, const at::T
 // Chunk-local backward: dv-contractions on tcgen05, then the WY/decay backward.
 std::vector<at::Tensor> gdn_chunk_bwd_local(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                             const at::Tensor& g, const at::Tensor& beta, const at::Tensor& tok0,
-                                            const at::Tensor& len, const at::Tensor& Gc, const at::Tensor& states,
+                                            const at::Tensor& len, const at::Tensor& Gc, const at::Tensor& aux,
+                                            const at::Tensor& states,
                                             const at::Tensor& dstates, const at::Tensor& rows,
                                             const at::Tensor& drows, const at::Tensor& dout, double scale,
                                             at::Tensor& status) {
@@ -1627,7 +1502,8 @@ std::vector<at::Tensor> gdn_chunk_bwd_local(const at::Tensor& q, const at::Tenso
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   LocalArgs la{reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k.data_ptr()),
                reinterpret_cast<const __nv_bfloat16*>(v.data_ptr()), g.data_ptr<float>(), beta.data_ptr<float>(),
-               tok0.data_ptr<int>(), len.data_ptr<int>(), Gc.data_ptr<float>(), dWnT.data_ptr<float>(),
+               tok0.data_ptr<int>(), len.data_ptr<int>(), Gc.data_ptr<float>(), aux.data_ptr<float>(),
+               dWnT.data_ptr<float>(),
                dQgT.data_ptr<float>(), dKdT.data_ptr<float>(), dAqk.data_ptr<float>(), dDV.data_ptr<float>(),
                dgam.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(drows.data_ptr()),
                reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()),

@@ -20,8 +20,8 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// [tokens, heads, 128] bf16 view, boxes of {64 dims, 1 head, 128 tokens}, 128-byte swizzle.
-inline CUtensorMap make_head_map_128(const at::Tensor& t) {
+// [tokens, heads, 128] bf16 view, boxes of {64 dims, 1 head, box_rows tokens}, 128-byte swizzle.
+inline CUtensorMap make_head_map(const at::Tensor& t, uint32_t box_rows) {
   TORCH_CHECK(t.dim() == 3 && t.size(2) == 128 && t.stride(2) == 1 && t.stride(1) == 128,
               "attention: tensors must be [tokens, heads, 128] with contiguous heads");
   TORCH_CHECK(t.scalar_type() == at::kBFloat16, "attention: bf16 tensors required");
@@ -30,7 +30,7 @@ inline CUtensorMap make_head_map_128(const at::Tensor& t) {
   CUtensorMap map;
   cuuint64_t dims[3] = {128, (cuuint64_t)t.size(1), (cuuint64_t)t.size(0)};
   cuuint64_t strides[2] = {256, (cuuint64_t)t.stride(0) * 2};
-  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t box[3] = {64, 1, box_rows};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, t.data_ptr(), dims, strides, box,
                                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -38,5 +38,7 @@ inline CUtensorMap make_head_map_128(const at::Tensor& t) {
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
   return map;
 }
+
+inline CUtensorMap make_head_map_128(const at::Tensor& t) { return make_head_map(t, 128); }
 
 }  // namespace prism

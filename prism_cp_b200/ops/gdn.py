@@ -236,6 +236,16 @@ def fused_supported(q: torch.Tensor, v: torch.Tensor) -> bool:
     return is_cuda(q) and q.shape[-1] == 128 and v.shape[-1] in (128, 256) and q.shape[0] >= CHUNK
 
 
+_SIDE = {}
+
+
+def _side_stream(device) -> torch.cuda.Stream:
+    s = _SIDE.get(device.index)
+    if s is None:
+        s = _SIDE[device.index] = torch.cuda.Stream(device=device)
+    return s
+
+
 class _FusedChunkRule(torch.autograd.Function):
     """Chunked gated delta rule on the fused kernels.
 
@@ -253,8 +263,8 @@ class _FusedChunkRule(torch.autograd.Function):
         qb, kb, vb = (t.to(bf).contiguous() for t in (q, k, v))
         gf, bt = g.float().contiguous(), beta.float().contiguous()
         st = status(q.device)
-        Wn, U, Kd, Qg, Aqk, gam, _ = L.gdn_chunk_prep(qb, kb, vb, gf, bt, layout.tok0_dev, layout.len_dev, scale,
-                                                     st)
+        Wn, U, Kd, Qg, Aqk, gam, _, _ = L.gdn_chunk_prep(qb, kb, vb, gf, bt, layout.tok0_dev, layout.len_dev,
+                                                        scale, False, st)
         T, H, DV = vb.shape
         o = torch.empty_like(vb)
         S_final = torch.empty((len(layout.lengths), H, qb.shape[-1], DV), dtype=torch.float32, device=q.device)
@@ -272,13 +282,22 @@ class _FusedChunkRule(torch.autograd.Function):
         qb, kb, vb, gf, bt, s0 = ctx.saved_tensors
         lay = ctx.layout
         st = status(qb.device)
-        Wn, U, Kd, Qg, Aqk, gam, Gc = L.gdn_chunk_prep(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, ctx.scale, st)
+        Wn, U, Kd, Qg, Aqk, gam, Gc, aux = L.gdn_chunk_prep(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, ctx.scale,
+                                                            True, st)
         Nc, H = Wn.shape[0], Wn.shape[1]
         DV = vb.shape[-1]
         states = torch.empty((Nc, H, DV, 128), dtype=torch.bfloat16, device=qb.device)
         rows = torch.empty((Nc, H, DV, CHUNK), dtype=torch.bfloat16, device=qb.device)
-        L.gdn_chunk_fwd(Wn, U, Kd, Qg, Aqk, gam, lay.tok0_dev, lay.len_dev, lay.seq_chunks_dev, s0, None, None,
-                        states, rows, st)
+        # the recomputed forward states and the reverse pass are independent sequential
+        # scans over a few dozen SMs each: run them side by side on two streams
+        main = torch.cuda.current_stream(qb.device)
+        side = _side_stream(qb.device)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            L.gdn_chunk_fwd(Wn, U, Kd, Qg, Aqk, gam, lay.tok0_dev, lay.len_dev, lay.seq_chunks_dev, s0, None, None,
+                            states, rows, st)
+        for t in (Wn, U, Kd, Qg, Aqk, gam, states, rows) + ((s0,) if s0 is not None else ()):
+            t.record_stream(side)
         dstates, drows = torch.empty_like(states), torch.empty_like(rows)
         dS0 = torch.empty_like(s0) if ctx.has_s0 else None
         if do is None:
@@ -287,7 +306,8 @@ class _FusedChunkRule(torch.autograd.Function):
         dsf = dS_final.float().contiguous() if dS_final is not None else None
         L.gdn_chunk_bwd_state(Wn, Kd, Qg, Aqk, gam, dob, lay.tok0_dev, lay.len_dev, lay.seq_chunks_dev, dsf, dS0,
                               dstates, drows, st)
-        dq, dk, dv, dg, dbeta = L.gdn_chunk_bwd_local(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, Gc, states,
+        main.wait_stream(side)
+        dq, dk, dv, dg, dbeta = L.gdn_chunk_bwd_local(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, Gc, aux, states,
                                                       dstates, rows, drows, dob, ctx.scale, st)
         tq, tk, tv, tg, tb = ctx.dtypes
         return dq.to(tq), dk.to(tk), dv.to(tv), dg.to(tg), dbeta.to(tb), None, None, dS0

@@ -13,6 +13,8 @@ ranks with an all-reduce MIN, and rank-max step time.
 from __future__ import annotations
 
 import math
+import os
+import sys
 import time
 from dataclasses import dataclass, field
 
@@ -25,6 +27,9 @@ from .batch import GlobalBatch, HostInputs, local_inputs
 from .executor import LayoutCache, MicrobatchRun
 from .optimizer import DistributedAdamW, FlatParameters
 from .records import StepRecorder, step_record
+
+
+DEBUG_SYNC = os.environ.get("PRISM_DEBUG_SYNC", "0") == "1"
 
 
 def hbm_budget(total_bytes: int) -> int:
@@ -86,16 +91,30 @@ class Trainer:
             dev = host.to(self.device) if host.tokens.device != self.device else host
             run = MicrobatchRun(mb, batch_lengths, self.cache)
             loss, _ = run.forward(self.model, dev.tokens, dev.labels, dev.weights)
+            self._debug_point(index, "forward")
             if self.overlap is not None:
                 # the last backward reduce-scatters each finished bucket while it runs
                 self.overlap.arm(index == last)
             loss.backward()
+            self._debug_point(index, "backward")
             if self.audit is not None:
                 self.audit.backward(len(self.audit.events))
             self.loss_acc += loss.detach()
         if self.world > 1:
             dist.all_reduce(self.loss_acc, op=dist.ReduceOp.SUM, group=self.group)
         return self.loss_acc
+
+    def _debug_point(self, index: int, phase: str) -> None:
+        """With PRISM_DEBUG_SYNC=1: synchronise, check the kernels' status word and log progress."""
+        if not DEBUG_SYNC or self.device.type != "cuda":
+            return
+        t0 = time.perf_counter()
+        torch.cuda.synchronize(self.device)
+        from ..ops._lib import check_status
+        check_status(self.device)
+        print(f"[debug] step {self.step_index} microbatch {index} {phase} done, waited "
+              f"{time.perf_counter() - t0:.3f}s, allocated {torch.cuda.memory_allocated(self.device) / 2**30:.1f} GiB, "
+              f"reserved {torch.cuda.memory_reserved(self.device) / 2**30:.1f} GiB", file=sys.stderr, flush=True)
 
     def train_step(self, batch: GlobalBatch, plan: Plan, inputs: list | None = None,
                    read_loss: bool = True) -> StepResult:
