@@ -155,7 +155,14 @@ struct PrepTcParams {
   int* status;
 };
 
-__host__ __device__ constexpr int prep_tc_smem(int DV) { return (6 + DV / 64) * BLK + C * LP * 4 + 2 * C * 4 + 64 + 1024; }
+// The kernel allocates all 512 TMEM columns; its shared-memory request is raised so that two CTAs
+// never share an SM (a second CTA would sit in tcgen05.alloc until the first one exits).
+constexpr int kOneCtaPerSmSmem = 120 * 1024;
+__host__ __device__ constexpr int prep_tc_smem(int DV) {
+  return (6 + DV / 64) * BLK + C * LP * 4 + 2 * C * 4 + 64 + 1024 > kOneCtaPerSmSmem
+             ? (6 + DV / 64) * BLK + C * LP * 4 + 2 * C * 4 + 64 + 1024
+             : kOneCtaPerSmSmem;
+}
 
 __global__ void __launch_bounds__(TP_THREADS, 1)
     gdn_prep_tc_kernel(const __grid_constant__ CUtensorMap mQ, const __grid_constant__ CUtensorMap mK,

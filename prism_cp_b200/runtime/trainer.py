@@ -29,7 +29,7 @@ from .optimizer import DistributedAdamW, FlatParameters
 from .records import StepRecorder, step_record
 
 
-DEBUG_SYNC = os.environ.get("PRISM_DEBUG_SYNC", "0") == "1"
+DEBUG_SYNC = os.environ.get("PRISM_DEBUG_SYNC", "0") in ("1", "2")
 
 
 def hbm_budget(total_bytes: int) -> int:
