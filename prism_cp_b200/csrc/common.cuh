@@ -140,17 +140,23 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int m, int n, int a_mn_ma
          ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
+// The allocation instructions are .sync.aligned: the whole warp must execute them together.
+// A warp whose lane 0 just ran a single-thread block (barrier init, TMA issue) is not guaranteed
+// to have reconverged, so each helper first reconverges the warp; a diverged alloc could run twice.
 PRISM_DEVICE void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {
+  __syncwarp();
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
                "r"(ncols)
                : "memory");
 }
 
 PRISM_DEVICE void tmem_relinquish() {
+  __syncwarp();
   asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
 }
 
 PRISM_DEVICE void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  __syncwarp();
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 

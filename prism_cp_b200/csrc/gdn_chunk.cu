@@ -1326,7 +1326,7 @@ CUtensorMap map2d(const at::Tensor& t, int64_t rows, int64_t cols, int64_t row_s
   CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, t.data_ptr(), dims, strides, box, estr,
                                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "gdn: cuTensorMapEncodeTiled failed with code ", (int)r);
+  if (r != CUDA_SUCCESS) tma_encode_failed("gdn map", (int)r, t.data_ptr(), 2, dims, strides, box);
   return m;
 }
 

@@ -18,6 +18,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "tma_host.cuh"
 
 namespace prism {
 namespace gemm {
@@ -286,7 +287,7 @@ CUtensorMap make_map(const void* ptr, uint64_t inner, uint64_t outer, uint64_t r
   CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r);
+  if (r != CUDA_SUCCESS) tma_encode_failed("gemm operand map", (int)r, ptr, 2, dims, strides, box);
   return map;
 }
 

@@ -2,11 +2,34 @@
 // cuTensorMapEncodeTiled is resolved through the runtime's driver entry point).
 #pragma once
 
+#include <cstdio>
+#include <stdexcept>
+
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 #include <c10/cuda/CUDAException.h>
 
 namespace prism {
+
+// A failed encode reports every argument with C formatting and throws (pybind turns it into a
+// Python RuntimeError).
+[[noreturn]] inline void tma_encode_failed(const char* who, int code, const void* ptr, int rank,
+                                           const cuuint64_t* dims, const cuuint64_t* strides,
+                                           const cuuint32_t* box) {
+  char msg[512];
+  unsigned long long d[3] = {0, 0, 0}, st[2] = {0, 0};
+  unsigned b[3] = {0, 0, 0};
+  for (int i = 0; i < rank && i < 3; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+  }
+  for (int i = 0; i + 1 < rank && i < 2; ++i) st[i] = strides[i];
+  snprintf(msg, sizeof(msg),
+           "%s: cuTensorMapEncodeTiled failed (code %d): ptr=%p dims=[%llu, %llu, %llu] "
+           "byte strides=[%llu, %llu] box=[%u, %u, %u]",
+           who, code, ptr, d[0], d[1], d[2], st[0], st[1], b[0], b[1], b[2]);
+  throw std::runtime_error(msg);
+}
 
 inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -35,7 +58,7 @@ inline CUtensorMap make_head_map(const at::Tensor& t, uint32_t box_rows) {
   CUresult r = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, t.data_ptr(), dims, strides, box,
                                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  if (r != CUDA_SUCCESS) tma_encode_failed("attention head map", (int)r, t.data_ptr(), 3, dims, strides, box);
   return map;
 }
 

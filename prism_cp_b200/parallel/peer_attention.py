@@ -1,23 +1,26 @@
-"""Zigzag context-parallel attention whose kernels read peer tiles over NVLink.
+"""Zigzag context-parallel attention over a symmetric heap (no ring, no LSE merge).
 
-Instead of rotating K/V around a ring with NCCL and merging partial outputs,
-every rank of the team places the tensors a kernel needs in a symmetric heap
-(``symm.SymmetricHeap``) and the tcgen05 attention kernels load each tile from
-the rank that owns it (``csrc/attention_peer.cuh``):
+Every rank of the team stages the tensors the attention kernels need in a
+symmetric heap (``symm.SymmetricHeap``); after a bounded ready signal each rank
+pulls the team's slabs into local memory with one P2P gather kernel (16-byte
+loads over NVLink, every byte crosses NVLink once), and the tcgen05 attention
+kernels then run over the whole sequence in global positions
+(``csrc/attention_peer.cuh``), reading the slab of the rank that owns each tile:
 
-* forward: this rank's query tiles over the team's keys - K/V tiles are TMA
-  loads from the owner's heap, so the exchange overlaps the tile loop and the
-  output needs no LSE merge;
-* backward: dK/dV for this rank's key tiles iterate over the team's query tiles
-  (Q/dO from the owner, LSE/D rows read over NVLink), dQ for this rank's query
-  tiles iterates over the team's K/V. Both are atomic-free.
+* forward: this rank's query tiles over the team's keys (K/V slabs);
+* backward: dK/dV for this rank's key tiles over the team's query tiles (Q/dO
+  slabs and their LSE / D rows), dQ for this rank's query tiles over the team's
+  K/V. Both are atomic-free and need no partial-result exchange.
 
-Per call the heap region alternates between two halves; a rank overwrites a half
-only after every peer has signalled that it finished reading it (bounded signal
-waits, ``csrc/symm.cu``). Requirements: causal attention, every sequence length a
-multiple of 256 * cp (chunks of whole 128-token tiles); other layouts use the
-NCCL ring (``cp_attention.ZigzagRing``). Same semantics as the reference's CP
-attention (TransformerEngine p2p ring, external to the reference).
+Reading peer tiles straight from the peers' heaps inside the tile loop re-reads
+each remote K/V tile once per query tile over NVLink, which made the kernels
+NVLink-bound; pulling the slabs once keeps NVLink traffic at the all-gather
+volume and the tile loop on HBM. Per call the heap region alternates between two
+halves; a rank overwrites a half only after every peer has signalled that it
+finished reading it (bounded signal waits, ``csrc/symm.cu``). Requirements:
+causal attention, every sequence length a multiple of 256 * cp; other layouts
+use the NCCL ring (``cp_attention.ZigzagRing``). Same semantics as the
+reference's CP attention (TransformerEngine p2p ring, external to the reference).
 """
 
 from __future__ import annotations
@@ -52,6 +55,7 @@ class TeamHeap:
         self.index = ctx.index
         self.seq = 0
         self.half = self.heap.nbytes // 2
+        self._gather_plans: dict = {}
 
     def begin(self, need: int) -> int:
         if need > self.half:
@@ -75,6 +79,34 @@ class TeamHeap:
         code = {torch.bfloat16: 15, torch.float32: 6}[dtype]
         dev = self.heap.device.index
         return [lib().symm_tensor(base + offset, list(shape), code, dev) for base in self.heap.bases]
+
+    def gather(self, offset: int, shape, dtype, rows_per_block: int = 64) -> list[torch.Tensor]:
+        """Copy every team rank's region [offset, offset + size) into one local buffer
+        (one P2P gather launch); returns the per-rank slabs in team order."""
+        n = len(self.ranks)
+        rows = shape[0]
+        row_bytes = 1
+        for x in shape[1:]:
+            row_bytes *= x
+        row_bytes *= torch.tensor([], dtype=dtype).element_size()
+        out = torch.empty((n,) + tuple(shape), dtype=dtype, device=self.heap.device)
+        key = (offset, tuple(shape), dtype, rows_per_block)
+        plan = self._gather_plans.get(key)
+        if plan is None:
+            routes, block_route, block_row0 = [], [], []
+            for r in range(n):
+                routes.append((r, offset, r * rows * row_bytes, rows))
+                for r0 in range(0, rows, rows_per_block):
+                    block_route.append(r)
+                    block_row0.append(r0)
+            dev = self.heap.device
+            plan = (torch.tensor(routes, dtype=torch.int64, device=dev),
+                    torch.tensor(block_route, dtype=torch.int64, device=dev),
+                    torch.tensor(block_row0, dtype=torch.int64, device=dev))
+            self._gather_plans[key] = plan
+        lib().symm_gather_rows(self.heap.bases_dev, plan[0], plan[1], plan[2], rows_per_block, row_bytes, out,
+                               status(self.heap.device))
+        return list(out.unbind(0))
 
 
 def team_heap(ctx, need: int) -> TeamHeap:
@@ -125,12 +157,13 @@ class PeerAttention:
         heap.local(base, (T, Hkv, D), torch.bfloat16).copy_(k)
         heap.local(base + kv_bytes, (T, Hkv, D), torch.bfloat16).copy_(v)
         heap.ready()
+        k_all = heap.gather(base, (T, Hkv, D), torch.bfloat16)
+        v_all = heap.gather(base + kv_bytes, (T, Hkv, D), torch.bfloat16)
+        heap.done()
         out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=q.device)
         lse = torch.empty((Hq, T), dtype=torch.float32, device=q.device)
-        lib().attention_fwd_peer(q.contiguous(), heap.peers(base, (T, Hkv, D), torch.bfloat16),
-                                 heap.peers(base + kv_bytes, (T, Hkv, D), torch.bfloat16), self.tiles, self.seq_n,
-                                 self.seq_row0, out, lse, scale, status(q.device))
-        heap.done()
+        lib().attention_fwd_peer(q.contiguous(), k_all, v_all, self.tiles, self.seq_n, self.seq_row0, out, lse,
+                                 scale, status(q.device))
         return out, lse
 
     # ---------------------------------------------------------------- backward
@@ -157,12 +190,12 @@ class PeerAttention:
         views["lse"].copy_(lse)
         lib().attention_bwd_dsum(out, views["do"], views["dsum"])
         heap.ready()
-        peers = {name: heap.peers(base + offs[name], shape, dt) for name, shape, dt in sizes}
+        slabs = {name: heap.gather(base + offs[name], shape, dt) for name, shape, dt in sizes}
+        heap.done()
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-        lib().attention_bwd_peer(peers["q"], peers["k"], peers["v"], peers["do"], peers["lse"], peers["dsum"],
+        lib().attention_bwd_peer(slabs["q"], slabs["k"], slabs["v"], slabs["do"], slabs["lse"], slabs["dsum"],
                                  self.ctx.index, self.tiles, self.seq_n, self.seq_row0, dq, dk, dv, scale,
                                  status(q.device))
-        heap.done()
         return dq, dk, dv
 
 
