@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--total-tokens", type=int, default=1 << 20)
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--overlap-grad-reduce", action="store_true",
+                    help="reduce-scatter gradient buckets during the last backward (side stream)")
     return ap.parse_args()
 
 
@@ -155,7 +157,7 @@ def main():
 
     model = HybridModel(cfg, dtype=torch.bfloat16, device=device, seed=0)
     teams = Teams(world)
-    trainer = Trainer(model, teams, device)
+    trainer = Trainer(model, teams, device, overlap_grad_reduce=args.overlap_grad_reduce)
     host_inputs = trainer.prepare(batch, plan, pin=True)
     dev_inputs = [h.to(device) for h in host_inputs]
     torch.cuda.synchronize()

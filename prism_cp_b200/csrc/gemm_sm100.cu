@@ -265,6 +265,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // ------------------------------------------------------------------ host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  bind_current_context();
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (fn == nullptr) {
     cudaDriverEntryPointQueryResult q;

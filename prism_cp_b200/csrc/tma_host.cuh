@@ -31,7 +31,20 @@ namespace prism {
   throw std::runtime_error(msg);
 }
 
+// The encoder is a driver entry point: it needs a current context on the calling thread, which a
+// fresh thread (e.g. the autograd engine's) may not have before its first runtime call.
+inline void bind_current_context() {
+  thread_local bool bound = false;
+  if (!bound) {
+    int dev = 0;
+    C10_CUDA_CHECK(cudaGetDevice(&dev));
+    C10_CUDA_CHECK(cudaSetDevice(dev));
+    bound = true;
+  }
+}
+
 inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  bind_current_context();
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (fn == nullptr) {
     cudaDriverEntryPointQueryResult q;
