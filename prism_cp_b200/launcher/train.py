@@ -37,6 +37,7 @@ from ..planner.onedim import from_rank_ids
 from ..runtime import checkpoint
 from ..runtime.batch import fixed_lengths, lognormal_lengths, make_batch, manifest_batch
 from ..runtime.trainer import Trainer
+from ..utils.tracing import ProfileWindow, enable_nvtx, nvtx, nvtx_enabled
 from .args import build_parser, model_config, validate
 
 
@@ -100,10 +101,16 @@ def main(argv=None) -> int:
     start = 1
     if args.load and checkpoint.latest(args.load) is not None:
         start = checkpoint.load(trainer, checkpoint.latest(args.load)) + 1
+    enable_nvtx(args.nvtx_ranges or nvtx_enabled())
+    window = ProfileWindow(args.profile_step_start, args.profile_step_end, args.profile_ranks, rank,
+                           enabled=args.profile and cuda)
     for step in range(start, args.train_iters + 1):
         batch = global_batch(args, world, step, pin=cuda)
         plan = plan_for(args, batch, world, cfg.pattern, step, replays)
-        res = trainer.train_step(batch, plan)
+        window.before(step)
+        with nvtx(f"step {step}"):
+            res = trainer.train_step(batch, plan)
+        window.after(step)
         if rank == 0 and step % args.log_interval == 0:
             print(json.dumps({"step": step, "loss": res.loss, "lr": res.lr, "tokens": res.tokens,
                               "microbatches": res.microbatches}), flush=True)

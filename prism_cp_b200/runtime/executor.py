@@ -16,6 +16,7 @@ import torch
 from ..parallel.layout import LocalLayout
 from ..parallel.transport import move
 from ..planner.joint.ir import Microbatch
+from ..utils.tracing import nvtx
 
 
 class LayoutCache:
@@ -45,9 +46,12 @@ class MicrobatchRun:
 
     def forward_layers(self, model, x, start_ctx=None):
         prev = start_ctx or self.ingress
-        for layer, ctx, mctx in zip(model.layers, self.contexts, self.mlp_contexts):
-            x = move(x, prev, ctx)
-            x = layer(x, ctx, mctx)
+        for i, (layer, ctx, mctx) in enumerate(zip(model.layers, self.contexts, self.mlp_contexts)):
+            if ctx is not prev:
+                with nvtx(f"route cp{getattr(prev, 'cp', '?')}->cp{getattr(ctx, 'cp', '?')}"):
+                    x = move(x, prev, ctx)
+            with nvtx(f"layer {i} {type(layer).__name__} cp{getattr(ctx, 'cp', '?')}"):
+                x = layer(x, ctx, mctx)
             prev = ctx
         return x, prev
 

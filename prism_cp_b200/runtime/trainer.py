@@ -27,6 +27,7 @@ from .batch import GlobalBatch, HostInputs, local_inputs
 from .executor import LayoutCache, MicrobatchRun
 from .optimizer import DistributedAdamW, FlatParameters
 from .records import StepRecorder, step_record
+from ..utils.tracing import nvtx
 
 
 DEBUG_SYNC = os.environ.get("PRISM_DEBUG_SYNC", "0") in ("1", "2")
@@ -90,12 +91,14 @@ class Trainer:
         for index, (mb, host) in enumerate(zip(plan.microbatches, inputs)):
             dev = host.to(self.device) if host.tokens.device != self.device else host
             run = MicrobatchRun(mb, batch_lengths, self.cache)
-            loss, _ = run.forward(self.model, dev.tokens, dev.labels, dev.weights)
+            with nvtx(f"microbatch {index} forward"):
+                loss, _ = run.forward(self.model, dev.tokens, dev.labels, dev.weights)
             self._debug_point(index, "forward")
             if self.overlap is not None:
                 # the last backward reduce-scatters each finished bucket while it runs
                 self.overlap.arm(index == last)
-            loss.backward()
+            with nvtx(f"microbatch {index} backward"):
+                loss.backward()
             self._debug_point(index, "backward")
             if self.audit is not None:
                 self.audit.backward(len(self.audit.events))

@@ -129,6 +129,37 @@ def main():
     for name, t, r in zip("qkvgb", loc, ins):
         assert rel(t.grad, r.grad[rows]) < 1e-1, f"GDN CP gradient d{name} {rel(t.grad, r.grad[rows])}"
 
+    # 4. tensor parallelism over all ranks (TP = world, CP = 1) on the sm_100a kernels vs one GPU
+    from prism_cp_b200.models.config import HybridConfig
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.parallel.tensor import make_tp
+    from prism_cp_b200.planner.fixed import uniform_plan
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.trainer import Trainer
+    cfg = HybridConfig(num_layers=4, hidden_size=512, ffn_hidden_size=1024, vocab_size=4096,
+                       num_attention_heads=8, num_query_groups=4, kv_channels=128,
+                       linear_num_key_heads=4, linear_key_head_dim=128, linear_value_head_dim=256, name="tp-check")
+    batch = make_batch([1024, 512], cfg.vocab_size, seed=3)
+    tpc = make_tp(world)
+    tp_model = HybridModel(cfg, dtype=torch.bfloat16, device=dev, seed=0, tp=tpc)
+    tp_trainer = Trainer(tp_model, Teams(tp=tpc), dev, lr=1e-3)
+    plan1 = uniform_plan(batch.lengths, 1, 1, 2048, cfg.pattern)
+    tp_losses = [tp_trainer.train_step(batch, plan1).loss for _ in range(2)]
+    ref_model = HybridModel(cfg, dtype=torch.bfloat16, device=dev, seed=0)
+
+    class Solo:
+        world, rank, initialized = 1, 0, False
+
+        def team(self, ranks):
+            return None
+
+    ref_trainer = Trainer(ref_model, Solo(), dev, lr=1e-3)
+    ref_losses = [ref_trainer.train_step(batch, plan1).loss for _ in range(2)]
+    torch.cuda.synchronize()
+    check_status(dev)
+    for a_, b_ in zip(tp_losses, ref_losses):
+        assert abs(a_ - b_) <= 2e-2 * abs(b_), f"TP loss {tp_losses} vs single GPU {ref_losses}"
+
     heap.close()
     dist.barrier()
     dist.destroy_process_group()
