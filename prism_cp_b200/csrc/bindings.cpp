@@ -4,6 +4,9 @@
 namespace prism {
 void gemm_sm100(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, bool a_mn, bool b_mn, bool accumulate,
                 const c10::optional<at::Tensor>& row_scale, at::Tensor& status);
+void gemm_allreduce_sm100(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, bool a_mn, bool b_mn,
+                          const at::Tensor& regions, int64_t me, int64_t max_tiles, int64_t ld, int64_t seq,
+                          at::Tensor& status);
 void rownorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& z,
                  at::Tensor& y, at::Tensor& rstd, int64_t heads, int64_t n, double inv_n, double eps);
 c10::optional<at::Tensor> rownorm_bwd(const at::Tensor& dy, const at::Tensor& x, const c10::optional<at::Tensor>& w,
@@ -82,6 +85,7 @@ at::Tensor symm_tensor(int64_t ptr, std::vector<int64_t> sizes, int64_t dtype_co
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "prism_cp_b200 sm_100a kernels";
   m.def("gemm", &prism::gemm_sm100, "tcgen05 GEMM C (+)= rowscale * A B^T");
+  m.def("gemm_allreduce", &prism::gemm_allreduce_sm100, "tcgen05 GEMM fused with an all-reduce over peer memory");
   m.def("rownorm_fwd", &prism::rownorm_fwd);
   m.def("rownorm_bwd", &prism::rownorm_bwd);
   m.def("rope_inplace", &prism::rope_inplace);

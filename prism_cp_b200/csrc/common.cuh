@@ -43,6 +43,41 @@ PRISM_DEVICE void record_error(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }
 
+// ---------------------------------------------------------------- peer flags
+// 64-bit sequence words in (possibly peer) global memory: writers publish with a
+// system-scope release store, readers poll with system-scope acquire loads.
+PRISM_DEVICE uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+PRISM_DEVICE void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Spin until *flag >= target. Gives up after kWaitLimitNs (records kTimeoutPeer,
+// raises `abort`) or as soon as a sibling warp raised `abort`.
+PRISM_DEVICE bool wait_flag_bounded(const uint64_t* flag, uint64_t target, volatile int* abort, int* status) {
+  if (ld_acquire_sys(flag) >= target) return true;
+  const uint64_t t0 = globaltimer();
+  while (ld_acquire_sys(flag) < target) {
+    if (abort != nullptr && *abort) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      record_error(status, kTimeoutPeer);
+      if (abort != nullptr) *abort = 1;
+      return false;
+    }
+    __nanosleep(128);
+  }
+  return true;
+}
+
+// Named barrier over `count` threads (a multiple of 32) with id `id` (1..15).
+PRISM_DEVICE void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 PRISM_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

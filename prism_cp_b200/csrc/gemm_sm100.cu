@@ -12,6 +12,22 @@
 // and input-gradient GEMMs of a linear layer run without any transpose.
 // Every mbarrier wait is bounded; a timeout writes an error code to `status`
 // and all roles leave their loops, release TMEM and return.
+//
+// AR = true turns the same kernel into the tensor-parallel GEMM -> all-reduce
+// over NVLink peer memory (a row-parallel linear's output, a column-parallel
+// linear's input gradient). Each of the t ranks computes its partial product
+// of every tile; the tile rows are cut into t contiguous owner blocks. A rank
+// visits the other owners' tiles first and its own last. For another owner's
+// tile the epilogue stores the bf16 partial straight into that owner's staging
+// slot (plain stores over NVLink) and publishes a per-tile sequence flag; for
+// its own tile it waits (bounded) for the t-1 peer flags, adds the staged
+// partials to its fp32 accumulator, writes the bf16 sum to its output and to
+// every peer's output region, and publishes a per-tile result flag. After its
+// tile loop each CTA copies the finished peer-owned tiles from the local output
+// region into the output. The reduce-scatter half of the exchange thereby runs
+// under the MMA of the following tiles; NVLink carries the same bytes as a
+// reduce-scatter + all-gather. The launch is cooperative (every CTA resident),
+// so a CTA never waits on a CTA of its own grid that could not be scheduled.
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -46,6 +62,23 @@ struct Params {
   int tiles_m, tiles_n;
 };
 
+constexpr int kMaxTp = 8;
+
+// Peer memory of one fused GEMM -> all-reduce call. Regions of rank i:
+//   staging[i]   [t][R*BM][ld] bf16   slot s: partials of rank s for rank i's rows
+//   outbuf[i]    [M][ld] bf16         sums of the tiles other ranks own
+//   part_flag[i] [t][max_tiles] u64   slot s, tile u: rank s staged its partial
+//   res_flag[i]  [max_tiles] u64      tile u: its owner wrote the sum here
+struct ArParams {
+  int t, me, R, max_tiles;
+  long ld;
+  unsigned long long seq;
+  __nv_bfloat16* staging[kMaxTp];
+  __nv_bfloat16* outbuf[kMaxTp];
+  uint64_t* part_flag[kMaxTp];
+  uint64_t* res_flag[kMaxTp];
+};
+
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
   // Grouped raster: GROUP_M m-blocks share a sweep over n so that concurrently
   // running CTAs reuse both A and B tiles from L2.
@@ -58,9 +91,152 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   tn = r / rows;
 }
 
-template <int A_MN, int B_MN>
+__device__ __forceinline__ int ar_owner(const ArParams& ar, int tm) { return min(tm / ar.R, ar.t - 1); }
+
+// Tile visiting order: plain grouped raster, or (AR) the owner blocks of ranks
+// me+1, me+2, ..., me, each in grouped raster.
+template <bool AR>
+__device__ __forceinline__ void map_tile(int t, const Params& p, const ArParams& ar, int& tm, int& tn) {
+  if constexpr (!AR) {
+    tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+  } else {
+    for (int g = 0; g < ar.t; ++g) {
+      const int o = (ar.me + 1 + g) % ar.t;
+      const int m_lo = o * ar.R;
+      const int rows = max(0, min(m_lo + ar.R, p.tiles_m) - m_lo);
+      const int n = rows * p.tiles_n;
+      if (t < n) {
+        tile_coords(t, rows, p.tiles_n, tm, tn);
+        tm += m_lo;
+        return;
+      }
+      t -= n;
+    }
+    tm = tn = 0;
+  }
+}
+
+// ------------------------------------------------------------------ all-reduce epilogue
+__device__ __forceinline__ void store_bf16_run(__nv_bfloat16* dst, const float* f, int ncol) {
+  if (ncol == 32) {
+#pragma unroll
+    for (int v = 0; v < 4; ++v)
+      reinterpret_cast<uint4*>(dst)[v] = make_uint4(pack_bf16x2(f[8 * v], f[8 * v + 1]), pack_bf16x2(f[8 * v + 2], f[8 * v + 3]),
+                                                    pack_bf16x2(f[8 * v + 4], f[8 * v + 5]),
+                                                    pack_bf16x2(f[8 * v + 6], f[8 * v + 7]));
+  } else {
+    for (int c = 0; c < ncol; ++c) dst[c] = __float2bfloat16(f[c]);
+  }
+}
+
+__device__ __forceinline__ void add_bf16_run(float* f, const __nv_bfloat16* src, int ncol) {
+  if (ncol == 32) {
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const uint4 raw = reinterpret_cast<const uint4*>(src)[v];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 x = __bfloat1622float2(h[e]);
+        f[8 * v + 2 * e] += x.x;
+        f[8 * v + 2 * e + 1] += x.y;
+      }
+    }
+  } else {
+    for (int c = 0; c < ncol; ++c) f[c] += __bfloat162float(src[c]);
+  }
+}
+
+// One tile of the fused all-reduce, run by the 128 epilogue threads (thread =
+// tile row). Returns false (jointly) when a peer wait gave up.
+__device__ __forceinline__ bool ar_epilogue_tile(const Params& p, const ArParams& ar, uint32_t taddr, int tm, int tn,
+                                                 int row, volatile int* abort_flag) {
+  const int owner = ar_owner(ar, tm);
+  const bool mine = owner == ar.me;
+  const int tile_id = tm * p.tiles_n + tn;
+  const long own_row0 = (long)owner * ar.R * BM;
+  bool ok = true;
+  if (mine) {
+    bool w = true;
+    for (int s = 0; s < ar.t; ++s)
+      if (s != ar.me)
+        w = w && wait_flag_bounded(ar.part_flag[ar.me] + (long)s * ar.max_tiles + tile_id, ar.seq, abort_flag, p.status);
+    ok = named_barrier_and(w, 1, 128);
+  }
+  if (ok) {
+    __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C);
+#pragma unroll 1
+    for (int j = 0; j < BN / 32; ++j) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + j * 32, r);
+      tmem_wait_ld();
+      const int col0 = tn * BN + j * 32;
+      if (row >= p.M || col0 >= p.N) continue;
+      const int ncol = min(32, p.N - col0);
+      float f[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(r[e]);
+      if (!mine) {
+        store_bf16_run(ar.staging[owner] + ((long)ar.me * ar.R * BM + (row - own_row0)) * ar.ld + col0, f, ncol);
+      } else {
+        for (int s = 0; s < ar.t; ++s)
+          if (s != ar.me)
+            add_bf16_run(f, ar.staging[ar.me] + ((long)s * ar.R * BM + (row - own_row0)) * ar.ld + col0, ncol);
+        store_bf16_run(C + (long)row * p.ldc + col0, f, ncol);
+        for (int q = 0; q < ar.t; ++q)
+          if (q != ar.me) store_bf16_run(ar.outbuf[q] + (long)row * ar.ld + col0, f, ncol);
+      }
+    }
+  }
+  // every thread's peer stores are ordered before the flag that publishes them
+  __threadfence_system();
+  ok = named_barrier_and(ok, 1, 128);
+  if (ok && threadIdx.x == 64) {
+    if (!mine) {
+      st_release_sys(ar.part_flag[owner] + (long)ar.me * ar.max_tiles + tile_id, ar.seq);
+    } else {
+      for (int q = 0; q < ar.t; ++q)
+        if (q != ar.me) st_release_sys(ar.res_flag[q] + tile_id, ar.seq);
+    }
+  }
+  return ok;
+}
+
+// After the tile loop: copy the peer-owned tiles of this CTA's share (tile u =
+// blockIdx.x + k * gridDim.x) from the local output region into C once their
+// owners published them. Warp `quarter` copies rows 32*quarter..+31, one row
+// per step, 16 bytes per lane.
+__device__ __forceinline__ void ar_gather_tail(const Params& p, const ArParams& ar, int quarter, int lane,
+                                               volatile int* abort_flag) {
+  __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C);
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  bool ok = named_barrier_and(*abort_flag == 0, 1, 128);
+  for (int u = blockIdx.x; ok && u < num_tiles; u += gridDim.x) {
+    const int tm = u / p.tiles_n, tn = u % p.tiles_n;
+    if (ar_owner(ar, tm) == ar.me) continue;
+    ok = named_barrier_and(wait_flag_bounded(ar.res_flag[ar.me] + u, ar.seq, abort_flag, p.status), 1, 128);
+    if (!ok) break;
+    const int ncols = min(BN, p.N - tn * BN);
+    for (int rr = 0; rr < 32; ++rr) {
+      const int row = tm * BM + quarter * 32 + rr;
+      if (row >= p.M) break;
+      const __nv_bfloat16* src = ar.outbuf[ar.me] + (long)row * ar.ld + tn * BN;
+      __nv_bfloat16* dst = C + (long)row * p.ldc + tn * BN;
+      for (int c = lane * 8; c < ncols; c += 256) {
+        if (c + 8 <= ncols) {
+          *reinterpret_cast<uint4*>(dst + c) = *reinterpret_cast<const uint4*>(src + c);
+        } else {
+          for (int e = c; e < ncols; ++e) dst[e] = src[e];
+        }
+      }
+    }
+  }
+}
+
+template <int A_MN, int B_MN, bool AR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p,
+                const __grid_constant__ ArParams ar) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
@@ -109,7 +285,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int tm, tn;
-        tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+        map_tile<AR>(t, p, ar, tm, tn);
         const int m0 = tm * BM, n0 = tn * BN;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % STAGES;
@@ -184,13 +360,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t tph = (local >> 1) & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&tfull[buf], tph, abort_flag, p.status, kTimeoutEpilogue))) break;
+      const bool got = mbar_wait_bounded(&tfull[buf], tph, abort_flag, p.status, kTimeoutEpilogue);
+      // AR: every exit decision is taken jointly by the four epilogue warps, which share named barriers
+      if (AR ? !named_barrier_and(got, 1, 128) : !__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       int tm, tn;
-      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      map_tile<AR>(t, p, ar, tm, tn);
       const int row = tm * BM + row_in_tile;
-      const float scale = (p.row_scale != nullptr && row < p.M) ? p.row_scale[row] : 1.0f;
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
+      if constexpr (AR) {
+        if (!ar_epilogue_tile(p, ar, taddr, tm, tn, row, abort_flag)) {
+          tc_fence_before();
+          mbar_arrive(&tempty[buf]);
+          break;
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[buf]);
+        continue;
+      }
+      const float scale = (p.row_scale != nullptr && row < p.M) ? p.row_scale[row] : 1.0f;
 #pragma unroll 1
       for (int j = 0; j < BN / 32; ++j) {
         uint32_t r[32];
@@ -253,6 +441,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(&tempty[buf]);
     }
+    if constexpr (AR) ar_gather_tail(p, ar, quarter, lane, abort_flag);
   }
 
   tc_fence_before();
@@ -302,17 +491,32 @@ int num_sms() {
   return n;
 }
 
-template <int A_MN, int B_MN>
-void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t stream) {
+template <int A_MN, int B_MN, bool AR>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, const ArParams& ar, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
     C10_CUDA_CHECK(
-        cudaFuncSetAttribute(gemm_kernel<A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        cudaFuncSetAttribute(gemm_kernel<A_MN, B_MN, AR>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     configured = true;
   }
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, num_sms());
-  gemm_kernel<A_MN, B_MN><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, p);
+  if constexpr (!AR) {
+    gemm_kernel<A_MN, B_MN, AR><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, p, ar);
+  } else {
+    // cooperative: all CTAs are resident before any of them waits on a peer
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_kernel<A_MN, B_MN, AR>, ta, tb, p, ar));
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -361,10 +565,86 @@ void gemm_sm100(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, bool a_
   p.tiles_m = (int)((M + BM - 1) / BM);
   p.tiles_n = (int)((N + BN - 1) / BN);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  if (!a_mn && !b_mn) launch<0, 0>(ta, tb, p, stream);
-  else if (!a_mn && b_mn) launch<0, 1>(ta, tb, p, stream);
-  else if (a_mn && !b_mn) launch<1, 0>(ta, tb, p, stream);
-  else launch<1, 1>(ta, tb, p, stream);
+  const ArParams none{};
+  if (!a_mn && !b_mn) launch<0, 0, false>(ta, tb, p, none, stream);
+  else if (!a_mn && b_mn) launch<0, 1, false>(ta, tb, p, none, stream);
+  else if (a_mn && !b_mn) launch<1, 0, false>(ta, tb, p, none, stream);
+  else launch<1, 1, false>(ta, tb, p, none, stream);
+}
+
+// Tensor-parallel GEMM -> all-reduce over peer memory: c = sum over the t ranks
+// of a_r b_r^T (bf16 out). regions: int64 CPU tensor [4, t] with every rank's
+// staging, output-region, partial-flag and result-flag base addresses (device
+// pointers valid in this process, peers' mapped through CUDA IPC); max_tiles
+// is the flag capacity per slot, ld the row stride of the staging and output
+// regions (>= N, multiple of 8), seq this call's sequence number (greater than
+// every earlier call's on the same regions).
+void gemm_allreduce_sm100(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, bool a_mn, bool b_mn,
+                          const at::Tensor& regions, int64_t me, int64_t max_tiles, int64_t ld, int64_t seq,
+                          at::Tensor& status) {
+  using namespace gemm;
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm_allreduce: CUDA tensors required");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 && c.scalar_type() == at::kBFloat16,
+              "gemm_allreduce: bf16 operands and output");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm_allreduce: 2-D tensors");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1, "gemm_allreduce: unit inner stride");
+  TORCH_CHECK(regions.device().is_cpu() && regions.scalar_type() == at::kLong && regions.dim() == 2 &&
+                  regions.size(0) == 4 && regions.size(1) >= 2 && regions.size(1) <= kMaxTp,
+              "gemm_allreduce: regions must be a CPU int64 [4, t] table, 2 <= t <= 8");
+  const int64_t M = a_mn ? a.size(1) : a.size(0);
+  const int64_t K = a_mn ? a.size(0) : a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  const int64_t Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "gemm_allreduce: K mismatch ", K, " vs ", Kb);
+  TORCH_CHECK(c.size(0) == M && c.size(1) == N, "gemm_allreduce: output shape mismatch");
+  TORCH_CHECK(N % 8 == 0 && c.stride(0) % 8 == 0 && ld % 8 == 0 && ld >= N, "gemm_allreduce: 16-byte rows required");
+  TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0, "gemm_allreduce: row strides must be multiples of 8");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(a.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(b.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(c.data_ptr()) & 15) == 0,
+              "gemm_allreduce: 16-byte aligned tensors required");
+  TORCH_CHECK(M > 0 && N > 0 && K > 0, "gemm_allreduce: empty problem");
+  const int t = (int)regions.size(1);
+  TORCH_CHECK(me >= 0 && me < t, "gemm_allreduce: rank out of range");
+  const c10::cuda::CUDAGuard guard(a.device());
+  CUtensorMap ta = a_mn ? make_map(a.data_ptr(), M, K, a.stride(0), 64, 64)
+                        : make_map(a.data_ptr(), K, M, a.stride(0), 64, BM);
+  CUtensorMap tb = b_mn ? make_map(b.data_ptr(), N, K, b.stride(0), 64, 64)
+                        : make_map(b.data_ptr(), K, N, b.stride(0), 64, BN);
+  Params p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.C = c.data_ptr();
+  p.ldc = c.stride(0);
+  p.c_fp32 = 0;
+  p.accumulate = 0;
+  p.row_scale = nullptr;
+  p.status = status.data_ptr<int>();
+  p.tiles_m = (int)((M + BM - 1) / BM);
+  p.tiles_n = (int)((N + BN - 1) / BN);
+  TORCH_CHECK((int64_t)p.tiles_m * p.tiles_n <= max_tiles, "gemm_allreduce: more tiles than flag slots");
+  ArParams ar{};
+  ar.t = t;
+  ar.me = (int)me;
+  ar.R = (p.tiles_m + t - 1) / t;
+  ar.max_tiles = (int)max_tiles;
+  ar.ld = ld;
+  ar.seq = (unsigned long long)seq;
+  const int64_t* reg = regions.data_ptr<int64_t>();
+  for (int i = 0; i < t; ++i) {
+    ar.staging[i] = reinterpret_cast<__nv_bfloat16*>(reg[0 * t + i]);
+    ar.outbuf[i] = reinterpret_cast<__nv_bfloat16*>(reg[1 * t + i]);
+    ar.part_flag[i] = reinterpret_cast<uint64_t*>(reg[2 * t + i]);
+    ar.res_flag[i] = reinterpret_cast<uint64_t*>(reg[3 * t + i]);
+    TORCH_CHECK((reg[0 * t + i] & 15) == 0 && (reg[1 * t + i] & 15) == 0 && (reg[2 * t + i] & 7) == 0 &&
+                    (reg[3 * t + i] & 7) == 0,
+                "gemm_allreduce: misaligned region");
+  }
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (!a_mn && !b_mn) launch<0, 0, true>(ta, tb, p, ar, stream);
+  else if (!a_mn && b_mn) launch<0, 1, true>(ta, tb, p, ar, stream);
+  else TORCH_CHECK(false, "gemm_allreduce: the A operand must be K-major");
 }
 
 }  // namespace prism

@@ -24,16 +24,6 @@ namespace symm {
 
 constexpr uint64_t kPeerWaitNs = 2000000000ull;  // 2 s
 
-__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
 // Spin until *flag >= target; false (and an error code) after kPeerWaitNs.
 __device__ __forceinline__ bool wait_flag(const uint64_t* flag, uint64_t target, int* status) {
   if (ld_acquire_sys(flag) >= target) return true;

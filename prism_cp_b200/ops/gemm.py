@@ -44,6 +44,20 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool =
     return out
 
 
+def weight_grad(dy2: torch.Tensor, x2: torch.Tensor, weight: torch.Tensor):
+    """dW = dy^T x: accumulated in fp32 into ``weight.main_grad`` when it exists (returns None), else returned."""
+    main = getattr(weight, "main_grad", None)
+    if main is not None and x2.is_cuda:
+        matmul(dy2, x2, a_mn=True, b_mn=True, out=main, accumulate=True)
+        on_main_grad(weight)
+        return None
+    if main is not None:
+        main.add_(_torch_mm(dy2, x2, True, True).to(main.dtype))
+        on_main_grad(weight)
+        return None
+    return matmul(dy2, x2, a_mn=True, b_mn=True, out_dtype=weight.dtype)
+
+
 class _Linear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight):
@@ -62,18 +76,7 @@ class _Linear(torch.autograd.Function):
         if dy2.stride(-1) != 1:
             dy2 = dy2.contiguous()
         dx = matmul(dy2, weight, b_mn=True).reshape(shape) if ctx.needs_input_grad[0] else None
-        dw = None
-        if ctx.needs_input_grad[1]:
-            main = getattr(weight, "main_grad", None)
-            if main is not None and x2.is_cuda:
-                matmul(dy2, x2, a_mn=True, b_mn=True, out=main, accumulate=True)
-                dw = None
-                on_main_grad(weight)
-            elif main is not None:
-                main.add_(_torch_mm(dy2, x2, True, True).to(main.dtype))
-                on_main_grad(weight)
-            else:
-                dw = matmul(dy2, x2, a_mn=True, b_mn=True, out_dtype=weight.dtype)
+        dw = weight_grad(dy2, x2, weight) if ctx.needs_input_grad[1] else None
         return dx, dw
 
 

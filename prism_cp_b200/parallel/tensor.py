@@ -13,9 +13,10 @@ group; attention/GDN heads and the MLP's hidden units are split:
 * ``row_linear(x_shard, w_shard)``: sharded input, partial outputs summed over
   the group (all-reduce in the forward, identity backward).
 
-The sums run as reduce-scatter + all-gather over NVLink (``dist`` on NCCL, the
-same two collectives a fused GEMM->reduce-scatter / all-gather->GEMM pair
-replaces). Parameters owned by a shard reduce their gradients only over the
+On CUDA both sums are fused into the GEMM that produces them
+(``tp_fused.FusedAllReduceGemm``: the tcgen05 kernel exchanges partial tiles and
+finished tiles over NVLink peer memory while it computes). Elsewhere (CPU,
+gloo, odd widths) they run as reduce-scatter + all-gather (``dist``). Parameters owned by a shard reduce their gradients only over the
 ranks of the same TP index; replicated parameters (norms, embedding, head,
 per-value-dim norm weights) reduce over the whole world.
 """
@@ -27,7 +28,9 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
-from ..ops.gemm import linear
+from ..ops._lib import aligned_rows
+from ..ops.gemm import linear, matmul, weight_grad
+from . import tp_fused
 
 
 @dataclass
@@ -110,13 +113,63 @@ class _ReduceFromTP(torch.autograd.Function):
         return g, None
 
 
+class _ColumnLinearFused(torch.autograd.Function):
+    """y = x W_shard^T with replicated x; dx = sum over the group of dy_shard W_shard (fused GEMM + all-reduce)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, group):
+        ctx.save_for_backward(x, weight)
+        ctx.group = group
+        x2 = x.reshape(-1, x.shape[-1])
+        return matmul(x2, weight).reshape(*x.shape[:-1], weight.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight = ctx.saved_tensors
+        x2 = x.reshape(-1, x.shape[-1])
+        dy2 = aligned_rows(dy.reshape(-1, dy.shape[-1]))
+        dx = None
+        if ctx.needs_input_grad[0]:
+            if tp_fused.usable(dy2, weight.shape[1], ctx.group):
+                dx = tp_fused.fused_for(ctx.group, dy2.device)(dy2, aligned_rows(weight), b_mn=True)
+            else:
+                dx = _sum_over_group(matmul(dy2, weight, b_mn=True), ctx.group)
+            dx = dx.reshape(x.shape)
+        dw = weight_grad(dy2, x2, weight) if ctx.needs_input_grad[1] else None
+        return dx, dw, None
+
+
+class _RowLinearFused(torch.autograd.Function):
+    """y = sum over the group of x_shard W_shard^T (fused GEMM + all-reduce); dx = dy W_shard locally."""
+
+    @staticmethod
+    def forward(ctx, x, weight, group):
+        ctx.save_for_backward(x, weight)
+        x2 = aligned_rows(x.reshape(-1, x.shape[-1]))
+        y = tp_fused.fused_for(group, x2.device)(x2, aligned_rows(weight))
+        return y.reshape(*x.shape[:-1], weight.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight = ctx.saved_tensors
+        x2 = x.reshape(-1, x.shape[-1])
+        dy2 = aligned_rows(dy.reshape(-1, dy.shape[-1]))
+        dx = matmul(dy2, weight, b_mn=True).reshape(x.shape) if ctx.needs_input_grad[0] else None
+        dw = weight_grad(dy2, x2, weight) if ctx.needs_input_grad[1] else None
+        return dx, dw, None
+
+
 def column_linear(x: torch.Tensor, weight: torch.Tensor, tp: TPContext | None) -> torch.Tensor:
     if tp is not None and tp.enabled:
+        if tp_fused.usable(x, weight.shape[1], tp.group):
+            return _ColumnLinearFused.apply(x, weight, tp.group)
         x = _CopyToTP.apply(x, tp.group)
     return linear(x, weight)
 
 
 def row_linear(x: torch.Tensor, weight: torch.Tensor, tp: TPContext | None) -> torch.Tensor:
+    if tp is not None and tp.enabled and tp_fused.usable(x, weight.shape[0], tp.group):
+        return _RowLinearFused.apply(x, weight, tp.group)
     y = linear(x, weight)
     if tp is not None and tp.enabled:
         y = _ReduceFromTP.apply(y, tp.group)

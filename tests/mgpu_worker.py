@@ -160,6 +160,26 @@ def main():
     for a_, b_ in zip(tp_losses, ref_losses):
         assert abs(a_ - b_) <= 2e-2 * abs(b_), f"TP loss {tp_losses} vs single GPU {ref_losses}"
 
+    # 5. fused tensor-parallel GEMM + all-reduce over peer memory vs GEMM + NCCL all-reduce (fp32 oracle)
+    from prism_cp_b200.parallel.tp_fused import FusedAllReduceGemm
+    fused = FusedAllReduceGemm(dist.group.WORLD, dev)
+    gen = torch.Generator(device=dev).manual_seed(100 + rank)
+    for (M, N, K, b_mn) in [(1000, 2048, 512, False), (4096, 1024, 768, True), (384, 520, 64, False),
+                            (8192, 2048, 1024, False), (1000, 2048, 512, False)]:
+        a = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+        b = torch.randn(K, N, device=dev, generator=gen).to(torch.bfloat16) if b_mn else \
+            torch.randn(N, K, device=dev, generator=gen).to(torch.bfloat16)
+        got = fused(a, b, b_mn=b_mn)
+        want = a.float() @ (b.float() if b_mn else b.float().t())
+        dist.all_reduce(want)
+        torch.cuda.synchronize()
+        check_status(dev)
+        assert rel(got, want) < 1e-2, f"fused GEMM+all-reduce {M}x{N}x{K} b_mn={b_mn}: {rel(got, want)}"
+        same = got.clone()
+        dist.broadcast(same, 0)
+        assert torch.equal(same, got), f"fused GEMM+all-reduce results differ between ranks ({M}x{N}x{K})"
+    fused.close()
+
     heap.close()
     dist.barrier()
     dist.destroy_process_group()
