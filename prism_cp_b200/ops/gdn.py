@@ -27,6 +27,7 @@ from __future__ import annotations
 import torch
 
 from ._lib import is_cuda, lib, status
+from ..utils import watchdog
 
 CHUNK = 64
 
@@ -269,8 +270,10 @@ class _FusedChunkRule(torch.autograd.Function):
         o = torch.empty_like(vb)
         S_final = torch.empty((len(layout.lengths), H, qb.shape[-1], DV), dtype=torch.float32, device=q.device)
         s0 = S0.float().contiguous() if S0 is not None else None
+        watchdog.beat("gdn forward prep")
         L.gdn_chunk_fwd(Wn, U, Kd, Qg, Aqk, gam, layout.tok0_dev, layout.len_dev, layout.seq_chunks_dev, s0, o,
                         S_final, None, None, st)
+        watchdog.beat("gdn forward state pass")
         ctx.save_for_backward(qb, kb, vb, gf, bt, s0)
         ctx.layout, ctx.scale, ctx.has_s0 = layout, scale, S0 is not None
         ctx.dtypes = (q.dtype, k.dtype, v.dtype, g.dtype, beta.dtype)
@@ -293,9 +296,11 @@ class _FusedChunkRule(torch.autograd.Function):
         main = torch.cuda.current_stream(qb.device)
         side = _side_stream(qb.device)
         side.wait_stream(main)
+        watchdog.beat("gdn backward prep")
         with torch.cuda.stream(side):
             L.gdn_chunk_fwd(Wn, U, Kd, Qg, Aqk, gam, lay.tok0_dev, lay.len_dev, lay.seq_chunks_dev, s0, None, None,
                             states, rows, st)
+            watchdog.beat("gdn backward state recompute (side stream)")
         for t in (Wn, U, Kd, Qg, Aqk, gam, states, rows) + ((s0,) if s0 is not None else ()):
             t.record_stream(side)
         dstates, drows = torch.empty_like(states), torch.empty_like(rows)
@@ -306,6 +311,7 @@ class _FusedChunkRule(torch.autograd.Function):
         dsf = dS_final.float().contiguous() if dS_final is not None else None
         L.gdn_chunk_bwd_state(Wn, Kd, Qg, Aqk, gam, dob, lay.tok0_dev, lay.len_dev, lay.seq_chunks_dev, dsf, dS0,
                               dstates, drows, st)
+        watchdog.beat("gdn backward reverse state pass")
         main.wait_stream(side)
         dq, dk, dv, dg, dbeta = L.gdn_chunk_bwd_local(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, Gc, aux, states,
                                                       dstates, rows, drows, dob, ctx.scale, st)

@@ -16,6 +16,7 @@ import torch
 from ..parallel.layout import LocalLayout
 from ..parallel.transport import move
 from ..planner.joint.ir import Microbatch
+from ..utils import watchdog
 from ..utils.tracing import nvtx
 
 
@@ -50,8 +51,11 @@ class MicrobatchRun:
             if ctx is not prev:
                 with nvtx(f"route cp{getattr(prev, 'cp', '?')}->cp{getattr(ctx, 'cp', '?')}"):
                     x = move(x, prev, ctx)
+            if watchdog._ACTIVE is not None and x.requires_grad:
+                x.register_hook(lambda g, i=i: watchdog.beat(f"layer {i} backward done"))
             with nvtx(f"layer {i} {type(layer).__name__} cp{getattr(ctx, 'cp', '?')}"):
                 x = layer(x, ctx, mctx)
+            watchdog.beat(f"layer {i} forward done")
             prev = ctx
         return x, prev
 

@@ -27,6 +27,7 @@ from .batch import GlobalBatch, HostInputs, local_inputs
 from .executor import LayoutCache, MicrobatchRun
 from .optimizer import DistributedAdamW, FlatParameters
 from .records import StepRecorder, step_record
+from ..utils import watchdog
 from ..utils.tracing import nvtx
 
 
@@ -78,6 +79,7 @@ class Trainer:
         self.numerics = numerics
         self.audit = AccumulationAudit() if audit else None
         self.step_index = 0
+        self.watchdog = watchdog.from_env()
 
     # ------------------------------------------------------------------ inputs
     def prepare(self, batch: GlobalBatch, plan: Plan, pin: bool = True) -> list[HostInputs]:
@@ -91,12 +93,14 @@ class Trainer:
         for index, (mb, host) in enumerate(zip(plan.microbatches, inputs)):
             dev = host.to(self.device) if host.tokens.device != self.device else host
             run = MicrobatchRun(mb, batch_lengths, self.cache)
+            watchdog.beat(f"step {self.step_index + 1} microbatch {index} forward")
             with nvtx(f"microbatch {index} forward"):
                 loss, _ = run.forward(self.model, dev.tokens, dev.labels, dev.weights)
             self._debug_point(index, "forward")
             if self.overlap is not None:
                 # the last backward reduce-scatters each finished bucket while it runs
                 self.overlap.arm(index == last)
+            watchdog.beat(f"step {self.step_index + 1} microbatch {index} backward")
             with nvtx(f"microbatch {index} backward"):
                 loss.backward()
             self._debug_point(index, "backward")
@@ -128,8 +132,10 @@ class Trainer:
             return self._tracked_step(batch, plan, inputs)
         self.flat.zero_grad()
         loss = self.forward_backward(batch.lengths, plan, inputs)
+        watchdog.beat(f"step {self.step_index + 1} optimizer")
         lr = self.optimizer.step()
         self.step_index += 1
+        watchdog.beat(f"step {self.step_index} done")
         value = float(loss.item()) if read_loss else float("nan")
         if read_loss and not math.isfinite(value):
             raise FloatingPointError("non-finite loss in training step")

@@ -48,3 +48,19 @@ def test_launcher_accepts_profile_flags(tmp_path):
                      "--profile", "--profile-step-start", "1", "--profile-step-end", "2", "--nvtx-ranges"])
     tracing.enable_nvtx(False)
     assert rc == 0
+
+
+def test_watchdog_reports_a_stall(capsys):
+    import io
+    import time
+    from prism_cp_b200.utils.watchdog import StallWatchdog
+    buf = io.StringIO()
+    wd = StallWatchdog(1.0, stream=buf)
+    try:
+        wd.beat("layer 0 forward done")
+        time.sleep(2.6)
+        assert "no progress" in buf.getvalue() and "layer 0 forward done" in buf.getvalue()
+        wd.beat("layer 1 forward done")
+        assert not wd.reported
+    finally:
+        wd.close()
