@@ -82,40 +82,42 @@ void symm_gather_rows(const at::Tensor& peer_bases, const at::Tensor& routes, co
 at::Tensor symm_tensor(int64_t ptr, std::vector<int64_t> sizes, int64_t dtype_code, int64_t device);
 }  // namespace prism
 
+// Every op releases the GIL while it runs: launches never call back into Python, and a
+// host call that blocks (an allocation that synchronises) must not stall other Python threads.
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "prism_cp_b200 sm_100a kernels";
-  m.def("gemm", &prism::gemm_sm100, "tcgen05 GEMM C (+)= rowscale * A B^T");
-  m.def("gemm_allreduce", &prism::gemm_allreduce_sm100, "tcgen05 GEMM fused with an all-reduce over peer memory");
-  m.def("rownorm_fwd", &prism::rownorm_fwd);
-  m.def("rownorm_bwd", &prism::rownorm_bwd);
-  m.def("rope_inplace", &prism::rope_inplace);
-  m.def("conv1d_silu_fwd", &prism::conv1d_silu_fwd);
-  m.def("conv1d_silu_bwd", &prism::conv1d_silu_bwd);
-  m.def("swiglu_fwd", &prism::swiglu_fwd);
-  m.def("swiglu_bwd", &prism::swiglu_bwd);
-  m.def("ce_fused", &prism::ce_fused);
-  m.def("sumsq_accumulate", &prism::sumsq_accumulate);
-  m.def("adamw_step", &prism::adamw_step);
-  m.def("attention_fwd", &prism::attention_fwd_sm100, "tcgen05 varlen GQA flash attention forward");
-  m.def("attention_bwd", &prism::attention_bwd_sm100, "tcgen05 varlen GQA flash attention backward");
-  m.def("gdn_state_fwd", &prism::gdn_state_fwd);
-  m.def("gdn_state_bwd", &prism::gdn_state_bwd);
-  m.def("gdn_chunk_prep", &prism::gdn_chunk_prep, "GDN chunk prep: WY form, decays, Aqk (CUDA cores)");
-  m.def("gdn_chunk_fwd", &prism::gdn_chunk_fwd, "GDN tcgen05 state pass with the output fused");
-  m.def("gdn_chunk_bwd_state", &prism::gdn_chunk_bwd_state, "GDN tcgen05 reverse state pass");
-  m.def("gdn_chunk_bwd_local", &prism::gdn_chunk_bwd_local, "GDN chunk-local backward (tcgen05 + CUDA cores)");
-  m.def("attention_fwd_peer", &prism::attention_fwd_peer,
+  m.def("gemm", &prism::gemm_sm100, py::call_guard<py::gil_scoped_release>(), "tcgen05 GEMM C (+)= rowscale * A B^T");
+  m.def("gemm_allreduce", &prism::gemm_allreduce_sm100, py::call_guard<py::gil_scoped_release>(), "tcgen05 GEMM fused with an all-reduce over peer memory");
+  m.def("rownorm_fwd", &prism::rownorm_fwd, py::call_guard<py::gil_scoped_release>());
+  m.def("rownorm_bwd", &prism::rownorm_bwd, py::call_guard<py::gil_scoped_release>());
+  m.def("rope_inplace", &prism::rope_inplace, py::call_guard<py::gil_scoped_release>());
+  m.def("conv1d_silu_fwd", &prism::conv1d_silu_fwd, py::call_guard<py::gil_scoped_release>());
+  m.def("conv1d_silu_bwd", &prism::conv1d_silu_bwd, py::call_guard<py::gil_scoped_release>());
+  m.def("swiglu_fwd", &prism::swiglu_fwd, py::call_guard<py::gil_scoped_release>());
+  m.def("swiglu_bwd", &prism::swiglu_bwd, py::call_guard<py::gil_scoped_release>());
+  m.def("ce_fused", &prism::ce_fused, py::call_guard<py::gil_scoped_release>());
+  m.def("sumsq_accumulate", &prism::sumsq_accumulate, py::call_guard<py::gil_scoped_release>());
+  m.def("adamw_step", &prism::adamw_step, py::call_guard<py::gil_scoped_release>());
+  m.def("attention_fwd", &prism::attention_fwd_sm100, py::call_guard<py::gil_scoped_release>(), "tcgen05 varlen GQA flash attention forward");
+  m.def("attention_bwd", &prism::attention_bwd_sm100, py::call_guard<py::gil_scoped_release>(), "tcgen05 varlen GQA flash attention backward");
+  m.def("gdn_state_fwd", &prism::gdn_state_fwd, py::call_guard<py::gil_scoped_release>());
+  m.def("gdn_state_bwd", &prism::gdn_state_bwd, py::call_guard<py::gil_scoped_release>());
+  m.def("gdn_chunk_prep", &prism::gdn_chunk_prep, py::call_guard<py::gil_scoped_release>(), "GDN chunk prep: WY form, decays, Aqk (CUDA cores)");
+  m.def("gdn_chunk_fwd", &prism::gdn_chunk_fwd, py::call_guard<py::gil_scoped_release>(), "GDN tcgen05 state pass with the output fused");
+  m.def("gdn_chunk_bwd_state", &prism::gdn_chunk_bwd_state, py::call_guard<py::gil_scoped_release>(), "GDN tcgen05 reverse state pass");
+  m.def("gdn_chunk_bwd_local", &prism::gdn_chunk_bwd_local, py::call_guard<py::gil_scoped_release>(), "GDN chunk-local backward (tcgen05 + CUDA cores)");
+  m.def("attention_fwd_peer", &prism::attention_fwd_peer, py::call_guard<py::gil_scoped_release>(),
         "context-parallel attention forward reading every KV tile from its owner's symmetric buffer");
-  m.def("attention_bwd_peer", &prism::attention_bwd_peer,
+  m.def("attention_bwd_peer", &prism::attention_bwd_peer, py::call_guard<py::gil_scoped_release>(),
         "context-parallel attention backward reading peer Q/dO/K/V tiles and LSE/D rows");
-  m.def("attention_bwd_dsum", &prism::attention_bwd_dsum);
-  m.def("symm_alloc", &prism::symm_alloc);
-  m.def("symm_free", &prism::symm_free);
-  m.def("symm_handle", &prism::symm_handle);
-  m.def("symm_open", &prism::symm_open);
-  m.def("symm_close", &prism::symm_close);
-  m.def("symm_signal", &prism::symm_signal);
-  m.def("symm_wait", &prism::symm_wait);
-  m.def("symm_gather_rows", &prism::symm_gather_rows, "P2P row gather over NVLink (CP-transition reshard)");
-  m.def("symm_tensor", &prism::symm_tensor);
+  m.def("attention_bwd_dsum", &prism::attention_bwd_dsum, py::call_guard<py::gil_scoped_release>());
+  m.def("symm_alloc", &prism::symm_alloc, py::call_guard<py::gil_scoped_release>());
+  m.def("symm_free", &prism::symm_free, py::call_guard<py::gil_scoped_release>());
+  m.def("symm_handle", &prism::symm_handle, py::call_guard<py::gil_scoped_release>());
+  m.def("symm_open", &prism::symm_open, py::call_guard<py::gil_scoped_release>());
+  m.def("symm_close", &prism::symm_close, py::call_guard<py::gil_scoped_release>());
+  m.def("symm_signal", &prism::symm_signal, py::call_guard<py::gil_scoped_release>());
+  m.def("symm_wait", &prism::symm_wait, py::call_guard<py::gil_scoped_release>());
+  m.def("symm_gather_rows", &prism::symm_gather_rows, py::call_guard<py::gil_scoped_release>(), "P2P row gather over NVLink (CP-transition reshard)");
+  m.def("symm_tensor", &prism::symm_tensor, py::call_guard<py::gil_scoped_release>());
 }

@@ -24,6 +24,8 @@ carry the recurrent state across context-parallel ranks.
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from ._lib import is_cuda, lib, status
@@ -240,6 +242,9 @@ def fused_supported(q: torch.Tensor, v: torch.Tensor) -> bool:
 _SIDE = {}
 
 
+SIDE_STREAM = os.environ.get("PRISM_GDN_SIDE_STREAM", "1") == "1"
+
+
 def _side_stream(device) -> torch.cuda.Stream:
     s = _SIDE.get(device.index)
     if s is None:
@@ -294,7 +299,7 @@ class _FusedChunkRule(torch.autograd.Function):
         # the recomputed forward states and the reverse pass are independent sequential
         # scans over a few dozen SMs each: run them side by side on two streams
         main = torch.cuda.current_stream(qb.device)
-        side = _side_stream(qb.device)
+        side = _side_stream(qb.device) if SIDE_STREAM else main
         side.wait_stream(main)
         watchdog.beat("gdn backward prep")
         with torch.cuda.stream(side):

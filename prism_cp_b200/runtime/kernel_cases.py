@@ -7,6 +7,7 @@ capture of one of its kernels (``-k <kernel> -c 1``) ends in a minute or two.
 
 Cases
   gdn        fused chunked gated delta rule fwd + bwd, 4 x 4096 tokens, 16 heads, dk 128, dv 256
+  gdn32k     the same on one 32768-token sequence (one GDN layer of the 1.3B model at CP = 1)
   attention  causal GQA flash attention fwd + bwd, 2 x 8192 tokens, 16 query / 4 kv heads, d 128
   gemm       bf16 GEMM 16384 x 2048 x 8192 (forward projection shape of the 1.3B model)
   conv       causal conv1d + SiLU fwd + bwd, 32768 tokens x 8192 channels
@@ -21,9 +22,8 @@ import torch
 import torch.nn.functional as F
 
 
-def case_gdn(dev):
+def case_gdn(dev, lens=(4096,) * 4):
     from ..ops.gdn import ChunkLayout, fused_gated_delta_rule
-    lens = (4096,) * 4
     T, H = sum(lens), 16
     g = torch.Generator(device=dev).manual_seed(0)
     q = F.normalize(torch.randn(T, H, 128, device=dev, generator=g), dim=-1).to(torch.bfloat16).requires_grad_(True)
@@ -77,25 +77,36 @@ def case_conv(dev):
     return run
 
 
-CASES = {"gdn": case_gdn, "attention": case_attention, "gemm": case_gemm, "conv": case_conv}
+def case_gdn32k(dev):
+    return case_gdn(dev, (32768,))
+
+
+CASES = {"gdn": case_gdn, "gdn32k": case_gdn32k, "attention": case_attention, "gemm": case_gemm, "conv": case_conv}
 
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("case", choices=sorted(CASES))
     ap.add_argument("--iters", type=int, default=2)
+    ap.add_argument("--no-sync", action="store_true", help="queue iterations back to back (host runs ahead)")
     args = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     run = CASES[args.case](dev)
+    from ..utils import watchdog
+    watchdog.from_env()
     ms = 0.0
-    for _ in range(args.iters):
+    for i in range(args.iters):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         run()
         b.record()
-        torch.cuda.synchronize()
-        ms = a.elapsed_time(b)
+        watchdog.beat(f"iteration {i} queued")
+        if not args.no_sync:
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
     from ..ops._lib import check_status
     check_status(dev)
     print(f"{args.case}: {ms:.3f} ms (last of {args.iters})")
