@@ -262,7 +262,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         ok = __all_sync(0xffffffffu, mbar_wait_bounded(pv_done, (j - 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
         if (!ok) break;
       }
-      if (j > 0 && alpha != 1.f) {
+      // tcgen05.ld/st are warp-collective (.sync.aligned): the rescale runs for the whole warp
+      // whenever any of its rows needs it (rows that do not multiply by alpha = 1)
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
