@@ -91,22 +91,44 @@ def main(argv=None) -> int:
                                 timeout=datetime.timedelta(minutes=args.distributed_timeout_minutes))
     cfg = model_config(args)
     dtype = torch.bfloat16 if (args.bf16 and cuda) else torch.float32
-    model = HybridModel(cfg, dtype=dtype, device=device, seed=args.seed)
-    trainer = Trainer(model, Teams(world), device, lr=args.lr, min_lr=args.min_lr, weight_decay=args.weight_decay,
-                      clip_grad=args.clip_grad, warmup_steps=args.lr_warmup_iters,
-                      decay_steps=args.lr_decay_iters or args.train_iters, records=args.records,
-                      overlap_grad_reduce=args.overlap_grad_reduce,
-                      bucket_bytes=(args.ddp_bucket_size or (64 << 20)) * 4)
+    tp_size, pp_size = args.tensor_model_parallel_size, args.pipeline_model_parallel_size
+    pipeline = None
+    if pp_size > 1:
+        # 1F1B over stages of world / pp ranks; each stage builds only its own layers
+        from ..runtime.pipeline import PipelineTrainer, make_stage
+        info = make_stage(pp_size, cfg.num_layers)
+        model = HybridModel(cfg, dtype=dtype, device=device, seed=args.seed,
+                            layers=range(info.first_layer, info.first_layer + info.num_layers),
+                            pre_process=info.stage == 0, post_process=info.stage == pp_size - 1)
+        pipeline = PipelineTrainer(model, info, device, lr=args.lr, min_lr=args.min_lr,
+                                   weight_decay=args.weight_decay, clip_grad=args.clip_grad,
+                                   warmup_steps=args.lr_warmup_iters,
+                                   decay_steps=args.lr_decay_iters or args.train_iters)
+        plan_world = info.stage_world
+        trainer = pipeline
+    else:
+        tpc = None
+        if tp_size > 1:
+            from ..parallel.tensor import make_tp
+            tpc = make_tp(tp_size)
+        model = HybridModel(cfg, dtype=dtype, device=device, seed=args.seed, tp=tpc)
+        teams = Teams(world, tp=tpc) if tpc is not None else Teams(world)
+        plan_world = world // tp_size
+        trainer = Trainer(model, teams, device, lr=args.lr, min_lr=args.min_lr, weight_decay=args.weight_decay,
+                          clip_grad=args.clip_grad, warmup_steps=args.lr_warmup_iters,
+                          decay_steps=args.lr_decay_iters or args.train_iters, records=args.records,
+                          overlap_grad_reduce=args.overlap_grad_reduce,
+                          bucket_bytes=(args.ddp_bucket_size or (64 << 20)) * 4)
     replays = json.loads(Path(args.joint_replay).read_text()) if args.joint_replay else None
     start = 1
-    if args.load and checkpoint.latest(args.load) is not None:
+    if pipeline is None and args.load and checkpoint.latest(args.load) is not None:
         start = checkpoint.load(trainer, checkpoint.latest(args.load)) + 1
     enable_nvtx(args.nvtx_ranges or nvtx_enabled())
     window = ProfileWindow(args.profile_step_start, args.profile_step_end, args.profile_ranks, rank,
                            enabled=args.profile and cuda)
     for step in range(start, args.train_iters + 1):
         batch = global_batch(args, world, step, pin=cuda)
-        plan = plan_for(args, batch, world, cfg.pattern, step, replays)
+        plan = plan_for(args, batch, plan_world, cfg.pattern, step, replays)
         window.before(step)
         with nvtx(f"step {step}"):
             res = trainer.train_step(batch, plan)
@@ -114,7 +136,7 @@ def main(argv=None) -> int:
         if rank == 0 and step % args.log_interval == 0:
             print(json.dumps({"step": step, "loss": res.loss, "lr": res.lr, "tokens": res.tokens,
                               "microbatches": res.microbatches}), flush=True)
-        if args.save and args.save_interval and step % args.save_interval == 0:
+        if pipeline is None and args.save and args.save_interval and step % args.save_interval == 0:
             checkpoint.save(trainer, args.save, plan_cursor=step)
     if world > 1:
         dist.barrier()
