@@ -1,5 +1,9 @@
 """Numerical contracts and the optimizer-shard / logical numerics gates.
 
+* ``LogicalNumerics``: per-sample embedding Y, decoder Y, embedding dX and
+  token loss rebuilt across ranks and layouts, compared with a reference run
+  (reference: logical_numerics.py:11-208).
+
 * ``contract(profile, architecture)``: named, frozen tolerance sets
   ``strict_v1``, ``cp_bf16_v2`` and ``cp_bf16_exploratory_v3`` for
   ``gdngqa_gpt`` / ``gqa_gpt`` (limits as the reference's
@@ -111,3 +115,111 @@ class TrainingNumerics:
             dist.all_reduce(flag, op=dist.ReduceOp.MAX)
         if flag.item() > 0:
             raise AssertionError(f"optimizer numerics gate failed at step {step}: {self.failures[:3]}")
+
+
+class LogicalNumerics:
+    """Logical per-sample gate: embedding Y, decoder Y, embedding dX and token loss.
+
+    Every rank holds rows of its ingress layout; ``record`` keeps, for one
+    microbatch, the local rows' (sample, position, token, label, weight) with
+    the embedding output, the decoder output before the final norm, the
+    gradient at the embedding output and the per-token loss. ``finish`` gathers
+    all ranks' rows (``all_gather_object``), rebuilds every logical sample in
+    position order, and either writes the samples (``mode="write"``, the
+    reference run, typically CP = 1) or compares them with the reference: data
+    fields exactly (the same token / label / mask at every position, every
+    position owned once), Y / dX / loss by relative L2 under the contract's
+    logical limits. The failure flag is MAX-all-reduced so all ranks stop
+    together (reference: logical_numerics.py:11-208, with zigzag positions).
+    """
+
+    def __init__(self, output: str | Path, mode: str = "off", reference: str | Path | None = None, steps: int = 1,
+                 limits: dict | None = None, rank: int = 0, group=None, device="cpu", distributed: bool = True):
+        if mode not in ("off", "write", "read"):
+            raise ValueError("logical numerics mode must be off, write or read")
+        self.output, self.mode, self.steps, self.rank, self.group = Path(output), mode, steps, rank, group
+        self.device = device
+        # a one-process reference run inside a distributed job gathers nothing
+        self.distributed = distributed
+        self.reference = Path(reference) if reference else self.output
+        self.limits = limits or contract("cp_bf16_v2")["logical"]
+        self.rows: list[dict] = []
+        self.failures: list[dict] = []
+
+    def active(self, step: int) -> bool:
+        return self.mode != "off" and step <= self.steps
+
+    def _multi(self) -> bool:
+        return (self.distributed and dist.is_available() and dist.is_initialized()
+                and dist.get_world_size(self.group) > 1)
+
+    def record(self, layout, tokens, labels, weights, y_embed, y_decoder, dx_embed, token_loss) -> None:
+        """Local rows of one microbatch in ``layout`` (a LocalLayout: spans of (sample, begin, _, count))."""
+        row = 0
+        for sample, begin, _, count in layout.spans:
+            sl = slice(row, row + count)
+            self.rows.append({
+                "sample": int(sample), "positions": list(range(begin, begin + count)),
+                "tokens": tokens[sl].cpu(), "labels": labels[sl].cpu(), "weights": weights[sl].float().cpu(),
+                "embedding_Y": y_embed[sl].float().cpu(), "decoder_Y": y_decoder[sl].float().cpu(),
+                "embedding_dX": dx_embed[sl].float().cpu(), "token_loss": token_loss[sl].float().cpu()})
+            row += count
+
+    def _assemble(self, rows: list[dict]) -> dict:
+        by_sample: dict = {}
+        for r in rows:
+            by_sample.setdefault(r["sample"], []).append(r)
+        out = {}
+        for s, parts in by_sample.items():
+            n = max(p for r in parts for p in r["positions"]) + 1
+            owned = torch.zeros(n, dtype=torch.int32)
+            fields = {}
+            for r in parts:
+                idx = torch.tensor(r["positions"])
+                owned[idx] += 1
+                for k in ("tokens", "labels", "weights", "embedding_Y", "decoder_Y", "embedding_dX", "token_loss"):
+                    t = r[k]
+                    if k not in fields:
+                        fields[k] = torch.zeros((n,) + tuple(t.shape[1:]), dtype=t.dtype)
+                    fields[k][idx] = t
+            fields["owned"] = owned
+            out[s] = fields
+        return out
+
+    def finish(self, step: int) -> None:
+        if not self.active(step):
+            self.rows = []
+            return
+        rows = self.rows
+        self.rows = []
+        if self._multi():
+            gathered = [None] * dist.get_world_size(self.group)
+            dist.all_gather_object(gathered, rows, group=self.group)
+            rows = [r for part in gathered for r in part]
+        samples = self._assemble(rows)
+        failures = []
+        if self.rank == 0:
+            if self.mode == "write":
+                self.output.mkdir(parents=True, exist_ok=True)
+                torch.save(samples, self.output / f"logical_step{step}.pt")
+            else:
+                ref = torch.load(self.reference / f"logical_step{step}.pt")
+                if set(ref) != set(samples):
+                    failures.append({"step": step, "field": "samples", "reason": "sample sets differ"})
+                for s in set(ref) & set(samples):
+                    a, e = samples[s], ref[s]
+                    if not torch.equal(a["owned"], torch.ones_like(a["owned"])):
+                        failures.append({"step": step, "sample": s, "field": "ownership"})
+                    for k in ("tokens", "labels", "weights"):
+                        if not torch.equal(a[k], e[k]):
+                            failures.append({"step": step, "sample": s, "field": k})
+                    for k in ("embedding_Y", "decoder_Y", "embedding_dX", "token_loss"):
+                        res = compare(a[k], e[k], self.limits[k], 0.0)
+                        if not res["ok"]:
+                            failures.append(dict(res, step=step, sample=s, field=k))
+        self.failures.extend(failures)
+        flag = torch.tensor([1.0 if failures else 0.0], device=self.device)
+        if self._multi():
+            dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.group)
+        if flag.item() > 0:
+            raise AssertionError(f"logical numerics gate failed at step {step}: {failures[:3]}")

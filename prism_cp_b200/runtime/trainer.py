@@ -56,7 +56,7 @@ class Trainer:
     def __init__(self, model, teams, device, lr=3e-4, min_lr=3e-5, weight_decay=0.1, clip_grad=1.0,
                  warmup_steps=0, decay_steps=1000, group=None, hbm_guard=True, records: str | None = None,
                  numerics=None, audit: bool = False, overlap_grad_reduce: bool = False,
-                 bucket_bytes: int = 256 << 20):
+                 bucket_bytes: int = 256 << 20, logical=None):
         self.model, self.teams, self.device = model, teams, device
         self.world = teams.world
         self.rank = teams.rank
@@ -77,6 +77,7 @@ class Trainer:
         self.loss_acc = torch.zeros((), dtype=torch.float32, device=device)
         self.recorder = StepRecorder(records, self.rank) if records else None
         self.numerics = numerics
+        self.logical = logical
         self.audit = AccumulationAudit() if audit else None
         self.step_index = 0
         self.watchdog = watchdog.from_env()
@@ -94,8 +95,17 @@ class Trainer:
             dev = host.to(self.device) if host.tokens.device != self.device else host
             run = MicrobatchRun(mb, batch_lengths, self.cache)
             watchdog.beat(f"step {self.step_index + 1} microbatch {index} forward")
+            logical = self.logical is not None and self.logical.active(self.step_index + 1)
             with nvtx(f"microbatch {index} forward"):
-                loss, _ = run.forward(self.model, dev.tokens, dev.labels, dev.weights)
+                if logical:
+                    from ..parallel.transport import move
+                    x0 = self.model.embed(dev.tokens)
+                    x0.retain_grad()
+                    y, prev = run.forward_layers(self.model, x0)
+                    y = move(y, prev, run.ingress)
+                    loss, ce = self.model.loss(y, dev.labels, dev.weights)
+                else:
+                    loss, _ = run.forward(self.model, dev.tokens, dev.labels, dev.weights)
             self._debug_point(index, "forward")
             if self.overlap is not None:
                 # the last backward reduce-scatters each finished bucket while it runs
@@ -103,6 +113,9 @@ class Trainer:
             watchdog.beat(f"step {self.step_index + 1} microbatch {index} backward")
             with nvtx(f"microbatch {index} backward"):
                 loss.backward()
+            if logical:
+                self.logical.record(run.ingress, dev.tokens, dev.labels, dev.weights, x0.detach(), y.detach(),
+                                    x0.grad, ce)
             self._debug_point(index, "backward")
             if self.audit is not None:
                 self.audit.backward(len(self.audit.events))
@@ -132,6 +145,8 @@ class Trainer:
             return self._tracked_step(batch, plan, inputs)
         self.flat.zero_grad()
         loss = self.forward_backward(batch.lengths, plan, inputs)
+        if self.logical is not None:
+            self.logical.finish(self.step_index + 1)
         watchdog.beat(f"step {self.step_index + 1} optimizer")
         lr = self.optimizer.step()
         self.step_index += 1
@@ -155,6 +170,8 @@ class Trainer:
             self.audit.events.clear()
         self.flat.zero_grad()
         loss = self.forward_backward(batch.lengths, plan, inputs)
+        if self.logical is not None:
+            self.logical.finish(self.step_index + 1)
         if self.audit is not None:
             self.optimizer.audit = self.audit
         lr = self.optimizer.step()

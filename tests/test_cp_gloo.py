@@ -364,3 +364,47 @@ def test_pipeline_1f1b_pp2_matches_single_process():
 
 def test_pipeline_1f1b_pp2_cp2_matches_single_process():
     run_ranks(_pp_case, 4, 2, 2, timeout=900)
+
+
+# ------------------------------------------------------------------ logical numerics gate
+def _logical_case(rank, world, ref_dir):
+    from prism_cp_b200.models.config import hybrid_tiny
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.parallel.teams import Teams
+    from prism_cp_b200.planner.joint.ir import Group, Layout, Microbatch, Plan
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.numerics import LogicalNumerics
+    from prism_cp_b200.runtime.trainer import Trainer
+    cfg = hybrid_tiny()
+    batch = make_batch([1152, 896], cfg.vocab_size, seed=4)
+    if rank == 0:
+        # reference: one process, CP = 1, writes every logical sample
+        one = Layout((Group((0,), (0, 1)),), "zigzag")
+        ref_plan = Plan(1, cfg.pattern, (Microbatch(one, tuple((one.with_mode("contiguous"),) * 2 if c == "G"
+                                                                  else (one, one) for c in cfg.pattern)),))
+
+        class Solo:
+            world, rank, initialized = 1, 0, False
+
+            def team(self, ranks):
+                return None
+
+        gate = LogicalNumerics(ref_dir, mode="write", steps=1, distributed=False)
+        ref = Trainer(HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0), Solo(), torch.device("cpu"),
+                      logical=gate)
+        ref.train_step(batch, ref_plan)
+    dist.barrier()
+    # GDN layers at CP = 2 (contiguous), GQA at CP = 2 (zigzag): rows move between layouts
+    gdn = Layout((Group((0, 1), (0, 1)),), "contiguous")
+    gqa = Layout((Group((0, 1), (0, 1)),), "zigzag")
+    plan = Plan(2, cfg.pattern, (Microbatch(gqa, tuple((gdn, gdn) if c == "G" else (gqa, gqa)
+                                                       for c in cfg.pattern)),))
+    gate = LogicalNumerics(ref_dir, mode="read", steps=1, rank=rank)
+    tr = Trainer(HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0), Teams(world), torch.device("cpu"),
+                 logical=gate)
+    tr.train_step(batch, plan)
+    assert not gate.failures
+
+
+def test_logical_gate_cp2_matches_cp1_reference(tmp_path):
+    run_ranks(_logical_case, 2, str(tmp_path))

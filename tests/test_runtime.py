@@ -126,3 +126,36 @@ def test_overlapped_bucket_reduce_matches_single_bucket():
     (l0, p0), (l1, p1) = results
     assert l0 == pytest.approx(l1, rel=1e-6)
     assert torch.allclose(p0, p1, rtol=1e-5, atol=1e-6)
+
+
+def test_logical_gate_flags_a_different_model(tmp_path):
+    """The logical gate passes against itself and fails against a differently initialised model."""
+    import pytest
+    import torch
+    from prism_cp_b200.models.config import hybrid_tiny
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.planner.fixed import uniform_plan
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.numerics import LogicalNumerics
+    from prism_cp_b200.runtime.trainer import Trainer
+
+    class Solo:
+        world, rank, initialized = 1, 0, False
+
+        def team(self, ranks):
+            return None
+
+    cfg = hybrid_tiny()
+    batch = make_batch([384, 256], cfg.vocab_size, seed=3)
+    plan = uniform_plan(batch.lengths, 1, 1, 1024, cfg.pattern)
+
+    def step(seed, mode):
+        gate = LogicalNumerics(tmp_path, mode=mode, steps=1)
+        Trainer(HybridModel(cfg, dtype=torch.float32, device="cpu", seed=seed), Solo(), torch.device("cpu"),
+                logical=gate).train_step(batch, plan)
+        return gate
+
+    step(0, "write")
+    assert not step(0, "read").failures
+    with pytest.raises(AssertionError, match="logical numerics gate failed"):
+        step(1, "read")
