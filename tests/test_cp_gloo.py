@@ -408,3 +408,39 @@ def _logical_case(rank, world, ref_dir):
 
 def test_logical_gate_cp2_matches_cp1_reference(tmp_path):
     run_ranks(_logical_case, 2, str(tmp_path))
+
+
+# ------------------------------------------------------------------ the benchmark's layout at 4 and 8 ranks
+def _wide_cp_case(rank, world):
+    from prism_cp_b200.models.config import hybrid_tiny
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.parallel.teams import Teams
+    from prism_cp_b200.planner.fixed import uniform_plan
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.trainer import Trainer
+    cfg = hybrid_tiny()
+    lengths = [256 * world * 2, 256 * world]      # every sequence splits into whole zigzag chunks
+    batch = make_batch(lengths, cfg.vocab_size, seed=6)
+    plan = uniform_plan(batch.lengths, world, world, 256 * 3, cfg.pattern)   # CP = world, as bench.py
+    tr = Trainer(HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0), Teams(world), torch.device("cpu"),
+                 lr=1e-3)
+    losses = [tr.train_step(batch, plan).loss for _ in range(2)]
+    if rank == 0:
+        ref_plan = uniform_plan(batch.lengths, 1, 1, sum(lengths), cfg.pattern)
+
+        class Solo:
+            world, rank, initialized = 1, 0, False
+
+            def team(self, ranks):
+                return None
+
+        ref = Trainer(HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0), Solo(), torch.device("cpu"),
+                      lr=1e-3)
+        ref_losses = [ref.train_step(batch, ref_plan).loss for _ in range(2)]
+        for a, b in zip(losses, ref_losses):
+            assert abs(a - b) <= 1e-4 * abs(b), (losses, ref_losses)
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_bench_layout_cp_world_matches_cp1(world):
+    run_ranks(_wide_cp_case, world, timeout=600)
