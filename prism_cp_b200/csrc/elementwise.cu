@@ -237,6 +237,58 @@ __global__ void conv_fwd_vec_kernel(const __nv_bfloat16* __restrict__ x, long xs
   }
 }
 
+// Token-parallel forward: thread (channel group, token) computes one 8-channel output row
+// from its four taps. A warp covers 32 consecutive channel groups of one token (512
+// contiguous bytes per row); a block covers 32 channel groups x 32 tokens, each thread
+// 4 tokens 8 apart. No sequential chain, so every load is independent and in flight
+// at once; the taps' rows are shared through L1/L2, DRAM traffic stays one read of x
+// and one write of y.
+constexpr int kConvTokP = 32;
+constexpr bool kConvTokenParallel = true;  // false: the sequential 256-token form above
+
+__global__ void __launch_bounds__(256) conv_fwd_tok_kernel(const __nv_bfloat16* __restrict__ x, long xs,
+                                                           const __nv_bfloat16* __restrict__ w,
+                                                           const __nv_bfloat16* __restrict__ halo,
+                                                           const int* __restrict__ cu, int nseg, int T, int C,
+                                                           __nv_bfloat16* __restrict__ y) {
+  const int tc = threadIdx.x & 31, tt = threadIdx.x >> 5;
+  const int c8 = 8 * (blockIdx.y * 32 + tc);
+  if (c8 >= C) return;
+  float wk[8][kConvK];
+  {
+    // 8 channels x 4 taps = 32 consecutive bf16 (64 bytes)
+    const uint4* wp = reinterpret_cast<const uint4*>(w + (long)c8 * kConvK);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float f[8];
+      ld8f(reinterpret_cast<const __nv_bfloat16*>(wp + q), f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) wk[2 * q + e / 4][e % 4] = f[e];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kConvTokP / 8; ++k) {
+    const int t = blockIdx.x * kConvTokP + tt + 8 * k;
+    if (t >= T) break;
+    const int seg = find_segment(cu, nseg, t);
+    const int start = cu[seg];
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kConvK; ++j) {
+      float f[8];
+      conv_x8(x, xs, halo, C, c8, seg, start, t - (kConvK - 1) + j, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(wk[i][j], f[i], acc[i]);
+    }
+    float out[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = silu(acc[i]);
+    st8f(y + (long)t * C + c8, out);
+  }
+}
+
 __global__ void conv_bwd_vec_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                                     long xs, const __nv_bfloat16* __restrict__ w,
                                     const __nv_bfloat16* __restrict__ halo, const int* __restrict__ cu, int nseg,
@@ -553,6 +605,15 @@ at::Tensor conv1d_silu_fwd(const at::Tensor& x, const at::Tensor& w, const c10::
   }
   const bool vec = C % 8 == 0 && x.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(w.data_ptr()) & 15) == 0;
+  if (vec && kConvTokenParallel) {
+    dim3 gp((T + kConvTokP - 1) / kConvTokP, (C / 8 + 31) / 32);
+    conv_fwd_tok_kernel<<<gp, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), hp, cu.data_ptr<int>(), (int)cu.numel() - 1, T, C,
+        reinterpret_cast<__nv_bfloat16*>(y.data_ptr()));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return y;
+  }
   if (vec) {
     dim3 gv((T + kConvTokV - 1) / kConvTokV, (C / 8 + 127) / 128);
     conv_fwd_vec_kernel<<<gv, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
