@@ -7,7 +7,7 @@
 * ``contract(profile, architecture)``: named, frozen tolerance sets
   ``strict_v1``, ``cp_bf16_v2`` and ``cp_bf16_exploratory_v3`` for
   ``gdngqa_gpt`` / ``gqa_gpt`` (limits as the reference's
-  numerical_contracts.py:9-54, so a run judged there is judged the same here);
+  numerical_contracts.py:9-54, so a run passes or fails the same limits in both);
   ``load_contract`` rejects any edited copy.
 * ``TrainingNumerics``: writes (``mode="write"``) or checks (``mode="read"``) the
   fp32 master weights, gradients and Adam states of the first steps against a
