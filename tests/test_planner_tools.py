@@ -109,3 +109,20 @@ def test_cli_study_reports_alpha_selection(tmp_path):
     assert {"native_K4096", "native_K8192", "native_K16384", "joint"} <= ids
     assert report["decision"]["selected"] in ids
     assert (out / "REPORT.md").read_text().startswith("# Native N vs joint plan")
+
+
+def test_b200_cp1_costfit_reproduces_measured_records():
+    """The committed B200 CP1 fit (from measured module records) matches its own measurements."""
+    import json
+    from pathlib import Path
+    import pytest
+    from prism_cp_b200.planner.costfit import CostFit
+    root = Path(__file__).resolve().parents[1] / "prism_cp_b200" / "planner" / "data"
+    fits = {m: CostFit(**f) for m, f in json.loads((root / "b200_cp1_costfit.json").read_text())["fits"].items()}
+    recs = json.loads((root / "b200_module_records.json").read_text())
+    for key, module in (("gqa", "GQA"), ("gdn", "GDN")):
+        for r in recs[key]["records"]:
+            if r.get("sequences", 1) == 1:
+                assert abs(fits[module].query(r["tokens"]) - r["fb_ms"]) <= 0.15 * r["fb_ms"] + 0.5
+    with pytest.raises(ValueError):
+        fits["GQA"].query(8192, cp=2)
