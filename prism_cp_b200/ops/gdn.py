@@ -243,6 +243,9 @@ _SIDE = {}
 
 
 SIDE_STREAM = os.environ.get("PRISM_GDN_SIDE_STREAM", "1") == "1"
+# keep the forward's prep outputs, per-chunk states and Delta rows for the backward (about 2 GB per
+# GDN layer per 32K tokens at 16 heads x dv 256) instead of recomputing them
+SAVE_INTERMEDIATES = os.environ.get("PRISM_GDN_SAVE", "1") == "1"
 
 
 def _side_stream(device) -> torch.cuda.Stream:
@@ -255,11 +258,14 @@ def _side_stream(device) -> torch.cuda.Stream:
 class _FusedChunkRule(torch.autograd.Function):
     """Chunked gated delta rule on the fused kernels.
 
-    Forward: prep (WY form, decays, Aqk) and one tcgen05 state pass that also
-    produces the output. Only the inputs are saved; the backward recomputes the
-    prep and the per-chunk states, runs the reverse state pass and the
-    chunk-local backward (dv contractions on tcgen05, WY/decay terms on CUDA
-    cores). Same recurrence as ``chunk_gated_delta_rule``.
+    Forward: prep (WY form, decays, Aqk, and the k.k / s q.k / T blocks the
+    backward needs) and one tcgen05 state pass that also produces the output and
+    writes the per-chunk states and Delta rows. These are kept for the backward,
+    which runs the reverse state pass and the chunk-local backward (dv
+    contractions on tcgen05, WY/decay terms on CUDA cores). With
+    ``PRISM_GDN_SAVE=0`` only the inputs are kept and the backward recomputes
+    the prep and the states (the recompute on a second stream, side by side
+    with the reverse pass). Same recurrence as ``chunk_gated_delta_rule``.
     """
 
     @staticmethod
@@ -269,17 +275,27 @@ class _FusedChunkRule(torch.autograd.Function):
         qb, kb, vb = (t.to(bf).contiguous() for t in (q, k, v))
         gf, bt = g.float().contiguous(), beta.float().contiguous()
         st = status(q.device)
-        Wn, U, Kd, Qg, Aqk, gam, _, _ = L.gdn_chunk_prep(qb, kb, vb, gf, bt, layout.tok0_dev, layout.len_dev,
-                                                        scale, False, st)
+        keep = SAVE_INTERMEDIATES and any(ctx.needs_input_grad[:5])
+        Wn, U, Kd, Qg, Aqk, gam, Gc, aux = L.gdn_chunk_prep(qb, kb, vb, gf, bt, layout.tok0_dev, layout.len_dev,
+                                                            scale, keep, st)
         T, H, DV = vb.shape
         o = torch.empty_like(vb)
         S_final = torch.empty((len(layout.lengths), H, qb.shape[-1], DV), dtype=torch.float32, device=q.device)
         s0 = S0.float().contiguous() if S0 is not None else None
+        states = rows = None
+        if keep:
+            Nc = Wn.shape[0]
+            states = torch.empty((Nc, H, DV, 128), dtype=torch.bfloat16, device=q.device)
+            rows = torch.empty((Nc, H, DV, CHUNK), dtype=torch.bfloat16, device=q.device)
         watchdog.beat("gdn forward prep")
         L.gdn_chunk_fwd(Wn, U, Kd, Qg, Aqk, gam, layout.tok0_dev, layout.len_dev, layout.seq_chunks_dev, s0, o,
-                        S_final, None, None, st)
+                        S_final, states, rows, st)
         watchdog.beat("gdn forward state pass")
-        ctx.save_for_backward(qb, kb, vb, gf, bt, s0)
+        if keep:
+            ctx.save_for_backward(qb, kb, vb, gf, bt, s0, Wn, U, Kd, Qg, Aqk, gam, Gc, aux, states, rows)
+        else:
+            ctx.save_for_backward(qb, kb, vb, gf, bt, s0)
+        ctx.kept = keep
         ctx.layout, ctx.scale, ctx.has_s0 = layout, scale, S0 is not None
         ctx.dtypes = (q.dtype, k.dtype, v.dtype, g.dtype, beta.dtype)
         return o.to(v.dtype), S_final
@@ -287,27 +303,32 @@ class _FusedChunkRule(torch.autograd.Function):
     @staticmethod
     def backward(ctx, do, dS_final):
         L = lib()
-        qb, kb, vb, gf, bt, s0 = ctx.saved_tensors
         lay = ctx.layout
-        st = status(qb.device)
-        Wn, U, Kd, Qg, Aqk, gam, Gc, aux = L.gdn_chunk_prep(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, ctx.scale,
-                                                            True, st)
-        Nc, H = Wn.shape[0], Wn.shape[1]
-        DV = vb.shape[-1]
-        states = torch.empty((Nc, H, DV, 128), dtype=torch.bfloat16, device=qb.device)
-        rows = torch.empty((Nc, H, DV, CHUNK), dtype=torch.bfloat16, device=qb.device)
-        # the recomputed forward states and the reverse pass are independent sequential
-        # scans over a few dozen SMs each: run them side by side on two streams
-        main = torch.cuda.current_stream(qb.device)
-        side = _side_stream(qb.device) if SIDE_STREAM else main
-        side.wait_stream(main)
-        watchdog.beat("gdn backward prep")
-        with torch.cuda.stream(side):
-            L.gdn_chunk_fwd(Wn, U, Kd, Qg, Aqk, gam, lay.tok0_dev, lay.len_dev, lay.seq_chunks_dev, s0, None, None,
-                            states, rows, st)
-            watchdog.beat("gdn backward state recompute (side stream)")
-        for t in (Wn, U, Kd, Qg, Aqk, gam, states, rows) + ((s0,) if s0 is not None else ()):
-            t.record_stream(side)
+        main = torch.cuda.current_stream(ctx.saved_tensors[0].device)
+        side = main
+        if ctx.kept:
+            qb, kb, vb, gf, bt, s0, Wn, U, Kd, Qg, Aqk, gam, Gc, aux, states, rows = ctx.saved_tensors
+            st = status(qb.device)
+        else:
+            qb, kb, vb, gf, bt, s0 = ctx.saved_tensors
+            st = status(qb.device)
+            Wn, U, Kd, Qg, Aqk, gam, Gc, aux = L.gdn_chunk_prep(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev,
+                                                                ctx.scale, True, st)
+            Nc, H = Wn.shape[0], Wn.shape[1]
+            DV = vb.shape[-1]
+            states = torch.empty((Nc, H, DV, 128), dtype=torch.bfloat16, device=qb.device)
+            rows = torch.empty((Nc, H, DV, CHUNK), dtype=torch.bfloat16, device=qb.device)
+            # the recomputed forward states and the reverse pass are independent sequential
+            # scans over a few dozen SMs each: run them side by side on two streams
+            side = _side_stream(qb.device) if SIDE_STREAM else main
+            side.wait_stream(main)
+            watchdog.beat("gdn backward prep")
+            with torch.cuda.stream(side):
+                L.gdn_chunk_fwd(Wn, U, Kd, Qg, Aqk, gam, lay.tok0_dev, lay.len_dev, lay.seq_chunks_dev, s0, None,
+                                None, states, rows, st)
+                watchdog.beat("gdn backward state recompute (side stream)")
+            for t in (Wn, U, Kd, Qg, Aqk, gam, states, rows) + ((s0,) if s0 is not None else ()):
+                t.record_stream(side)
         dstates, drows = torch.empty_like(states), torch.empty_like(rows)
         dS0 = torch.empty_like(s0) if ctx.has_s0 else None
         if do is None:
