@@ -269,3 +269,23 @@ def test_model_step_gpu_matches_fp32_cpu_direction():
         losses.append(loss.item())
         assert all(p.grad is None or torch.isfinite(p.grad).all() for p in model.parameters())
     assert abs(losses[0] - losses[1]) / abs(losses[0]) < 2e-2
+
+
+# ------------------------------------------------------------------ bounded device waits
+def test_a_device_wait_that_runs_out_reports_an_error_and_the_context_survives():
+    """A flag nothing sets: the bounded wait gives up after its limit, records an error status the
+    host reads, and the CUDA context keeps working (no trap, no hang)."""
+    import time
+    from prism_cp_b200.ops._lib import check_status, lib, status
+    dev = torch.device(DEV, torch.cuda.current_device())
+    flags = torch.zeros(8, dtype=torch.int64, device=dev)
+    torch.cuda.synchronize()
+    t0 = time.monotonic()
+    lib().symm_wait(flags.data_ptr(), 0, 1, 1, status(dev))
+    torch.cuda.synchronize()
+    waited = time.monotonic() - t0
+    assert 1.5 < waited < 60, waited
+    with pytest.raises(RuntimeError, match="timed out"):
+        check_status(dev)
+    a = torch.randn(256, 256, device=dev)
+    assert torch.allclose(a @ torch.eye(256, device=dev), a)
