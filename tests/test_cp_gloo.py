@@ -444,3 +444,44 @@ def _wide_cp_case(rank, world):
 @pytest.mark.parametrize("world", [4, 8])
 def test_bench_layout_cp_world_matches_cp1(world):
     run_ranks(_wide_cp_case, world, timeout=600)
+
+
+# ------------------------------------------------------------------ heterogeneous CP inside one microbatch
+def _mixed_case(rank, world):
+    from prism_cp_b200.models.config import hybrid_tiny
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.parallel.teams import Teams
+    from prism_cp_b200.planner.joint.ir import Group, Layout, Microbatch, Plan
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.trainer import Trainer
+    cfg = hybrid_tiny()
+    batch = make_batch([1024, 384, 256], cfg.vocab_size, seed=8)
+    # attention: sample 0 at CP = 2 (zigzag) beside samples 1 and 2 at CP = 1, all in one microbatch;
+    # GDN: all three samples at CP = 4 (contiguous); every GDN <-> GQA boundary reshards
+    gqa = Layout((Group((0, 1), (0,)), Group((2,), (1,)), Group((3,), (2,))), "zigzag")
+    gdn = Layout((Group((0, 1, 2, 3), (0, 1, 2)),), "contiguous")
+    plan = Plan(4, cfg.pattern, (Microbatch(gqa, tuple((gdn, gdn) if c == "G" else (gqa, gqa)
+                                                       for c in cfg.pattern)),))
+    tr = Trainer(HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0), Teams(world), torch.device("cpu"),
+                 lr=1e-3)
+    losses = [tr.train_step(batch, plan).loss for _ in range(2)]
+    if rank == 0:
+        one = Layout((Group((0,), (0, 1, 2)),), "zigzag")
+        ref_plan = Plan(1, cfg.pattern, (Microbatch(one, tuple((one.with_mode("contiguous"),) * 2 if c == "G"
+                                                                  else (one, one) for c in cfg.pattern)),))
+
+        class Solo:
+            world, rank, initialized = 1, 0, False
+
+            def team(self, ranks):
+                return None
+
+        ref = Trainer(HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0), Solo(), torch.device("cpu"),
+                      lr=1e-3)
+        ref_losses = [ref.train_step(batch, ref_plan).loss for _ in range(2)]
+        for a, b in zip(losses, ref_losses):
+            assert abs(a - b) <= 1e-4 * abs(b), (losses, ref_losses)
+
+
+def test_heterogeneous_cp_in_one_microbatch_matches_cp1():
+    run_ranks(_mixed_case, 4, timeout=600)
