@@ -1,0 +1,110 @@
+"""Calibrate the planner's operator costs to measured single-GPU (CP = 1) module times.
+
+The evaluator prices an operator from analytic FLOPs at ``Model.compute_tflops``
+(token-linear work, plus causal-attention work for GQA) and analytic CP
+communication. ``calibrate(records, model)`` fits, per operator, the measured
+forward + backward milliseconds of single-sequence module-bench records as
+
+    ms = linear_flops / (e_lin * rate) + quadratic_flops / (e_quad * rate) + fixed_ms
+
+with non-negative coefficients (exact active-set NNLS, ``costfit.nnls_exact``),
+so ``e_lin`` / ``e_quad`` are the fractions of the envelope the kernels reach
+and ``fixed_ms`` the per-call overhead. The result goes into
+``Model.operator_calibration``; CP > 1 keeps the analytic communication terms
+(at the measured NVLink bandwidth) unless a measured CP response profile is
+given. The committed ``data/b200_operator_calibration.json`` is fitted to this
+framework's own kernels on one B200 for the 1.3B shape.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+import numpy as np
+
+from .costfit import nnls_exact
+from .joint.cost import Model
+
+DEFAULT = Path(__file__).resolve().parent / "data" / "b200_operator_calibration.json"
+
+MODULES = {"GDN": "G", "GQA": "*", "M": "M", "MLP": "M"}
+
+
+def _analytic_ms(model: Model, symbol: str, tokens: int) -> tuple[float, float]:
+    """(linear ms, quadratic ms) the uncalibrated evaluator assigns one CP = 1 sequence of ``tokens``."""
+    m = model
+    h, f, d = m.hidden, m.ffn, m.gdn_heads * m.gdn_dim
+    n = tokens
+    rate = m.compute_tflops * 1e9
+    if symbol == "M":
+        return 18 * n * h * f / rate, 0.0
+    if symbol == "*":
+        proj = 6 * n * (h * (m.q_heads + 2 * m.kv_heads) * m.head_dim + h * h)
+        quad = 6 * m.q_heads * m.head_dim * n * n
+        return proj / rate, quad / rate
+    return 6 * n * (6 * h * d + 4 * m.gdn_heads * m.gdn_dim ** 2) / rate, 0.0
+
+
+def load_default() -> dict:
+    """The committed B200 calibration (fitted on the 1.3B shape)."""
+    return json.loads(DEFAULT.read_text())["calibration"]
+
+
+def calibrate(records: list[dict], model: Model) -> dict:
+    out = {}
+    by_sym: dict = {}
+    for r in records:
+        if int(r.get("cp", 1)) != 1 or int(r.get("sequences", 1)) != 1:
+            continue
+        sym = MODULES.get(r["module"])
+        if sym is not None:
+            by_sym.setdefault(sym, []).append((int(r["tokens"]), float(r["fb_ms"])))
+    for sym, pts in sorted(by_sym.items()):
+        rows, b = [], []
+        for tokens, ms in pts:
+            lin, quad = _analytic_ms(model, sym, tokens)
+            rows.append([lin, quad, 1.0] if sym == "*" else [lin, 1.0])
+            b.append(ms)
+        coef = nnls_exact(np.asarray(rows), np.asarray(b))
+        if sym == "*":
+            a, q, c = (float(x) for x in coef)
+        else:
+            (a, c), q = (float(x) for x in coef), 0.0
+        if a <= 0:
+            raise ValueError(f"{sym}: the token-linear term vanished; the records cannot calibrate it")
+        cal = {"linear": 1.0 / a, "fixed_ms": c, "points": len(pts)}
+        if sym == "*":
+            if q <= 0:
+                raise ValueError("GQA: the quadratic term vanished")
+            cal["quadratic"] = 1.0 / q
+        out[sym] = cal
+    return out
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--records", type=Path, required=True, help="module records (one file per module or combined)")
+    ap.add_argument("--model-config", default="hybrid-1.3b")
+    ap.add_argument("--output", type=Path, required=True)
+    args = ap.parse_args(argv)
+    from ..models.config import PRESETS
+    from .cli import B200_ENVELOPE
+    from .joint.cost import model_from_config
+    data = json.loads(args.records.read_text())
+    if "records" in data:
+        records = data["records"]
+    else:
+        records = [r for v in data.values() if isinstance(v, dict) for r in v.get("records", [])]
+    model = model_from_config(PRESETS[args.model_config](), B200_ENVELOPE["device_bytes"],
+                              **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"})
+    cal = calibrate(records, model)
+    args.output.write_text(json.dumps({"model_config": args.model_config, "compute_tflops": model.compute_tflops,
+                                       "source": str(args.records), "calibration": cal}, indent=1) + "\n")
+    print(json.dumps(cal))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -13,8 +13,11 @@ Commands
   handoff  CPU self-check of the planner stack
 
 Hardware models: ``--hardware B200`` uses this framework's B200 envelope
-(180 GB HBM3e, NVLink 5 through NVSwitch); ``--model-profile`` loads any Model
-JSON, including the reference's H100/H800 profiles, which share the schema.
+(180 GB HBM3e, NVLink 5 through NVSwitch) with operator costs calibrated to
+measured single-GPU module times of this framework's kernels
+(``calibrate.py``; ``--uncalibrated`` keeps the analytic envelope);
+``--model-profile`` loads any Model JSON, including the reference's H100/H800
+profiles, which share the schema.
 """
 
 from __future__ import annotations
@@ -48,6 +51,11 @@ def build_model(args) -> Model:
                                   **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"})
     else:
         model = Model(**B200_ENVELOPE)
+    if not getattr(args, "uncalibrated", False) and getattr(args, "hardware", "B200") == "B200":
+        from .calibrate import load_default
+        model = replace(model, operator_calibration={k: {x: v[x] for x in ("linear", "quadratic", "fixed_ms")
+                                                         if x in v} for k, v in load_default().items()},
+                        provenance=model.provenance + "; operator costs calibrated to measured B200 module times")
     if getattr(args, "cp_response", None):
         profile = json.loads(Path(args.cp_response).read_text())
         model = replace(model, cp_response=profile,
@@ -68,6 +76,8 @@ def _model_args(ap):
     g.add_argument("--hardware", choices=("B200",), default="B200")
     ap.add_argument("--model-config", help="framework model preset (e.g. hybrid-1.3b) for the model shape")
     ap.add_argument("--cp-response", type=Path, help="CP response profile JSON (e.g. a B200 anchor profile)")
+    ap.add_argument("--uncalibrated", action="store_true",
+                    help="analytic operator costs at the B200 envelope, without the measured module calibration")
 
 
 def _search_args(ap):

@@ -53,6 +53,10 @@ class Model:
     provenance: str = "analytic_unvalidated; throughput, link and storage envelopes are assumptions"
     cp_response: dict | None = None
     byte_scale: float = 1.0
+    # measured single-GPU efficiency per operator ("G", "*", "M"): {"linear": fraction of
+    # compute_tflops reached by the token-linear work, "quadratic": the same for causal attention,
+    # "fixed_ms": per-call overhead}; None keeps the analytic envelope
+    operator_calibration: dict | None = None
 
     def __post_init__(self):
         for key, value in asdict(self).items():
@@ -66,6 +70,10 @@ class Model:
                 raise ValueError(f"Model field must be positive: {key}")
         if self.cp_response is not None:
             validate_response(self.cp_response, self)
+        for sym, cal in (self.operator_calibration or {}).items():
+            if sym not in ("G", "*", "M") or not (cal.get("linear", 0) > 0 and cal.get("quadratic", 1) > 0
+                                                  and cal.get("fixed_ms", 0) >= 0):
+                raise ValueError(f"invalid operator calibration for {sym!r}: {cal}")
 
     @property
     def budget(self) -> int:
@@ -167,7 +175,12 @@ class Evaluator:
             bandwidth = m.inter_gbps if cross else m.intra_gbps
             latency = 2 * m.latency_ms * (cp - 1) if symbol != "M" else 0.0
             rate = m.compute_tflops * 1e9
-            ms = self.response.cost(symbol, cp, (flops - quadratic) / rate, quadratic / rate,
+            lin_ms, quad_ms = (flops - quadratic) / rate, quadratic / rate
+            cal = (m.operator_calibration or {}).get(symbol)
+            if cal is not None:
+                lin_ms = lin_ms / cal["linear"] + cal.get("fixed_ms", 0.0)
+                quad_ms = quad_ms / cal.get("quadratic", 1.0)
+            ms = self.response.cost(symbol, cp, lin_ms, quad_ms,
                                     comm / (bandwidth * 1e6) + latency, comm / (m.intra_gbps * 1e6) + latency,
                                     sum(lens), squares, cross_node=cross)
             times.append(ms)

@@ -126,3 +126,32 @@ def test_b200_cp1_costfit_reproduces_measured_records():
                 assert abs(fits[module].query(r["tokens"]) - r["fb_ms"]) <= 0.15 * r["fb_ms"] + 0.5
     with pytest.raises(ValueError):
         fits["GQA"].query(8192, cp=2)
+
+
+def test_b200_operator_calibration_reproduces_module_times():
+    """Evaluator costs with the committed calibration match the measured CP = 1 module times."""
+    import json
+    from dataclasses import replace
+    from pathlib import Path
+    from prism_cp_b200.models.config import PRESETS
+    from prism_cp_b200.planner.calibrate import load_default
+    from prism_cp_b200.planner.cli import B200_ENVELOPE
+    from prism_cp_b200.planner.joint.cost import Evaluator, model_from_config
+    from prism_cp_b200.planner.joint.ir import Group, Layout
+    model = model_from_config(PRESETS["hybrid-1.3b"](), B200_ENVELOPE["device_bytes"],
+                              **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"})
+    cal = {k: {x: v[x] for x in ("linear", "quadratic", "fixed_ms") if x in v} for k, v in load_default().items()}
+    calibrated = replace(model, operator_calibration=cal)
+    root = Path(__file__).resolve().parents[1] / "prism_cp_b200" / "planner" / "data"
+    recs = json.loads((root / "b200_module_records.json").read_text())
+    for key, sym in (("gqa", "*"), ("gdn", "G"), ("mlp", "M")):
+        for r in recs[key]["records"]:
+            if r.get("sequences", 1) != 1:
+                continue
+            ev = Evaluator(calibrated, {0: r["tokens"]}, 1, "G*")
+            ms, _, _ = ev.operator(sym, Layout((Group((0,), (0,)),), "zigzag"))
+            assert abs(ms - r["fb_ms"]) <= 0.2 * r["fb_ms"] + 0.5, (sym, r["tokens"], ms, r["fb_ms"])
+    # the uncalibrated envelope is much more optimistic for the GDN recurrence
+    ev0 = Evaluator(model, {0: 32768}, 1, "G*")
+    ms0, _, _ = ev0.operator("G", Layout((Group((0,), (0,)),), "zigzag"))
+    assert ms0 < 0.5 * [r for r in recs["gdn"]["records"] if r["tokens"] == 32768 and r["sequences"] == 1][0]["fb_ms"]
