@@ -239,11 +239,11 @@ __global__ void conv_fwd_vec_kernel(const __nv_bfloat16* __restrict__ x, long xs
 
 // Token-parallel forward: thread (channel group, token) computes one 8-channel output row
 // from its four taps. A warp covers 32 consecutive channel groups of one token (512
-// contiguous bytes per row); a block covers 32 channel groups x 32 tokens, each thread
-// 4 tokens 8 apart. No sequential chain, so every load is independent and in flight
+// contiguous bytes per row); a block covers 32 channel groups x 128 tokens, each thread
+// 16 tokens 8 apart, four at a time. No sequential chain, so every load is independent and in flight
 // at once; the taps' rows are shared through L1/L2, DRAM traffic stays one read of x
 // and one write of y.
-constexpr int kConvTokP = 32;
+constexpr int kConvTokP = 128;
 constexpr bool kConvTokenParallel = true;  // false: the sequential 256-token form above
 
 __global__ void __launch_bounds__(256) conv_fwd_tok_kernel(const __nv_bfloat16* __restrict__ x, long xs,
@@ -266,10 +266,10 @@ __global__ void __launch_bounds__(256) conv_fwd_tok_kernel(const __nv_bfloat16* 
       for (int e = 0; e < 8; ++e) wk[2 * q + e / 4][e % 4] = f[e];
     }
   }
-#pragma unroll
+#pragma unroll 4
   for (int k = 0; k < kConvTokP / 8; ++k) {
     const int t = blockIdx.x * kConvTokP + tt + 8 * k;
-    if (t >= T) break;
+    if (t >= T) continue;  // predicated, so the unrolled iterations' loads can all be in flight
     const int seg = find_segment(cu, nseg, t);
     const int start = cu[seg];
     float acc[8];
