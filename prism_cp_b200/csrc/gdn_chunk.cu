@@ -653,6 +653,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         for (int m = 0; m < 4; ++m) {
           const uint4 pk = pack8u(r + 8 * m);
           *reinterpret_cast<uint4*>(blk + swz(vl, (q4 & 1) * 4 + m)) = pk;
+          if (p.states != nullptr) reinterpret_cast<uint4*>(p.states + (ch * DV + v) * DK + q4 * 32)[m] = pk;
         }
 #pragma unroll
         for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * gm);
@@ -662,16 +663,6 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
       fence_proxy_async();
       tc_fence_before();
       mbar_arrive(a1_ready);
-      if (p.states != nullptr) {
-        // the bf16 state rows go to HBM from the A1 copy while the tensor cores read it (A1 is
-        // rewritten only after s_ready of this chunk), off the chunk-to-chunk critical path
-        uint4* dst = reinterpret_cast<uint4*>(p.states + (ch * DV + v) * DK);
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-#pragma unroll
-          for (int m = 0; m < 4; ++m)
-            dst[q4 * 4 + m] = *reinterpret_cast<const uint4*>(A1 + (q4 >> 1) * 16384 + swz(vl, (q4 & 1) * 4 + m));
-      }
       if (!BWD && want_out && j > 0) {
         drain_out(j - 1);
         tc_fence_before();
@@ -704,16 +695,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
       for (int m = 0; m < 8; ++m) {
         const uint4 pk = pack8(d + 8 * m);
         *reinterpret_cast<uint4*>(A2 + swz(vl, m)) = pk;
+        if (p.rows != nullptr) reinterpret_cast<uint4*>(p.rows + (ch * DV + v) * C)[m] = pk;
       }
       fence_proxy_async();
       tc_fence_before();
       mbar_arrive(a2_ready);
-      if (p.rows != nullptr) {
-        // same for the Delta rows: A2 is rewritten only in the next chunk
-        uint4* dst = reinterpret_cast<uint4*>(p.rows + (ch * DV + v) * C);
-#pragma unroll
-        for (int m = 0; m < 8; ++m) dst[m] = *reinterpret_cast<const uint4*>(A2 + swz(vl, m));
-      }
     }
     if (nch == 0 && p.S_out != nullptr) {
       // an empty sequence leaves its state unchanged
