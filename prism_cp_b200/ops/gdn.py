@@ -269,13 +269,13 @@ class _FusedChunkRule(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, q, k, v, g, beta, layout, scale, S0):
+    def forward(ctx, q, k, v, g, beta, layout, scale, S0, keep_intermediates):
         L = lib()
         bf = torch.bfloat16
         qb, kb, vb = (t.to(bf).contiguous() for t in (q, k, v))
         gf, bt = g.float().contiguous(), beta.float().contiguous()
         st = status(q.device)
-        keep = SAVE_INTERMEDIATES and any(ctx.needs_input_grad[:5])
+        keep = keep_intermediates and any(ctx.needs_input_grad[:5])
         Wn, U, Kd, Qg, Aqk, gam, Gc, aux = L.gdn_chunk_prep(qb, kb, vb, gf, bt, layout.tok0_dev, layout.len_dev,
                                                             scale, keep, st)
         T, H, DV = vb.shape
@@ -342,16 +342,21 @@ class _FusedChunkRule(torch.autograd.Function):
         dq, dk, dv, dg, dbeta = L.gdn_chunk_bwd_local(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, Gc, aux, states,
                                                       dstates, rows, drows, dob, ctx.scale, st)
         tq, tk, tv, tg, tb = ctx.dtypes
-        return dq.to(tq), dk.to(tk), dv.to(tv), dg.to(tg), dbeta.to(tb), None, None, dS0
+        return dq.to(tq), dk.to(tk), dv.to(tv), dg.to(tg), dbeta.to(tb), None, None, dS0, None
 
 
 def fused_gated_delta_rule(q, k, v, g, beta, layout: ChunkLayout, scale: float | None = None,
-                           initial_state: torch.Tensor | None = None):
-    """``(o, final_state)`` of the chunked gated delta rule on the fused sm_100a kernels."""
+                           initial_state: torch.Tensor | None = None, keep_intermediates: bool | None = None):
+    """``(o, final_state)`` of the chunked gated delta rule on the fused sm_100a kernels.
+
+    ``keep_intermediates`` (default: on unless ``PRISM_GDN_SAVE=0``) keeps the forward's prep
+    outputs and per-chunk states for the backward; auxiliary passes that only feed a small state
+    (the CP tail state and transition map) pass False and are recomputed in the backward."""
     if not fused_supported(q, v):
         raise ValueError("fused gated delta rule needs CUDA tensors with dk = 128 and dv in {128, 256}")
     scale = q.shape[-1] ** -0.5 if scale is None else scale
-    return _FusedChunkRule.apply(q, k, v, g, beta, layout, scale, initial_state)
+    keep = SAVE_INTERMEDIATES if keep_intermediates is None else bool(keep_intermediates)
+    return _FusedChunkRule.apply(q, k, v, g, beta, layout, scale, initial_state, keep)
 
 
 def naive_gated_delta_rule(q, k, v, g, beta, lengths, scale=None, initial_state=None):

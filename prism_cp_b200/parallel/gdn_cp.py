@@ -163,11 +163,13 @@ def delta_rule_cp(ctx, q, k, v, g, beta):
     if fused and last_cont:
         # tail state from zero, and (for a single continuing segment) the linear
         # map of the incoming state: the recurrence with zero values from I
-        _, S_zero = fused_gated_delta_rule(q, k, v, g, beta, layout)
+        # these passes only feed a small state: recomputed in the backward rather than kept
+        _, S_zero = fused_gated_delta_rule(q, k, v, g, beta, layout, keep_intermediates=False)
         F_tail = S_zero[nseg - 1]
         if first_cont and single:
             eye = torch.eye(DK, dtype=f32, device=q.device).expand(nseg, H, DK, DK).contiguous()
-            _, M_all = fused_gated_delta_rule(q, k, torch.zeros_like(q), g, beta, layout, initial_state=eye)
+            _, M_all = fused_gated_delta_rule(q, k, torch.zeros_like(q), g, beta, layout, initial_state=eye,
+                                              keep_intermediates=False)
             M_tail = M_all[nseg - 1]
         else:
             M_tail = torch.zeros((H, DK, DK), dtype=f32, device=q.device)
