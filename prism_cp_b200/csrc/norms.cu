@@ -75,6 +75,39 @@ __global__ void rownorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, long x_s
   }
 }
 
+// Weight-gradient accumulators a lane keeps in registers (8 columns per 256-column chunk): rows
+// of up to kRegChunks * 256 elements sum their dw terms there and reach shared memory once per
+// warp instead of once per row; wider rows add each term to shared memory directly.
+constexpr int kRegChunks = 8;
+
+template <bool HAS_W, bool GATED>
+__device__ __forceinline__ void rownorm_bwd_chunk(const __nv_bfloat16* xr, const __nv_bfloat16* dyr,
+                                                  const __nv_bfloat16* w, const __nv_bfloat16* zr,
+                                                  __nv_bfloat16* dxr, __nv_bfloat16* dzr, int i, float r, float c,
+                                                  float* dwv) {
+  float xf[8], dyf[8], wf[8], zf[8], out[8], dzo[8];
+  load8(xr + i, xf);
+  load8(dyr + i, dyf);
+  if (HAS_W) load8(w + i, wf);
+  if (GATED) load8(zr + i, zf);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float wv = HAS_W ? wf[e] : 1.f;
+    float gate = 1.f;
+    if (GATED) {
+      const float s = sigmoidf_(zf[e]);
+      gate = zf[e] * s;
+      const float dsilu = s * (1.f + zf[e] * (1.f - s));
+      dzo[e] = dyf[e] * xf[e] * r * wv * dsilu;
+    }
+    const float g = dyf[e] * wv * gate;
+    out[e] = g * r - xf[e] * c;
+    if (HAS_W) dwv[e] = dyf[e] * gate * xf[e] * r;
+  }
+  store8(dxr + i, out);
+  if (GATED) store8(dzr + i, dzo);
+}
+
 template <bool HAS_W, bool GATED>
 __global__ void rownorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, long dy_stride,
                                    const __nv_bfloat16* __restrict__ x, long x_stride,
@@ -89,6 +122,12 @@ __global__ void rownorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, long dy
   }
   const int lane = threadIdx.x & 31;
   const int warps_total = gridDim.x * kWarpsPerBlock;
+  const bool reg_acc = HAS_W && n <= kRegChunks * 256;
+  float acc[kRegChunks][8];
+#pragma unroll
+  for (int k = 0; k < kRegChunks; ++k)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[k][e] = 0.f;
   for (int row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); row < rows; row += warps_total) {
     const long tok = row / heads, hd = row % heads;
     const __nv_bfloat16* xr = x + tok * x_stride + hd * n;
@@ -115,31 +154,39 @@ __global__ void rownorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, long dy
     const float c = dot * r * r * r * inv_n;
     __nv_bfloat16* dxr = dx + tok * dx_stride + hd * n;
     __nv_bfloat16* dzr = GATED ? dz + tok * dz_stride + hd * n : nullptr;
-    for (int i = lane * 8; i < n; i += 256) {
-      float xf[8], dyf[8], wf[8], zf[8], out[8], dzo[8];
-      load8(xr + i, xf);
-      load8(dyr + i, dyf);
-      if (HAS_W) load8(w + i, wf);
-      if (GATED) load8(zr + i, zf);
+    if (reg_acc) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float wv = HAS_W ? wf[e] : 1.f;
-        float gate = 1.f;
-        if (GATED) {
-          const float s = sigmoidf_(zf[e]);
-          gate = zf[e] * s;
-          const float dsilu = s * (1.f + zf[e] * (1.f - s));
-          dzo[e] = dyf[e] * xf[e] * r * wv * dsilu;
+      for (int k = 0; k < kRegChunks; ++k) {
+        const int i = lane * 8 + k * 256;
+        if (i < n) {
+          float dwv[8];
+          rownorm_bwd_chunk<HAS_W, GATED>(xr, dyr, w, zr, dxr, dzr, i, r, c, dwv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[k][e] += dwv[e];
         }
-        const float g = dyf[e] * wv * gate;
-        out[e] = g * r - xf[e] * c;
-        if (HAS_W) atomicAdd(&dw_s[i + e], dyf[e] * gate * xf[e] * r);
       }
-      store8(dxr + i, out);
-      if (GATED) store8(dzr + i, dzo);
+    } else {
+      for (int i = lane * 8; i < n; i += 256) {
+        float dwv[8];
+        rownorm_bwd_chunk<HAS_W, GATED>(xr, dyr, w, zr, dxr, dzr, i, r, c, dwv);
+        if (HAS_W) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) atomicAdd(&dw_s[i + e], dwv[e]);
+        }
+      }
     }
   }
   if (HAS_W) {
+    if (reg_acc) {
+#pragma unroll
+      for (int k = 0; k < kRegChunks; ++k) {
+        const int i = lane * 8 + k * 256;
+        if (i < n) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) atomicAdd(&dw_s[i + e], acc[k][e]);
+        }
+      }
+    }
     __syncthreads();
     for (int i = threadIdx.x; i < n; i += blockDim.x) dw_partial[(long)blockIdx.x * n + i] = dw_s[i];
   }
