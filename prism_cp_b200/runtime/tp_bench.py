@@ -1,7 +1,7 @@
 """Timing of the tensor-parallel GEMM + all-reduce: fused kernel vs GEMM + NCCL.
 
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m prism_cp_b200.runtime.tp_bench \\
-        --m 16384 --n 4096 --k 2048
+        --tokens 16384 --out-features 4096 --in-features 2048
 
 Every rank holds a [M, K] bf16 shard of the activations and a [N, K] shard of the
 weight (a row-parallel linear: the 7B hybrid's attention output projection at
@@ -53,9 +53,10 @@ def _time(fn, iters: int, warmup: int) -> float:
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--m", type=int, default=16384)
-    ap.add_argument("--n", type=int, default=4096)
-    ap.add_argument("--k", type=int, default=2048)
+    # (long names: torchrun would take --m / --n / --k for abbreviations of its own options)
+    ap.add_argument("--tokens", dest="m", type=int, default=16384)
+    ap.add_argument("--out-features", dest="n", type=int, default=4096)
+    ap.add_argument("--in-features", dest="k", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     args = ap.parse_args(argv)
