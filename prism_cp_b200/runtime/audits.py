@@ -16,6 +16,7 @@
 from __future__ import annotations
 
 import contextlib
+import time
 import traceback
 
 import torch
@@ -80,18 +81,28 @@ class AccumulationAudit:
 
     def __init__(self):
         self.events: list[tuple] = []
+        self.times: list[int] = []      # host nanoseconds of each event (the bucket timeline)
+
+    def _add(self, ev: tuple):
+        self.events.append(ev)
+        self.times.append(time.perf_counter_ns())
 
     def backward(self, microbatch: int):
-        self.events.append(("backward", microbatch))
+        self._add(("backward", microbatch))
 
     def reduce_scatter(self, nbytes: int):
-        self.events.append(("reduce_scatter", nbytes))
+        self._add(("reduce_scatter", nbytes))
 
     def optimizer_step(self):
-        self.events.append(("optimizer_step",))
+        self._add(("optimizer_step",))
 
     def all_gather(self, nbytes: int):
-        self.events.append(("all_gather", nbytes))
+        self._add(("all_gather", nbytes))
+
+    def timeline(self) -> list[dict]:
+        t0 = self.times[0] if self.times else 0
+        return [{"event": ev[0], "arg": ev[1] if len(ev) > 1 else None, "host_ns": t - t0}
+                for ev, t in zip(self.events, self.times)]
 
     def check(self, microbatches: int, loss_tokens: int | None = None, observed_loss_tokens: int | None = None):
         kinds = [e[0] for e in self.events]

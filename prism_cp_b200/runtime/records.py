@@ -29,6 +29,86 @@ class StepRecorder:
             f.write(json.dumps(record, sort_keys=True) + "\n")
 
 
+class RunRecords:
+    """The auxiliary per-run records beside ``steps_rank*.jsonl``.
+
+    * ``model_inventory.json`` (rank 0, once): every parameter's name, shape, dtype,
+      element count and whether it is replicated across a tensor-parallel group;
+    * ``mixed_execution.jsonl`` (rank 0, per update): for every microbatch the ingress
+      groups (ranks, samples, mode) and the CP degrees of each layer's attention and MLP
+      layouts;
+    * ``buckets_rank{R}.jsonl``: the optimizer buckets (element range, members, bytes)
+      and the update's reduce-scatter / all-gather payloads;
+    * ``timeline_rank{R}.jsonl``: the accumulation audit's events with host nanoseconds
+      (backward per microbatch, bucket reduce-scatters, the update, all-gathers);
+    * ``optimizer_memory_rank{R}.jsonl``: bytes of the fp32 master shard, Adam moments,
+      gradient shard, bf16 shard and the flat parameter / gradient buffers;
+    * ``numerics_rank{R}.jsonl``: the outcome of the optimizer-shard and logical gates.
+
+    Same files as the reference's runtime and accumulation audit write
+    (experiments/sequence_dynamic_cp/runtime.py:197-208,315-336;
+    accumulation_audit.py:31-39,158-167).
+    """
+
+    def __init__(self, output: str | Path, rank: int):
+        self.root = Path(output)
+        self.root.mkdir(parents=True, exist_ok=True)
+        self.rank = rank
+        self._inventory_done = False
+
+    def _append(self, name: str, record: dict) -> None:
+        with (self.root / name).open("a") as f:
+            f.write(json.dumps(record, sort_keys=True) + "\n")
+
+    def model_inventory(self, model) -> None:
+        if self.rank != 0 or self._inventory_done:
+            return
+        params = [{"name": n, "shape": list(p.shape), "dtype": str(p.dtype).replace("torch.", ""),
+                   "numel": p.numel(), "tp_replicated": bool(getattr(p, "tp_replicated", False))}
+                  for n, p in model.named_parameters()]
+        (self.root / "model_inventory.json").write_text(json.dumps(
+            {"parameters": params, "total_numel": sum(p["numel"] for p in params)}, indent=1))
+        self._inventory_done = True
+
+    @staticmethod
+    def _groups(layout) -> list:
+        return [{"ranks": list(g.ranks), "samples": list(g.samples), "cp": len(g.ranks)} for g in layout.groups]
+
+    def step(self, step: int, trainer, plan) -> None:
+        self.model_inventory(trainer.model)
+        if self.rank == 0:
+            mbs = []
+            for i, mb in enumerate(plan.microbatches):
+                mbs.append({"microbatch": i, "ingress": self._groups(mb.ingress), "mode": mb.ingress.mode,
+                            "layer_cp": [{"attention": sorted({len(g.ranks) for g in a.groups}),
+                                          "mlp": sorted({len(g.ranks) for g in m.groups})} for a, m in mb.layers]})
+            self._append("mixed_execution.jsonl", {"step": step, "microbatches": mbs})
+        opt = trainer.optimizer
+        flat = opt.flat
+        self._append(f"buckets_rank{self.rank}.jsonl", {
+            "step": step, "buckets": [{"index": b, "lo": lo, "hi": hi, "members": len(mem), "bytes": (hi - lo) * 4}
+                                      for b, (lo, hi, mem) in enumerate(flat.buckets)],
+            "reduce_scatter_bytes": opt.stats.get("reduce_scatter_bytes", 0),
+            "all_gather_bytes": opt.stats.get("all_gather_bytes", 0),
+            "overlapped_buckets": opt.stats.get("overlapped_buckets", 0)})
+        if trainer.audit is not None:
+            self._append(f"timeline_rank{self.rank}.jsonl", {"step": step, "events": trainer.audit.timeline()})
+
+        def nbytes(t):
+            return int(t.numel() * t.element_size()) if t is not None else 0
+        self._append(f"optimizer_memory_rank{self.rank}.jsonl", {
+            "step": step, "master": nbytes(opt.master), "exp_avg": nbytes(opt.m), "exp_avg_sq": nbytes(opt.v),
+            "grad_shard": nbytes(opt.grad_shard), "param_shard_bf16": nbytes(opt.shard_bf16),
+            "flat_params": nbytes(flat.flat), "flat_grads": nbytes(flat.grad)})
+        gates = {}
+        if trainer.numerics is not None:
+            gates["optimizer"] = {"mode": trainer.numerics.mode, "failures": len(trainer.numerics.failures)}
+        if trainer.logical is not None:
+            gates["logical"] = {"mode": trainer.logical.mode, "failures": len(trainer.logical.failures)}
+        if gates:
+            self._append(f"numerics_rank{self.rank}.jsonl", {"step": step, **gates})
+
+
 def step_record(step: int, loss: float, grad_norm: float, elapsed_ms: float, local_ms: float, *, tokens: int,
                 loss_tokens: int, samples: int, microbatches: int, peak_allocated: int, peak_reserved: int,
                 memory_budget: int, memory_required: int, admitted: bool, external_before: int = 0,

@@ -26,7 +26,7 @@ from .audits import AccumulationAudit
 from .batch import GlobalBatch, HostInputs, local_inputs
 from .executor import LayoutCache, MicrobatchRun
 from .optimizer import DistributedAdamW, FlatParameters
-from .records import StepRecorder, step_record
+from .records import RunRecords, StepRecorder, step_record
 from ..utils import watchdog
 from ..utils.tracing import nvtx
 
@@ -76,6 +76,7 @@ class Trainer:
         self.hbm_guard = hbm_guard and device.type == "cuda"
         self.loss_acc = torch.zeros((), dtype=torch.float32, device=device)
         self.recorder = StepRecorder(records, self.rank) if records else None
+        self.run_records = RunRecords(records, self.rank) if records else None
         self.numerics = numerics
         self.logical = logical
         self.audit = AccumulationAudit() if audit else None
@@ -168,6 +169,7 @@ class Trainer:
         t0 = time.perf_counter()
         if self.audit is not None:
             self.audit.events.clear()
+            self.audit.times.clear()
         self.flat.zero_grad()
         loss = self.forward_backward(batch.lengths, plan, inputs)
         if self.logical is not None:
@@ -199,6 +201,8 @@ class Trainer:
                 memory_budget=mem.get("budget", 0), memory_required=mem.get("required", 0), admitted=admitted,
                 external_before=external_before, external_after=mem.get("external", 0),
                 sync=dict(self.optimizer.stats), finite=finite_ok))
+        if self.run_records is not None:
+            self.run_records.step(self.step_index, self, plan)
         if not finite_ok:
             raise FloatingPointError("non-finite loss or gradient norm in training step")
         if not admitted:

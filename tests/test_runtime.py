@@ -159,3 +159,24 @@ def test_logical_gate_flags_a_different_model(tmp_path):
     assert not step(0, "read").failures
     with pytest.raises(AssertionError, match="logical numerics gate failed"):
         step(1, "read")
+
+
+def test_auxiliary_run_records(tmp_path):
+    """Inventory, mixed-execution, bucket, timeline and optimizer-memory records beside the step records."""
+    tr, batch, plan = _trainer(tmp_path, records=str(tmp_path), audit=True)
+    for _ in range(2):
+        tr.train_step(batch, plan)
+    inv = json.loads((tmp_path / "model_inventory.json").read_text())
+    assert inv["total_numel"] == sum(p.numel() for p in tr.model.parameters())
+    mixed = [json.loads(x) for x in (tmp_path / "mixed_execution.jsonl").read_text().splitlines()]
+    assert [m["step"] for m in mixed] == [1, 2]
+    assert len(mixed[0]["microbatches"]) == len(plan.microbatches)
+    assert len(mixed[0]["microbatches"][0]["layer_cp"]) == len(tr.model.cfg.pattern)
+    buckets = [json.loads(x) for x in (tmp_path / "buckets_rank0.jsonl").read_text().splitlines()]
+    assert buckets[-1]["buckets"] and buckets[-1]["buckets"][0]["bytes"] > 0
+    timeline = [json.loads(x) for x in (tmp_path / "timeline_rank0.jsonl").read_text().splitlines()]
+    events = [e["event"] for e in timeline[-1]["events"]]
+    assert events.count("backward") == len(plan.microbatches) and "optimizer_step" in events
+    assert all(b["host_ns"] >= a["host_ns"] for a, b in zip(timeline[-1]["events"], timeline[-1]["events"][1:]))
+    mem = [json.loads(x) for x in (tmp_path / "optimizer_memory_rank0.jsonl").read_text().splitlines()]
+    assert mem[-1]["master"] == mem[-1]["exp_avg"] == mem[-1]["exp_avg_sq"] > 0
