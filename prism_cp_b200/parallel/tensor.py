@@ -13,10 +13,11 @@ group; attention/GDN heads and the MLP's hidden units are split:
 * ``row_linear(x_shard, w_shard)``: sharded input, partial outputs summed over
   the group (all-reduce in the forward, identity backward).
 
-On CUDA both sums are fused into the GEMM that produces them
-(``tp_fused.FusedAllReduceGemm``: the tcgen05 kernel exchanges partial tiles and
-finished tiles over NVLink peer memory while it computes). Elsewhere (CPU,
-gloo, odd widths) they run as reduce-scatter + all-gather (``dist``). Parameters owned by a shard reduce their gradients only over the
+The sums run as reduce-scatter + all-gather (``dist``; NCCL over NVLink on
+CUDA). With ``PRISM_TP_FUSED=1`` they are fused into the GEMM that produces them
+instead (``tp_fused.FusedAllReduceGemm``: the tcgen05 kernel exchanges partial
+and finished tiles over NVLink peer memory while it computes); that form is
+correct but measured slower, see ``tp_fused``. Parameters owned by a shard reduce their gradients only over the
 ranks of the same TP index; replicated parameters (norms, embedding, head,
 per-value-dim norm weights) reduce over the whole world.
 """
