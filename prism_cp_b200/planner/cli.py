@@ -189,6 +189,16 @@ def cmd_native(args) -> int:
     return 0
 
 
+def resolve_pattern(args) -> None:
+    """A plan covers the model's own layers: the preset's pattern unless one is given."""
+    if getattr(args, "pattern", "unset") is None:
+        if getattr(args, "model_config", None):
+            from ..models.config import PRESETS
+            args.pattern = PRESETS[args.model_config]().pattern
+        else:
+            args.pattern = "GGG*GGG*"
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="prism_cp_b200.planner.cli", description=__doc__.splitlines()[0])
     sub = ap.add_subparsers(dest="command", required=True)
@@ -197,7 +207,8 @@ def main(argv=None) -> int:
     s.add_argument("--manifest", type=Path, required=True)
     s.add_argument("--output", type=Path, required=True)
     s.add_argument("--world", type=int, default=8)
-    s.add_argument("--pattern", default="GGG*GGG*")
+    s.add_argument("--pattern", default=None,
+                   help="layer pattern (default: the --model-config preset's, else GGG*GGG*)")
     s.add_argument("--updates", type=int, default=3)
     _search_args(s)
     _model_args(s)
@@ -207,7 +218,8 @@ def main(argv=None) -> int:
     sc.add_argument("--output", type=Path, required=True)
     sc.add_argument("--cases", nargs="+", required=True)
     sc.add_argument("--world", type=int, default=8)
-    sc.add_argument("--pattern", default="GGG*GGG*")
+    sc.add_argument("--pattern", default=None,
+                   help="layer pattern (default: the --model-config preset's, else GGG*GGG*)")
     _search_args(sc)
     _model_args(sc)
     sc.set_defaults(fn=cmd_scale)
@@ -217,7 +229,8 @@ def main(argv=None) -> int:
     au.add_argument("--case", required=True)
     au.add_argument("--output", type=Path, required=True)
     au.add_argument("--world", type=int, default=8)
-    au.add_argument("--pattern", default="GGG*GGG*")
+    au.add_argument("--pattern", default=None,
+                   help="layer pattern (default: the --model-config preset's, else GGG*GGG*)")
     au.add_argument("--max-attention-cp", type=int)
     au.add_argument("--memory-time-tolerance", type=float, default=0.001)
     _model_args(au)
@@ -227,7 +240,8 @@ def main(argv=None) -> int:
     st.add_argument("--manifest", type=Path, required=True)
     st.add_argument("--output", type=Path, required=True)
     st.add_argument("--world", type=int, default=8)
-    st.add_argument("--pattern", default="GGG*GGG*")
+    st.add_argument("--pattern", default=None,
+                   help="layer pattern (default: the --model-config preset's, else GGG*GGG*)")
     st.add_argument("--capacities", type=int, nargs="+", default=[8192, 16384, 24576, 32768, 40960])
     st.add_argument("--reference-capacity", type=int, default=16384)
     st.add_argument("--alpha", type=float, default=2.0)
@@ -239,7 +253,8 @@ def main(argv=None) -> int:
     nv.add_argument("--manifest", type=Path, required=True)
     nv.add_argument("--output", type=Path, required=True)
     nv.add_argument("--world", type=int, default=8)
-    nv.add_argument("--pattern", default="GGG*GGG*")
+    nv.add_argument("--pattern", default=None,
+                   help="layer pattern (default: the --model-config preset's, else GGG*GGG*)")
     nv.add_argument("--capacity", type=int, default=16384)
     _model_args(nv)
     nv.set_defaults(fn=cmd_native)
@@ -256,6 +271,7 @@ def main(argv=None) -> int:
     ho.set_defaults(fn=lambda a: __import__("prism_cp_b200.planner.handoff", fromlist=["main"]).main(a.rest))
 
     args = ap.parse_args(argv)
+    resolve_pattern(args)
     return int(args.fn(args) or 0)
 
 

@@ -13,19 +13,22 @@ def test_prepare_run_summarize_cpu(tmp_path):
     mpath = tmp_path / "m.json"
     mpath.write_text(json.dumps(manifest))
     out = tmp_path / "runs"
-    arms = matrix.prepare(mpath, out, world=2, arms=("fixed", "native"), model="hybrid-tiny", capacity=512,
-                          updates=2, device="cpu")
-    assert set(arms) == {"fixed", "native"}
+    arms = matrix.prepare(mpath, out, world=2, arms=("fixed", "native", "joint"), model="hybrid-tiny",
+                          capacity=512, updates=2, device="cpu")
+    assert set(arms) == {"fixed", "native", "joint"}
+    # the joint planner plans the preset's own layers
+    result = json.loads((out / "arms" / "joint" / "plan" / "result.json").read_text())
+    assert result["plan"]["pattern"] == "GGG*"
     assert (out / "arms" / "native" / "native_replay.json").exists()
     with pytest.raises(FileExistsError):
         matrix.prepare(mpath, out, world=2, arms=("fixed",), model="hybrid-tiny", device="cpu")
-    for i, arm in enumerate(("fixed", "native")):
+    for i, arm in enumerate(("fixed", "native", "joint")):
         res = matrix.run(out, arm, ["localhost"], nproc_per_node=2, transport="local", timeout_s=240,
                          master_port=29650 + i)
         assert res.status == "ok", (out / "arms" / arm / "launch" / "node0.log").read_text()[-3000:]
         assert (out / "arms" / arm / "run" / "protocol.json").exists()
     comp = matrix.summarize(out)
-    for arm in ("fixed", "native"):
+    for arm in ("fixed", "native", "joint"):
         assert comp[arm]["launch"] == "ok"
         assert comp[arm]["status"] in ("complete", "actual_memory_guard_rejected"), comp
     sup = json.loads((out / "supervision.json").read_text())
