@@ -49,7 +49,7 @@ def build_parser() -> argparse.ArgumentParser:
     c.add_argument("--dynamic-context-parallel", action="store_true")
     c.add_argument("--min-dynamic-context-parallel-size", type=int, default=1)
     c.add_argument("--sequence-packing-scheduler", default="default_dynamic_cp",
-                   choices=("default_dynamic_cp", "joint", "fixed"))
+                   choices=("default_dynamic_cp", "joint", "fixed", "online"))
     c.add_argument("--gdn-preserve-parent-contiguous", action="store_true")
     c.add_argument("--max-seqlen-per-dp-cp-rank", type=int, default=32768)
     c.add_argument("--joint-replay", default=None, help="replay.json from the joint planner")

@@ -60,6 +60,24 @@ def global_batch(args, world: int, step: int, pin: bool):
                       pin=pin)
 
 
+_PLANNER_MODEL: dict = {}
+
+
+def _planner_model(args, world: int):
+    """The planner's cost model of this run's model shape on B200 (calibrated operator costs)."""
+    key = world
+    if key not in _PLANNER_MODEL:
+        from dataclasses import replace
+        from ..planner.calibrate import load_default
+        from ..planner.cli import B200_ENVELOPE
+        from ..planner.joint.cost import model_from_config
+        m = model_from_config(model_config(args), B200_ENVELOPE["device_bytes"],
+                              **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"})
+        cal = {k: {x: v[x] for x in ("linear", "quadratic", "fixed_ms") if x in v} for k, v in load_default().items()}
+        _PLANNER_MODEL[key] = replace(m, operator_calibration=cal)
+    return _PLANNER_MODEL[key]
+
+
 def plan_for(args, batch, world: int, pattern: str, step: int, replays):
     if args.sequence_packing_scheduler == "joint":
         row = replays[(step - 1) % len(replays)]
@@ -67,6 +85,15 @@ def plan_for(args, batch, world: int, pattern: str, step: int, replays):
         if list(batch.lengths.values()) != row["expected_lengths"]:
             raise SystemExit("joint replay lengths differ from the batch")
         return plan
+    if args.sequence_packing_scheduler == "online":
+        # per-batch (cp_gdn, cp_gqa) from the calibrated B200 cost model; the dyadic teams already
+        # exist, so a new degree needs no new process group
+        from ..planner.online import select
+        sel = select(batch.lengths, world, pattern, _planner_model(args, world))
+        if step == 1 or step % max(1, args.log_interval) == 0:
+            print(json.dumps({"step": step, "online_cp": {"gdn": sel.cp_gdn, "gqa": sel.cp_gqa},
+                              "predicted_update_ms": round(sel.predicted_update_ms, 3)}), flush=True)
+        return sel.plan
     if args.sequence_packing_scheduler == "fixed":
         cp = args.context_parallel_size or world
         return uniform_plan(batch.lengths, world, cp, args.max_seqlen_per_dp_cp_rank, pattern)

@@ -48,3 +48,11 @@ def test_launcher_tensor_parallel_two_ranks():
 
 def test_launcher_pipeline_parallel_two_ranks():
     _run(TINY + ["--pipeline-model-parallel-size", "2", "--context-parallel-size", "1"])
+
+
+def test_launcher_online_scheduler_two_ranks():
+    """Per-batch CP degrees chosen online by the calibrated cost model, applied on pre-built teams."""
+    argv = [a for a in TINY]
+    i = argv.index("--sequence-packing-scheduler")
+    argv[i + 1] = "online"
+    _run(argv + ["--use-varlen-dataset"])
