@@ -39,6 +39,9 @@ def parse():
     ap.add_argument("--impl", choices=("native", "reference"), default="native")
     ap.add_argument("--model", default="hybrid-1.3b")
     ap.add_argument("--workload", choices=("fixed", "lognormal"), default="fixed")
+    ap.add_argument("--plan", choices=("uniform", "online"), default="uniform",
+                    help="uniform: CP = N for every layer; online: per-batch (cp_gdn, cp_gqa) from the "
+                         "calibrated B200 cost model")
     ap.add_argument("--seqs", type=int, default=8)
     ap.add_argument("--seq-len", type=int, default=32768)
     ap.add_argument("--tokens-per-rank", type=int, default=32768)
@@ -153,7 +156,22 @@ def main():
         workload = {"global_batch_tokens": sum(lengths), "documents": len(lengths), "seq_len": max(lengths),
                     "lengths": "log-normal median 4096 sigma 1.0 clipped 512..131072"}
     batch = make_batch(lengths, cfg.vocab_size, args.seed, pin=True)
-    plan = uniform_plan(batch.lengths, world, world, args.tokens_per_rank, cfg.pattern)
+    plan_desc = f"cp{world}"
+    if args.plan == "online":
+        from dataclasses import replace
+        from prism_cp_b200.planner.calibrate import load_default
+        from prism_cp_b200.planner.cli import B200_ENVELOPE
+        from prism_cp_b200.planner.joint.cost import model_from_config
+        from prism_cp_b200.planner.online import select
+        pm = model_from_config(cfg, B200_ENVELOPE["device_bytes"],
+                               **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"})
+        pm = replace(pm, operator_calibration={k: {x: v[x] for x in ("linear", "quadratic", "fixed_ms") if x in v}
+                                               for k, v in load_default().items()})
+        sel = select(batch.lengths, world, cfg.pattern, pm)
+        plan = sel.plan
+        plan_desc = f"online cp_gdn{sel.cp_gdn} cp_gqa{sel.cp_gqa} over {world}"
+    else:
+        plan = uniform_plan(batch.lengths, world, world, args.tokens_per_rank, cfg.pattern)
 
     model = HybridModel(cfg, dtype=torch.bfloat16, device=device, seed=0)
     teams = Teams(world)
@@ -223,7 +241,7 @@ def main():
             "config": dict(model=f"{cfg.name} ({cfg.num_layers}L {cfg.pattern.count('G')} GDN + "
                                  f"{cfg.pattern.count('*')} GQA, h{cfg.hidden_size}, "
                                  f"{cfg.parameter_count() / 1e9:.2f}B params)",
-                           parallelism=f"cp{world}", workload=args.workload, microbatches=len(plan.microbatches),
+                           parallelism=plan_desc, workload=args.workload, microbatches=len(plan.microbatches),
                            l2="per-step working set (32K-token activations) far exceeds the 126 MB L2",
                            **workload),
             "clocks": clocks.summary(), "e2e": e2e, "gpu_launches": launches * args.steps,
