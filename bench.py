@@ -158,15 +158,12 @@ def main():
     batch = make_batch(lengths, cfg.vocab_size, args.seed, pin=True)
     plan_desc = f"cp{world}"
     if args.plan == "online":
-        from dataclasses import replace
-        from prism_cp_b200.planner.calibrate import load_default
+        from prism_cp_b200.planner.calibrate import calibrated
         from prism_cp_b200.planner.cli import B200_ENVELOPE
         from prism_cp_b200.planner.joint.cost import model_from_config
         from prism_cp_b200.planner.online import select
-        pm = model_from_config(cfg, B200_ENVELOPE["device_bytes"],
-                               **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"})
-        pm = replace(pm, operator_calibration={k: {x: v[x] for x in ("linear", "quadratic", "fixed_ms") if x in v}
-                                               for k, v in load_default().items()})
+        pm = calibrated(model_from_config(cfg, B200_ENVELOPE["device_bytes"],
+                                          **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"}))
         sel = select(batch.lengths, world, cfg.pattern, pm)
         plan = sel.plan
         plan_desc = f"online cp_gdn{sel.cp_gdn} cp_gqa{sel.cp_gqa} over {world}"

@@ -67,14 +67,12 @@ def _planner_model(args, world: int):
     """The planner's cost model of this run's model shape on B200 (calibrated operator costs)."""
     key = world
     if key not in _PLANNER_MODEL:
-        from dataclasses import replace
-        from ..planner.calibrate import load_default
+        from ..planner.calibrate import calibrated
         from ..planner.cli import B200_ENVELOPE
         from ..planner.joint.cost import model_from_config
         m = model_from_config(model_config(args), B200_ENVELOPE["device_bytes"],
                               **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"})
-        cal = {k: {x: v[x] for x in ("linear", "quadratic", "fixed_ms") if x in v} for k, v in load_default().items()}
-        _PLANNER_MODEL[key] = replace(m, operator_calibration=cal)
+        _PLANNER_MODEL[key] = calibrated(m)
     return _PLANNER_MODEL[key]
 
 

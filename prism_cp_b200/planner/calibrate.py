@@ -12,7 +12,9 @@ so ``e_lin`` / ``e_quad`` are the fractions of the envelope the kernels reach
 and ``fixed_ms`` the per-call overhead. The result goes into
 ``Model.operator_calibration``; CP > 1 keeps the analytic communication terms
 (at the measured NVLink bandwidth) unless a measured CP response profile is
-given. The committed ``data/b200_operator_calibration.json`` is fitted to this
+given. ``fit_byte_scale`` does the same for memory: the activation-byte scale at
+which the evaluator's peak of one microbatch equals a measured peak. The
+committed ``data/b200_operator_calibration.json`` holds both, fitted to this
 framework's own kernels on one B200 for the 1.3B shape.
 """
 
@@ -25,7 +27,7 @@ from pathlib import Path
 import numpy as np
 
 from .costfit import nnls_exact
-from .joint.cost import Model
+from .joint.cost import Evaluator, Model
 
 DEFAULT = Path(__file__).resolve().parent / "data" / "b200_operator_calibration.json"
 
@@ -48,8 +50,43 @@ def _analytic_ms(model: Model, symbol: str, tokens: int) -> tuple[float, float]:
 
 
 def load_default() -> dict:
-    """The committed B200 calibration (fitted on the 1.3B shape)."""
+    """The committed B200 operator calibration (fitted on the 1.3B shape)."""
     return json.loads(DEFAULT.read_text())["calibration"]
+
+
+def load_byte_scale() -> float:
+    """The committed activation-byte scale (measured peak of one 32K-token microbatch, 1.3B)."""
+    return float(json.loads(DEFAULT.read_text()).get("byte_scale", 1.0))
+
+
+def calibrated(model: Model) -> Model:
+    """``model`` with the committed operator calibration and activation-byte scale."""
+    from dataclasses import replace
+    cal = {k: {x: v[x] for x in ("linear", "quadratic", "fixed_ms") if x in v} for k, v in load_default().items()}
+    return replace(model, operator_calibration=cal, byte_scale=load_byte_scale())
+
+
+def fit_byte_scale(model: Model, pattern: str, tokens: int, peak_bytes: int) -> float:
+    """Activation-byte scale that makes the evaluator's peak of one CP = 1 microbatch of ``tokens``
+    equal a measured peak (bisection; the peak grows monotonically with the scale)."""
+    from dataclasses import replace
+    from .joint.ir import Group, Layout, Microbatch
+    one = Layout((Group((0,), (0,)),), "zigzag")
+    mb = Microbatch(one, tuple((one, one) for _ in pattern))
+
+    def peak(scale):
+        ev = Evaluator(replace(model, byte_scale=scale), {0: tokens}, 1, pattern)
+        return max(ev.evaluate(mb)["peak_bytes"])
+    lo, hi = 0.05, 20.0
+    if not peak(lo) <= peak_bytes <= peak(hi):
+        raise ValueError("the measured peak is outside what a byte scale can reach")
+    for _ in range(60):
+        mid = 0.5 * (lo + hi)
+        if peak(mid) < peak_bytes:
+            lo = mid
+        else:
+            hi = mid
+    return 0.5 * (lo + hi)
 
 
 def calibrate(records: list[dict], model: Model) -> dict:

@@ -52,10 +52,10 @@ def build_model(args) -> Model:
     else:
         model = Model(**B200_ENVELOPE)
     if not getattr(args, "uncalibrated", False) and getattr(args, "hardware", "B200") == "B200":
-        from .calibrate import load_default
-        model = replace(model, operator_calibration={k: {x: v[x] for x in ("linear", "quadratic", "fixed_ms")
-                                                         if x in v} for k, v in load_default().items()},
-                        provenance=model.provenance + "; operator costs calibrated to measured B200 module times")
+        from .calibrate import calibrated
+        model = replace(calibrated(model),
+                        provenance=model.provenance + "; operator costs and activation bytes calibrated to "
+                                                      "measured B200 module times and peak memory")
     if getattr(args, "cp_response", None):
         profile = json.loads(Path(args.cp_response).read_text())
         model = replace(model, cp_response=profile,

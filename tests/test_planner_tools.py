@@ -155,3 +155,22 @@ def test_b200_operator_calibration_reproduces_module_times():
     ev0 = Evaluator(model, {0: 32768}, 1, "G*")
     ms0, _, _ = ev0.operator("G", Layout((Group((0,), (0,)),), "zigzag"))
     assert ms0 < 0.5 * [r for r in recs["gdn"]["records"] if r["tokens"] == 32768 and r["sequences"] == 1][0]["fb_ms"]
+
+
+def test_b200_calibrated_memory_matches_the_measured_peak():
+    """With the committed byte scale, one 32K-token CP = 1 microbatch of the 1.3B model is priced at the
+    141.15 GiB peak the bench measured, inside the HBM budget; the uncalibrated model underestimates it."""
+    from prism_cp_b200.models.config import PRESETS
+    from prism_cp_b200.planner.calibrate import calibrated
+    from prism_cp_b200.planner.cli import B200_ENVELOPE
+    from prism_cp_b200.planner.joint.cost import Evaluator, model_from_config
+    from prism_cp_b200.planner.joint.ir import Group, Layout, Microbatch
+    cfg = PRESETS["hybrid-1.3b"]()
+    raw = model_from_config(cfg, B200_ENVELOPE["device_bytes"],
+                            **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"})
+    one = Layout((Group((0,), (0,)),), "zigzag")
+    mb = Microbatch(one, tuple((one, one) for _ in cfg.pattern))
+    gib = 2 ** 30
+    peak = max(Evaluator(calibrated(raw), {0: 32768}, 1, cfg.pattern).evaluate(mb)["peak_bytes"]) / gib
+    assert abs(peak - 141.15) < 0.5 and peak * gib <= calibrated(raw).budget
+    assert max(Evaluator(raw, {0: 32768}, 1, cfg.pattern).evaluate(mb)["peak_bytes"]) / gib < 100
