@@ -118,7 +118,16 @@ def select(lengths: dict, world: int, pattern: str, model: Model, degrees=(1, 2,
     """Best (cp_gdn, cp_gqa) plan for this batch under ``model``."""
     degrees = tuple(d for d in degrees if d <= world and world % d == 0)
     if capacity is None:
-        capacity = max(1, model.token_capacity_upper_bound(pattern, world) // world)
+        # the memory model's token ceiling is necessary, not sufficient (CP workspaces come on top):
+        # shrink the per-rank capacity until some candidate fits
+        top = max(1, model.token_capacity_upper_bound(pattern, world) // world)
+        last = None
+        for frac in (1.0, 0.9, 0.8, 0.7, 0.6, 0.5, 0.4, 0.3):
+            try:
+                return select(lengths, world, pattern, model, degrees, max(1, int(top * frac)))
+            except ValueError as err:
+                last = err
+        raise last
     ev = Evaluator(model, lengths, world, pattern)
     rows = []
     best = None
