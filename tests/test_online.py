@@ -31,3 +31,23 @@ def test_long_documents_force_context_parallelism():
     sel = select(lengths, 8, hybrid_1p3b().pattern, model, capacity=32768)
     assert max(sel.cp_gdn, sel.cp_gqa) >= 4
     assert any(r["fits"] for r in sel.candidates)
+
+
+def test_selection_shrinks_capacity_until_a_plan_fits_the_calibrated_memory():
+    """On the calibrated B200 model the token ceiling alone packs microbatches that do not fit;
+    the selector backs off to a smaller per-rank capacity and returns a plan that fits."""
+    from prism_cp_b200.models.config import PRESETS
+    from prism_cp_b200.planner.calibrate import calibrated
+    from prism_cp_b200.planner.cli import B200_ENVELOPE
+    from prism_cp_b200.planner.joint.cost import Evaluator, model_from_config
+    from prism_cp_b200.planner.online import select
+    from prism_cp_b200.runtime.batch import lognormal_lengths
+    cfg = PRESETS["hybrid-1.3b"]()
+    model = calibrated(model_from_config(cfg, B200_ENVELOPE["device_bytes"],
+                                         **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"}))
+    lengths = dict(enumerate(lognormal_lengths(1 << 20, 4096, 1.0, 512, 131072, 8, 1234)))
+    sel = select(lengths, 4, cfg.pattern, model)
+    ev = Evaluator(model, lengths, 4, cfg.pattern)
+    assert all(ev.evaluate(mb)["fits"] for mb in sel.plan.microbatches)
+    placed = sorted(s for mb in sel.plan.microbatches for g in mb.ingress.groups for s in g.samples)
+    assert placed == sorted(lengths)
