@@ -174,3 +174,22 @@ def test_b200_calibrated_memory_matches_the_measured_peak():
     peak = max(Evaluator(calibrated(raw), {0: 32768}, 1, cfg.pattern).evaluate(mb)["peak_bytes"]) / gib
     assert abs(peak - 141.15) < 0.5 and peak * gib <= calibrated(raw).budget
     assert max(Evaluator(raw, {0: 32768}, 1, cfg.pattern).evaluate(mb)["peak_bytes"]) / gib < 100
+
+
+def test_calibrated_planner_prices_the_measured_bench_steps():
+    """The calibrated B200 model's step time for the bench workload (8 x 32K tokens, 1.3B) is within
+    6 % of the measured 5780 ms (one GPU) and 3126 ms (two GPUs, CP = 2)."""
+    from prism_cp_b200.models.config import PRESETS
+    from prism_cp_b200.planner.calibrate import calibrated
+    from prism_cp_b200.planner.cli import B200_ENVELOPE
+    from prism_cp_b200.planner.fixed import uniform_plan
+    from prism_cp_b200.planner.joint.cost import Evaluator, model_from_config
+    cfg = PRESETS["hybrid-1.3b"]()
+    m = calibrated(model_from_config(cfg, B200_ENVELOPE["device_bytes"],
+                                     **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"}))
+    lengths = {i: 32768 for i in range(8)}
+    for world, measured in ((1, 5780.0), (2, 3126.0)):
+        plan = uniform_plan(lengths, world, world, 32768, cfg.pattern)
+        ev = Evaluator(m, lengths, world, cfg.pattern)
+        ms = sum(ev.evaluate(mb)["predicted_ms"] for mb in plan.microbatches)
+        assert abs(ms - measured) <= 0.06 * measured, (world, ms, measured)
