@@ -146,7 +146,7 @@ def main(argv=None) -> int:
                           bucket_bytes=(args.ddp_bucket_size or (64 << 20)) * 4)
     replays = json.loads(Path(args.joint_replay).read_text()) if args.joint_replay else None
     start = 1
-    if pipeline is None and args.load and checkpoint.latest(args.load) is not None:
+    if args.load and checkpoint.latest(args.load) is not None:
         start = checkpoint.load(trainer, checkpoint.latest(args.load)) + 1
     enable_nvtx(args.nvtx_ranges or nvtx_enabled())
     window = ProfileWindow(args.profile_step_start, args.profile_step_end, args.profile_ranks, rank,
@@ -161,7 +161,7 @@ def main(argv=None) -> int:
         if rank == 0 and step % args.log_interval == 0:
             print(json.dumps({"step": step, "loss": res.loss, "lr": res.lr, "tokens": res.tokens,
                               "microbatches": res.microbatches}), flush=True)
-        if pipeline is None and args.save and args.save_interval and step % args.save_interval == 0:
+        if args.save and args.save_interval and step % args.save_interval == 0:
             checkpoint.save(trainer, args.save, plan_cursor=step)
     if world > 1:
         dist.barrier()

@@ -2,8 +2,8 @@
 
 A checkpoint directory holds, via ``torch.distributed.checkpoint.save``:
   * ``model``     - the bf16 model state (replicated on every rank, written once);
-  * ``optimizer`` - each rank's fp32 master / Adam shard, keyed by rank so a
-    resume on the same world size restores it exactly;
+  * ``optimizer`` - each rank's fp32 master / Adam shard, keyed by rank (and by
+    pipeline stage) so a resume on the same world size restores it exactly;
   * ``meta``      - step, scheduler position, plan cursor and RNG states.
 Reference: Megatron ``--ckpt-format torch_dist --save --save-interval``
 (scripts/run_manual_gdn_cp_case.sh:379,395-397), which the reference exposes
@@ -19,14 +19,27 @@ import torch.distributed as dist
 import torch.distributed.checkpoint as dcp
 
 
+def _keys(trainer) -> tuple[str, str]:
+    """(model key prefix, optimizer / RNG shard name) of this rank.
+
+    A pipeline stage holds only its own layers, numbered from 0 inside the stage, and its optimizer
+    ranks count from 0 inside the stage: both are qualified by the stage so that the stages of one
+    run write disjoint entries of the same checkpoint."""
+    opt = trainer.optimizer
+    info = getattr(trainer, "info", None)
+    if info is not None and getattr(info, "pp", 1) > 1:
+        return f"stage{info.stage}.", f"stage{info.stage}_rank{opt.rank}"
+    return "", f"rank{opt.rank}"
+
+
 def _state(trainer, plan_cursor: int) -> dict:
     opt = trainer.optimizer
-    rank = opt.rank
-    return {"model": {k: v for k, v in trainer.model.state_dict().items()},
-            "optimizer": {f"rank{rank}": {"master": opt.master, "m": opt.m, "v": opt.v}},
+    prefix, shard = _keys(trainer)
+    return {"model": {prefix + k: v for k, v in trainer.model.state_dict().items()},
+            "optimizer": {shard: {"master": opt.master, "m": opt.m, "v": opt.v}},
             "meta": {"step": torch.tensor(opt.step_count), "plan_cursor": torch.tensor(plan_cursor),
                      "world": torch.tensor(opt.world),
-                     f"cpu_rng_rank{rank}": torch.get_rng_state()}}
+                     f"cpu_rng_{shard}": torch.get_rng_state()}}
 
 
 def save(trainer, directory: str | Path, plan_cursor: int = 0) -> Path:
@@ -51,12 +64,13 @@ def load(trainer, path: str | Path) -> int:
     opt = trainer.optimizer
     if int(state["meta"]["world"]) != opt.world:
         raise ValueError("checkpoint world size differs from the current run")
-    trainer.model.load_state_dict(state["model"])
-    shard = state["optimizer"][f"rank{opt.rank}"]
-    opt.master.copy_(shard["master"])
-    opt.m.copy_(shard["m"])
-    opt.v.copy_(shard["v"])
+    prefix, shard = _keys(trainer)
+    trainer.model.load_state_dict({k[len(prefix):]: v for k, v in state["model"].items()})
+    saved = state["optimizer"][shard]
+    opt.master.copy_(saved["master"])
+    opt.m.copy_(saved["m"])
+    opt.v.copy_(saved["v"])
     opt.step_count = int(state["meta"]["step"])
     trainer.step_index = opt.step_count
-    torch.set_rng_state(state["meta"][f"cpu_rng_rank{opt.rank}"])
+    torch.set_rng_state(state["meta"][f"cpu_rng_{shard}"])
     return int(state["meta"]["plan_cursor"])

@@ -485,3 +485,41 @@ def _mixed_case(rank, world):
 
 def test_heterogeneous_cp_in_one_microbatch_matches_cp1():
     run_ranks(_mixed_case, 4, timeout=600)
+
+
+# ------------------------------------------------------------------ pipeline checkpoint / resume
+def _pp_resume_case(rank, world, ck):
+    from prism_cp_b200.models.config import hybrid_tiny
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.planner.fixed import uniform_plan
+    from prism_cp_b200.runtime import checkpoint
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.pipeline import PipelineTrainer, make_stage
+    cfg = hybrid_tiny()
+    pp = world
+    batch = make_batch([512, 256, 256], cfg.vocab_size, seed=3)
+    plan = uniform_plan(batch.lengths, 1, 1, 512, cfg.pattern)
+    info = make_stage(pp, cfg.num_layers)
+
+    def fresh():
+        model = HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0,
+                            layers=range(info.first_layer, info.first_layer + info.num_layers),
+                            pre_process=info.stage == 0, post_process=info.stage == pp - 1)
+        return PipelineTrainer(model, info, torch.device("cpu"), lr=1e-3)
+
+    straight = fresh()
+    want = [straight.train_step(batch, plan).loss for _ in range(3)]
+    first = fresh()
+    for _ in range(2):
+        first.train_step(batch, plan)
+    checkpoint.save(first, ck, plan_cursor=2)
+    dist.barrier()
+    resumed = fresh()
+    cursor = checkpoint.load(resumed, checkpoint.latest(ck))
+    assert cursor == 2 and resumed.optimizer.step_count == 2
+    got = resumed.train_step(batch, plan).loss
+    assert abs(got - want[2]) <= 1e-5 * abs(want[2]), (got, want)
+
+
+def test_pipeline_checkpoint_resume_matches_uninterrupted_run(tmp_path):
+    run_ranks(_pp_resume_case, 2, str(tmp_path / "ck"))
