@@ -23,12 +23,17 @@ def _keys(trainer) -> tuple[str, str]:
     """(model key prefix, optimizer / RNG shard name) of this rank.
 
     A pipeline stage holds only its own layers, numbered from 0 inside the stage, and its optimizer
-    ranks count from 0 inside the stage: both are qualified by the stage so that the stages of one
-    run write disjoint entries of the same checkpoint."""
+    ranks count from 0 inside the stage; a tensor-parallel index holds its own weight shards under
+    the layer names every index uses. Both are qualified (by stage, by TP index) so that all ranks
+    of one run write disjoint entries of the same checkpoint."""
     opt = trainer.optimizer
     info = getattr(trainer, "info", None)
     if info is not None and getattr(info, "pp", 1) > 1:
         return f"stage{info.stage}.", f"stage{info.stage}_rank{opt.rank}"
+    tp = getattr(trainer, "tp", None)
+    if tp is not None and tp.enabled:
+        # each tensor-parallel index holds its own shard of the weights under the same names
+        return f"tp{tp.index}.", f"tp{tp.index}_rank{opt.rank}"
     return "", f"rank{opt.rank}"
 
 

@@ -523,3 +523,38 @@ def _pp_resume_case(rank, world, ck):
 
 def test_pipeline_checkpoint_resume_matches_uninterrupted_run(tmp_path):
     run_ranks(_pp_resume_case, 2, str(tmp_path / "ck"))
+
+
+def _tp_resume_case(rank, world, ck):
+    from prism_cp_b200.models.config import hybrid_tiny
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.parallel.teams import Teams
+    from prism_cp_b200.parallel.tensor import make_tp
+    from prism_cp_b200.planner.fixed import uniform_plan
+    from prism_cp_b200.runtime import checkpoint
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.trainer import Trainer
+    cfg = hybrid_tiny()
+    batch = make_batch([512, 256, 256], cfg.vocab_size, seed=3)
+    plan = uniform_plan(batch.lengths, 1, 1, 1024, cfg.pattern)
+    tpc = make_tp(world)
+
+    def fresh():
+        return Trainer(HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0, tp=tpc), Teams(tp=tpc),
+                       torch.device("cpu"), lr=1e-3)
+
+    straight = fresh()
+    want = [straight.train_step(batch, plan).loss for _ in range(3)]
+    first = fresh()
+    for _ in range(2):
+        first.train_step(batch, plan)
+    checkpoint.save(first, ck, plan_cursor=2)
+    dist.barrier()
+    resumed = fresh()
+    assert checkpoint.load(resumed, checkpoint.latest(ck)) == 2
+    got = resumed.train_step(batch, plan).loss
+    assert abs(got - want[2]) <= 1e-5 * abs(want[2]), (got, want)
+
+
+def test_tensor_parallel_checkpoint_resume_matches_uninterrupted_run(tmp_path):
+    run_ranks(_tp_resume_case, 2, str(tmp_path / "ck"))
