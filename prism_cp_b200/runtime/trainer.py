@@ -75,10 +75,15 @@ class Trainer:
         self.cache = LayoutCache(self.world, self.rank, device, teams)
         self.hbm_guard = hbm_guard and device.type == "cuda"
         self.loss_acc = torch.zeros((), dtype=torch.float32, device=device)
-        self.recorder = StepRecorder(records, self.rank) if records else None
-        self.run_records = RunRecords(records, self.rank) if records else None
+        # record files are per process: under TP several ranks share one logical rank
+        rec_rank = dist.get_rank() if (dist.is_available() and dist.is_initialized()) else self.rank
+        self.recorder = StepRecorder(records, rec_rank) if records else None
+        self.run_records = RunRecords(records, rec_rank) if records else None
         self.numerics = numerics
         self.logical = logical
+        if logical is not None and logical.group is None and self.group is not None:
+            # rebuild logical samples from the ranks of this TP index only (the others hold copies)
+            logical.group = self.group
         self.audit = AccumulationAudit() if audit else None
         self.step_index = 0
         self.watchdog = watchdog.from_env()
