@@ -128,7 +128,7 @@ def main(argv=None) -> int:
         pipeline = PipelineTrainer(model, info, device, lr=args.lr, min_lr=args.min_lr,
                                    weight_decay=args.weight_decay, clip_grad=args.clip_grad,
                                    warmup_steps=args.lr_warmup_iters,
-                                   decay_steps=args.lr_decay_iters or args.train_iters)
+                                   decay_steps=args.lr_decay_iters or args.train_iters, records=args.records)
         plan_world = info.stage_world
         trainer = pipeline
     else:

@@ -24,6 +24,7 @@ device, the time spent waiting for peers, and the bubble fraction
 
 from __future__ import annotations
 
+import math
 import time
 from dataclasses import dataclass
 
@@ -92,7 +93,7 @@ class StageTeams(Teams):
 
 class PipelineTrainer:
     def __init__(self, model, info: StageInfo, device, lr=3e-4, min_lr=3e-5, weight_decay=0.1, clip_grad=1.0,
-                 warmup_steps=0, decay_steps=1000):
+                 warmup_steps=0, decay_steps=1000, records: str | None = None):
         self.model, self.info, self.device = model, info, device
         self.teams = StageTeams(info)
         self.cache = LayoutCache(info.stage_world, info.stage_rank, device, self.teams)
@@ -103,6 +104,11 @@ class PipelineTrainer:
         self.first = info.stage == 0
         self.last = info.stage == info.pp - 1
         self.stats = {}
+        self.recorder = None
+        if records:
+            from .records import StepRecorder
+            rank = dist.get_rank() if (dist.is_available() and dist.is_initialized()) else 0
+            self.recorder = StepRecorder(records, rank)
 
     def prepare(self, batch, plan, pin: bool = True):
         from .batch import local_inputs
@@ -245,7 +251,20 @@ class PipelineTrainer:
         tokens = sum(lengths.values())
         extra = {"pipeline_stages": info.pp, "bubble_fraction": max(0.0, 1.0 - comp_ms / step_ms) if step_ms else 0.0,
                  "exposed_p2p_ms": wait_ms, "step_ms": step_ms, "compute_ms": comp_ms}
-        return StepResult(float(loss_t.item()), loss_t, tokens, M, lr, elapsed_ms=step_ms, extra=extra)
+        loss = float(loss_t.item())
+        if self.recorder is not None:
+            from .records import step_record
+            cuda = self.device.type == "cuda"
+            rec = step_record(
+                opt.step_count, loss, float(opt.sumsq.sqrt().item()), step_ms, step_ms, tokens=tokens,
+                loss_tokens=batch.loss_tokens, samples=len(lengths), microbatches=M,
+                peak_allocated=torch.cuda.max_memory_allocated(self.device) if cuda else 0,
+                peak_reserved=torch.cuda.max_memory_reserved(self.device) if cuda else 0,
+                memory_budget=0, memory_required=0, admitted=True, sync=dict(opt.stats),
+                finite=math.isfinite(loss))
+            rec["pipeline"] = dict(extra, stage=info.stage)
+            self.recorder.write(rec)
+        return StepResult(loss, loss_t, tokens, M, lr, elapsed_ms=step_ms, extra=extra)
 
     def _apply(self, opt: DistributedAdamW) -> float:
         """AdamW on the stage's shard using the already-combined squared norm."""

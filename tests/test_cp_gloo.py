@@ -558,3 +558,35 @@ def _tp_resume_case(rank, world, ck):
 
 def test_tensor_parallel_checkpoint_resume_matches_uninterrupted_run(tmp_path):
     run_ranks(_tp_resume_case, 2, str(tmp_path / "ck"))
+
+
+def _pp_records_case(rank, world, out):
+    import json
+    from pathlib import Path
+    from prism_cp_b200.models.config import hybrid_tiny
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.planner.fixed import uniform_plan
+    from prism_cp_b200.runtime import records
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.pipeline import PipelineTrainer, make_stage
+    cfg = hybrid_tiny()
+    batch = make_batch([512, 256, 256], cfg.vocab_size, seed=3)
+    plan = uniform_plan(batch.lengths, 1, 1, 512, cfg.pattern)
+    info = make_stage(world, cfg.num_layers)
+    model = HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0,
+                        layers=range(info.first_layer, info.first_layer + info.num_layers),
+                        pre_process=info.stage == 0, post_process=info.stage == world - 1)
+    tr = PipelineTrainer(model, info, torch.device("cpu"), lr=1e-3, records=out)
+    for _ in range(3):
+        tr.train_step(batch, plan)
+    dist.barrier()
+    if rank == 0:
+        rows = [json.loads(x) for x in (Path(out) / "steps_rank1.jsonl").read_text().splitlines()]
+        assert [r["step"] for r in rows] == [1, 2, 3] and rows[0]["pipeline"]["stage"] == 1
+        manifest = {"input_tokens": batch.total_tokens, "loss_tokens": batch.loss_tokens}
+        summary = records.summarize_records(out, manifest, 3, [2, 3], len(plan.microbatches), world=world)
+        assert summary["status"] == "complete", summary
+
+
+def test_pipeline_step_records_summarize_as_complete(tmp_path):
+    run_ranks(_pp_records_case, 2, str(tmp_path / "rec"))
