@@ -115,6 +115,16 @@ def main(argv=None) -> int:
         dist.init_process_group(backend, device_id=device if cuda else None,
                                 timeout=datetime.timedelta(minutes=args.distributed_timeout_minutes))
     cfg = model_config(args)
+    if rank == 0 and (args.records or args.save):
+        # the run's full configuration beside its records / checkpoints (the reference's launch
+        # recipe writes its config and command files the same way)
+        out = Path(args.records or args.save)
+        out.mkdir(parents=True, exist_ok=True)
+        env = {k: v for k, v in os.environ.items() if k.startswith(("PRISM_", "NCCL_", "CUDA_VISIBLE"))}
+        (out / "launch_config.json").write_text(json.dumps(
+            {"argv": list(sys.argv if argv is None else argv), "args": vars(args), "world": world,
+             "model": {"name": cfg.name, "pattern": cfg.pattern, "parameters": cfg.parameter_count()},
+             "environment": env}, indent=1, default=str))
     dtype = torch.bfloat16 if (args.bf16 and cuda) else torch.float32
     tp_size, pp_size = args.tensor_model_parallel_size, args.pipeline_model_parallel_size
     pipeline = None

@@ -180,3 +180,17 @@ def test_auxiliary_run_records(tmp_path):
     assert all(b["host_ns"] >= a["host_ns"] for a, b in zip(timeline[-1]["events"], timeline[-1]["events"][1:]))
     mem = [json.loads(x) for x in (tmp_path / "optimizer_memory_rank0.jsonl").read_text().splitlines()]
     assert mem[-1]["master"] == mem[-1]["exp_avg"] == mem[-1]["exp_avg_sq"] > 0
+
+
+def test_launcher_writes_its_run_configuration(tmp_path):
+    from prism_cp_b200.launcher.train import main
+    rec = tmp_path / "rec"
+    argv = ["--device", "cpu", "--num-layers", "4", "--hidden-size", "256", "--ffn-hidden-size", "512",
+            "--vocab-size", "4096", "--num-attention-heads", "4", "--num-query-groups", "2", "--kv-channels", "64",
+            "--linear-num-key-heads", "4", "--linear-num-value-heads", "4", "--linear-key-head-dim", "64",
+            "--linear-value-head-dim", "64", "--global-batch-size", "2", "--seq-length", "256",
+            "--max-seqlen-per-dp-cp-rank", "512", "--train-iters", "1", "--records", str(rec)]
+    assert main(argv) == 0
+    cfg = json.loads((rec / "launch_config.json").read_text())
+    assert cfg["argv"] == argv and cfg["args"]["train_iters"] == 1 and cfg["model"]["pattern"] == "GGG*"
+    assert (rec / "steps_rank0.jsonl").exists()
