@@ -164,7 +164,11 @@ def main():
         from prism_cp_b200.planner.online import select
         pm = calibrated(model_from_config(cfg, B200_ENVELOPE["device_bytes"],
                                           **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"}))
-        sel = select(batch.lengths, world, cfg.pattern, pm)
+        try:
+            sel = select(batch.lengths, world, cfg.pattern, pm)
+        except ValueError as err:
+            raise SystemExit(f"--plan online: no (cp_gdn, cp_gqa) plan of this batch fits {world} GPU(s) under "
+                             f"the calibrated memory model ({err}); use more GPUs or shorter documents")
         plan = sel.plan
         plan_desc = f"online cp_gdn{sel.cp_gdn} cp_gqa{sel.cp_gqa} over {world}"
     else:
