@@ -56,3 +56,15 @@ def test_launcher_online_scheduler_two_ranks():
     i = argv.index("--sequence-packing-scheduler")
     argv[i + 1] = "online"
     _run(argv + ["--use-varlen-dataset"])
+
+
+def test_launcher_tensor_parallel_records_save_and_resume(tmp_path):
+    """TP = 2 through the launcher: one record file per process, a checkpoint, and a resumed run."""
+    rec, ck = tmp_path / "rec", tmp_path / "ck"
+    base = TINY + ["--tensor-model-parallel-size", "2", "--context-parallel-size", "1"]
+    _run(base + ["--records", str(rec), "--save", str(ck), "--save-interval", "2"])
+    assert (rec / "steps_rank0.jsonl").exists() and (rec / "steps_rank1.jsonl").exists()
+    assert (ck / "latest_checkpointed_iteration.txt").read_text().strip() == "2"
+    argv = list(base)
+    argv[argv.index("--train-iters") + 1] = "3"
+    _run(argv + ["--load", str(ck)])
