@@ -63,7 +63,8 @@ def calibrated(model: Model) -> Model:
     """``model`` with the committed operator calibration and activation-byte scale."""
     from dataclasses import replace
     cal = {k: {x: v[x] for x in ("linear", "quadratic", "fixed_ms") if x in v} for k, v in load_default().items()}
-    return replace(model, operator_calibration=cal, byte_scale=load_byte_scale())
+    cp = json.loads(DEFAULT.read_text()).get("cp_overhead")
+    return replace(model, operator_calibration=cal, byte_scale=load_byte_scale(), cp_overhead=cp)
 
 
 def fit_byte_scale(model: Model, pattern: str, tokens: int, peak_bytes: int) -> float:

@@ -57,6 +57,9 @@ class Model:
     # compute_tflops reached by the token-linear work, "quadratic": the same for causal attention,
     # "fixed_ms": per-call overhead}; None keeps the analytic envelope
     operator_calibration: dict | None = None
+    # measured step-time factor of CP > 1 operators over the analytic CP terms, keyed by CP degree
+    # ("2": 1.07); degrees without an entry use the largest measured degree's factor
+    cp_overhead: dict | None = None
 
     def __post_init__(self):
         for key, value in asdict(self).items():
@@ -104,6 +107,14 @@ class Model:
         head = 4 * self.vocab + 4 * self.hidden
         room = self.budget - self.static(pattern, world) - self.external_bytes - self.margin_bytes
         return max(0, int(room * world // (self.saved_per_token(pattern) + head)))
+
+
+def _cp_factor(table: dict, cp: int) -> float:
+    """Measured CP overhead factor for degree ``cp``: its own entry, else the largest measured degree
+    below it, else the smallest measured degree."""
+    known = sorted(int(k) for k in table)
+    below = [k for k in known if k <= cp]
+    return float(table[str(cp if cp in known else (below[-1] if below else known[0]))])
 
 
 class Evaluator:
@@ -183,6 +194,8 @@ class Evaluator:
             ms = self.response.cost(symbol, cp, lin_ms, quad_ms,
                                     comm / (bandwidth * 1e6) + latency, comm / (m.intra_gbps * 1e6) + latency,
                                     sum(lens), squares, cross_node=cross)
+            if cp > 1 and m.cp_overhead and symbol != "M":
+                ms *= _cp_factor(m.cp_overhead, cp)
             times.append(ms)
             for r in g.ranks:
                 saved[r], work[r] = int(bs * save), int(bs * ws)
