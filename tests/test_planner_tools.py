@@ -193,3 +193,24 @@ def test_calibrated_planner_prices_the_measured_bench_steps():
         ev = Evaluator(m, lengths, world, cfg.pattern)
         ms = sum(ev.evaluate(mb)["predicted_ms"] for mb in plan.microbatches)
         assert abs(ms - measured) <= 0.06 * measured, (world, ms, measured)
+
+
+def test_cp_overhead_factor_lookup_and_measured_ratio():
+    from prism_cp_b200.models.config import PRESETS
+    from prism_cp_b200.planner.calibrate import calibrated
+    from prism_cp_b200.planner.cli import B200_ENVELOPE
+    from prism_cp_b200.planner.fixed import uniform_plan
+    from prism_cp_b200.planner.joint.cost import Evaluator, _cp_factor, model_from_config
+    table = {"2": 1.1, "8": 1.3}
+    assert _cp_factor(table, 2) == 1.1 and _cp_factor(table, 4) == 1.1 and _cp_factor(table, 8) == 1.3
+    assert _cp_factor({"4": 1.2}, 2) == 1.2
+    cfg = PRESETS["hybrid-1.3b"]()
+    m = calibrated(model_from_config(cfg, B200_ENVELOPE["device_bytes"],
+                                     **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"}))
+    lengths = {i: 32768 for i in range(8)}
+    steps = {}
+    for world in (1, 2):
+        plan = uniform_plan(lengths, world, world, 32768, cfg.pattern)
+        ev = Evaluator(m, lengths, world, cfg.pattern)
+        steps[world] = sum(ev.evaluate(mb)["predicted_ms"] for mb in plan.microbatches)
+    assert abs(steps[2] / steps[1] - 3126.0 / 5780.0) < 0.01
