@@ -88,7 +88,7 @@ def plan_for(args, batch, world: int, pattern: str, step: int, replays):
         # exist, so a new degree needs no new process group
         from ..planner.online import select
         sel = select(batch.lengths, world, pattern, _planner_model(args, world))
-        if step == 1 or step % max(1, args.log_interval) == 0:
+        if int(os.environ.get("RANK", "0")) == 0 and (step == 1 or step % max(1, args.log_interval) == 0):
             print(json.dumps({"step": step, "online_cp": {"gdn": sel.cp_gdn, "gqa": sel.cp_gqa},
                               "predicted_update_ms": round(sel.predicted_update_ms, 3)}), flush=True)
         return sel.plan
