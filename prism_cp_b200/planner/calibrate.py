@@ -14,8 +14,14 @@ and ``fixed_ms`` the per-call overhead. The result goes into
 (at the measured NVLink bandwidth) unless a measured CP response profile is
 given. ``fit_byte_scale`` does the same for memory: the activation-byte scale at
 which the evaluator's peak of one microbatch equals a measured peak. The
-committed ``data/b200_operator_calibration.json`` holds both, fitted to this
-framework's own kernels on one B200 for the 1.3B shape.
+committed ``data/b200_operator_calibration.json`` holds both, plus a CP = 2
+overhead factor fitted to the bench's one- and two-GPU step times, for this
+framework's own kernels on B200 and the 1.3B shape. It is regenerated with
+
+    python -m prism_cp_b200.planner.calibrate \
+        --records prism_cp_b200/planner/data/b200_module_records.json \
+        --output prism_cp_b200/planner/data/b200_operator_calibration.json \
+        --peak-gib 141.15 --bench-steps 5780 3126
 """
 
 from __future__ import annotations
@@ -121,12 +127,41 @@ def calibrate(records: list[dict], model: Model) -> dict:
     return out
 
 
+def fit_cp_overhead(model: Model, pattern: str, lengths: dict, world: int, step_ms: float, cp1_step_ms: float,
+                    tokens_per_rank: int) -> float:
+    """CP overhead factor on the GDN and attention operators at CP = ``world`` that makes the model's
+    CP = world / CP = 1 step ratio for ``lengths`` equal the measured ``step_ms / cp1_step_ms``."""
+    from dataclasses import replace
+    from .fixed import uniform_plan
+
+    def step(m, w):
+        plan = uniform_plan(lengths, w, w, tokens_per_rank, pattern)
+        ev = Evaluator(m, lengths, w, pattern)
+        return sum(ev.evaluate(mb)["predicted_ms"] for mb in plan.microbatches)
+    base = replace(model, cp_overhead=None)
+    target = step_ms * step(base, 1) / cp1_step_ms
+    lo, hi = 0.5, 3.0
+    for _ in range(60):
+        mid = 0.5 * (lo + hi)
+        if step(replace(base, cp_overhead={str(world): mid}), world) < target:
+            lo = mid
+        else:
+            hi = mid
+    return 0.5 * (lo + hi)
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--records", type=Path, required=True, help="module records (one file per module or combined)")
     ap.add_argument("--model-config", default="hybrid-1.3b")
     ap.add_argument("--output", type=Path, required=True)
+    ap.add_argument("--peak-gib", type=float, default=None,
+                    help="measured peak_allocated of one CP = 1 microbatch (bench.py) for the byte scale")
+    ap.add_argument("--peak-tokens", type=int, default=32768)
+    ap.add_argument("--bench-steps", type=float, nargs=2, default=None, metavar=("CP1_MS", "CP2_MS"),
+                    help="measured bench.py ms/step on one GPU and on two (CP = 2), 8 x 32K tokens")
     args = ap.parse_args(argv)
+    from dataclasses import replace
     from ..models.config import PRESETS
     from .cli import B200_ENVELOPE
     from .joint.cost import model_from_config
@@ -135,12 +170,26 @@ def main(argv=None) -> int:
         records = data["records"]
     else:
         records = [r for v in data.values() if isinstance(v, dict) for r in v.get("records", [])]
-    model = model_from_config(PRESETS[args.model_config](), B200_ENVELOPE["device_bytes"],
+    cfg = PRESETS[args.model_config]()
+    model = model_from_config(cfg, B200_ENVELOPE["device_bytes"],
                               **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"})
     cal = calibrate(records, model)
-    args.output.write_text(json.dumps({"model_config": args.model_config, "compute_tflops": model.compute_tflops,
-                                       "source": str(args.records), "calibration": cal}, indent=1) + "\n")
-    print(json.dumps(cal))
+    out = {"model_config": args.model_config, "compute_tflops": model.compute_tflops,
+           "source": str(args.records), "calibration": cal}
+    model = replace(model, operator_calibration={k: {x: v[x] for x in ("linear", "quadratic", "fixed_ms") if x in v}
+                                                 for k, v in cal.items()})
+    if args.peak_gib is not None:
+        out["byte_scale"] = fit_byte_scale(model, cfg.pattern, args.peak_tokens, int(args.peak_gib * 2 ** 30))
+        out["byte_scale_source"] = f"measured peak_allocated {args.peak_gib} GiB, one {args.peak_tokens}-token microbatch"
+        model = replace(model, byte_scale=out["byte_scale"])
+    if args.bench_steps is not None:
+        lengths = {i: 32768 for i in range(8)}
+        out["cp_overhead"] = {"2": fit_cp_overhead(model, cfg.pattern, lengths, 2, args.bench_steps[1],
+                                                   args.bench_steps[0], 32768)}
+        out["cp_overhead_source"] = (f"bench.py, 8 x 32K tokens: {args.bench_steps[0]} ms per step on one GPU, "
+                                     f"{args.bench_steps[1]} ms on two (CP = 2); CP 4 and 8 use it until measured")
+    args.output.write_text(json.dumps(out, indent=1) + "\n")
+    print(json.dumps({k: out[k] for k in out if k in ("calibration", "byte_scale", "cp_overhead")}))
     return 0
 
 

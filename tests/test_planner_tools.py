@@ -214,3 +214,17 @@ def test_cp_overhead_factor_lookup_and_measured_ratio():
         ev = Evaluator(m, lengths, world, cfg.pattern)
         steps[world] = sum(ev.evaluate(mb)["predicted_ms"] for mb in plan.microbatches)
     assert abs(steps[2] / steps[1] - 3126.0 / 5780.0) < 0.01
+
+
+def test_calibration_cli_reproduces_the_committed_file(tmp_path):
+    import json
+    from pathlib import Path
+    from prism_cp_b200.planner import calibrate
+    data = Path(calibrate.__file__).resolve().parent / "data"
+    out = tmp_path / "cal.json"
+    assert calibrate.main(["--records", str(data / "b200_module_records.json"), "--output", str(out),
+                           "--peak-gib", "141.15", "--bench-steps", "5780", "3126"]) == 0
+    got, committed = json.loads(out.read_text()), json.loads((data / "b200_operator_calibration.json").read_text())
+    assert got["calibration"] == committed["calibration"]
+    assert abs(got["byte_scale"] - committed["byte_scale"]) < 1e-9
+    assert abs(got["cp_overhead"]["2"] - committed["cp_overhead"]["2"]) < 1e-9
