@@ -285,42 +285,22 @@ c10::optional<at::Tensor> rownorm_bwd(const at::Tensor& dy, const at::Tensor& x,
 }  // namespace prism
 
 // ============================================================================
-// Allocation-free RMSNorm backward (C ABI). This entry point has no counterpart
-// in the reference framework.
-//
-// Who it is for: callers that run where device allocation is not available to
-// them - a host program embedding this library without PyTorch's caching
-// allocator, a runtime that forbids cudaMalloc/cudaFree while a step is in
-// flight because allocation synchronizes the device, or code on a pre-reserved
-// memory budget. They still pass every input and output buffer; the only
-// working memory the routine needs, the per-block partial sums of dW, lives in
+// Allocation-free RMSNorm backward (C ABI), declared with its full contract in
+// prism_noalloc.h. This entry point has no counterpart in the reference
+// framework: it serves callers that cannot allocate device memory (no caching
+// allocator, allocation forbidden while a step is in flight, or a fixed memory
+// budget). Its only working memory, the per-block partial sums of dW, lives in
 // the fixed array below instead of a fresh allocation.
-//
-// Limits and contract:
-//   * scratch: kNoAllocScratchFloats fp32 values (4 MiB) in a file-scope
-//     __device__ array, held on every GPU that loads this library until exit;
-//   * n (normalised length) must be a multiple of 8 and at most 8192; the
-//     number of partial-sum blocks is capped so blocks * n fits the scratch;
-//   * pointers must be 16-byte aligned; dy, x and dx are contiguous [rows, n]
-//     bf16, w is bf16 [n], rstd fp32 [rows] from the forward, dw fp32 [n];
-//   * every call shares the one array and leaves its last contents behind.
-//     Each call writes every scratch row it later reads, so nothing has to be
-//     cleared, but calls whose kernels overlap on the GPU (different streams,
-//     or different host threads) race on the array and must be serialized;
-//   * the first call on a device looks up the array's device address with
-//     cudaGetSymbolAddress (a host-side symbol is not a device pointer); make
-//     that first call before any stream capture;
-//   * no cudaMalloc, cudaFree or allocating library routine is called.
-// Returns 0 on success, otherwise a positive error code (see below); the
-// matching message is available from prism_noalloc_error_string.
 // ============================================================================
 #include <mutex>
+
+#include "prism_noalloc.h"
 
 namespace prism {
 namespace {
 
-constexpr int kNoAllocScratchFloats = 1 << 20;  // 4 MiB of fp32 partial sums
-constexpr int kNoAllocMaxN = 8192;
+constexpr int kNoAllocScratchFloats = PRISM_NOALLOC_SCRATCH_BYTES / sizeof(float);  // 4 MiB of fp32 sums
+constexpr int kNoAllocMaxN = PRISM_NOALLOC_MAX_N;
 constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
@@ -329,32 +309,26 @@ std::mutex g_noalloc_mutex;
 float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
 int g_noalloc_sms[kNoAllocMaxDevices] = {};
 
-enum NoAllocStatus : int {
-  kNoAllocOk = 0,
-  kNoAllocBadArgument = 1,
-  kNoAllocTooLarge = 2,
-  kNoAllocSetupFailed = 3,
-  kNoAllocLaunchFailed = 4,
-};
-
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+bool aligned_to(const void* p, uintptr_t bytes) { return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0; }
 
 // Device address of the scratch array on the current device (looked up once).
 int noalloc_setup(int device, float** out, int* sms) {
   std::lock_guard<std::mutex> guard(g_noalloc_mutex);
   if (g_noalloc_ptr[device] == nullptr) {
     void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return kNoAllocSetupFailed;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) {
+      return PRISM_NOALLOC_SETUP_FAILED;
+    }
     int count = 0;
     if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
-      return kNoAllocSetupFailed;
+      return PRISM_NOALLOC_SETUP_FAILED;
     }
     g_noalloc_ptr[device] = static_cast<float*>(ptr);
     g_noalloc_sms[device] = count;
   }
   *out = g_noalloc_ptr[device];
   *sms = g_noalloc_sms[device];
-  return kNoAllocOk;
+  return PRISM_NOALLOC_OK;
 }
 
 }  // namespace
@@ -362,11 +336,13 @@ int noalloc_setup(int device, float** out, int* sms) {
 
 extern "C" __attribute__((visibility("default"))) const char* prism_noalloc_error_string(int code) {
   switch (code) {
-    case prism::kNoAllocOk: return "ok";
-    case prism::kNoAllocBadArgument: return "bad argument (null or misaligned pointer, rows < 1, or n not a multiple of 8)";
-    case prism::kNoAllocTooLarge: return "n exceeds the 8192 maximum of the fixed scratch array";
-    case prism::kNoAllocSetupFailed: return "could not resolve the scratch array on the current device";
-    case prism::kNoAllocLaunchFailed: return "kernel launch failed";
+    case PRISM_NOALLOC_OK: return "ok";
+    case PRISM_NOALLOC_BAD_ARGUMENT:
+      return "bad argument (null or misaligned pointer, rows < 1, or n not a multiple of 8)";
+    case PRISM_NOALLOC_TOO_LARGE: return "n exceeds the 8192 maximum of the fixed scratch array";
+    case PRISM_NOALLOC_SETUP_FAILED: return "could not resolve the scratch array on the current device";
+    case PRISM_NOALLOC_LAUNCH_FAILED: return "kernel launch failed";
+    case PRISM_NOALLOC_PENDING_ERROR: return "a CUDA error from earlier work was pending; nothing was launched";
     default: return "unknown error";
   }
 }
@@ -379,18 +355,23 @@ extern "C" __attribute__((visibility("default"))) int prism_rmsnorm_bwd_noalloc(
   using namespace prism;
   if (dy == nullptr || x == nullptr || w == nullptr || rstd == nullptr || dx == nullptr || dw == nullptr ||
       rows < 1 || n < 8 || n % 8 != 0) {
-    return kNoAllocBadArgument;
+    return PRISM_NOALLOC_BAD_ARGUMENT;
   }
-  if (!aligned16(dy) || !aligned16(x) || !aligned16(w) || !aligned16(dx)) return kNoAllocBadArgument;
-  if (n > kNoAllocMaxN) return kNoAllocTooLarge;
+  if (!aligned_to(dy, 16) || !aligned_to(x, 16) || !aligned_to(w, 16) || !aligned_to(dx, 16) ||
+      !aligned_to(rstd, 4) || !aligned_to(dw, 4)) {
+    return PRISM_NOALLOC_BAD_ARGUMENT;
+  }
+  if (n > kNoAllocMaxN) return PRISM_NOALLOC_TOO_LARGE;
+  // an error left by the caller's earlier work is reported as such, not as this call's launch failure
+  if (cudaPeekAtLastError() != cudaSuccess) return PRISM_NOALLOC_PENDING_ERROR;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kNoAllocMaxDevices) {
-    return kNoAllocSetupFailed;
+    return PRISM_NOALLOC_SETUP_FAILED;
   }
   float* scratch = nullptr;
   int sms = 0;
   const int setup = noalloc_setup(device, &scratch, &sms);
-  if (setup != kNoAllocOk) return setup;
+  if (setup != PRISM_NOALLOC_OK) return setup;
   int blocks = std::min((rows + kWarpsPerBlock - 1) / kWarpsPerBlock, sms * 4);
   blocks = std::max(1, std::min(blocks, kNoAllocScratchFloats / n));
   const auto* dyp = static_cast<const __nv_bfloat16*>(dy);
@@ -399,8 +380,8 @@ extern "C" __attribute__((visibility("default"))) int prism_rmsnorm_bwd_noalloc(
   auto* dxp = static_cast<__nv_bfloat16*>(dx);
   rownorm_bwd_kernel<true, false><<<blocks, kWarpsPerBlock * 32, n * sizeof(float), stream>>>(
       dyp, n, xp, n, wp, nullptr, 0, rstd, dxp, n, nullptr, 0, scratch, rows, 1, n, 1.0f / n);
-  if (cudaGetLastError() != cudaSuccess) return kNoAllocLaunchFailed;
+  if (cudaGetLastError() != cudaSuccess) return PRISM_NOALLOC_LAUNCH_FAILED;
   column_sum_kernel<<<(n + 255) / 256, 256, 0, stream>>>(scratch, blocks, n, dw, nullptr);
-  if (cudaGetLastError() != cudaSuccess) return kNoAllocLaunchFailed;
-  return kNoAllocOk;
+  if (cudaGetLastError() != cudaSuccess) return PRISM_NOALLOC_LAUNCH_FAILED;
+  return PRISM_NOALLOC_OK;
 }

@@ -12,7 +12,8 @@
 //  * p2p_gather_rows: the CP-transition reshard as one kernel - every
 //    destination row block is copied straight from the owning peer's heap
 //    (16-byte vector loads over NVLink) into the local layout, driven by a
-//    device route table, after a bounded wait for the sender's "ready" signal.
+//    device route table, after a bounded wait for the sender's "ready" signal;
+//    it copies nothing when that wait (or any earlier one) recorded an error.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -65,6 +66,9 @@ struct RouteEntry {
 __global__ void gather_rows_kernel(const int64_t* peer_bases, const RouteEntry* routes, int n_routes,
                                    const int64_t* block_route, const int64_t* block_row0, int rows_per_block,
                                    int64_t row_bytes, uint8_t* dst, int* status) {
+  // a bounded wait before this launch gave up (peer missing or late): copy nothing rather than rows a
+  // peer may not have finished writing; the host sees the status at its next check
+  if (*reinterpret_cast<volatile int*>(status) != 0) return;
   const int b = blockIdx.x;
   const RouteEntry e = routes[block_route[b]];
   const int64_t r0 = block_row0[b];

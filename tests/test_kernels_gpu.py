@@ -285,7 +285,21 @@ def test_a_device_wait_that_runs_out_reports_an_error_and_the_context_survives()
     torch.cuda.synchronize()
     waited = time.monotonic() - t0
     assert 1.5 < waited < 60, waited
+    # a gather queued behind the failed wait copies nothing (no stale rows reach the output)
+    src = torch.arange(64 * 8, dtype=torch.float32, device=dev).view(64, 8)
+    dst = torch.full((64, 8), -1.0, device=dev)
+    bases = torch.tensor([src.data_ptr()], dtype=torch.int64, device=dev)
+    routes = torch.tensor([[0, 0, 0, 64]], dtype=torch.int64, device=dev)
+    block_route = torch.zeros(2, dtype=torch.int64, device=dev)
+    block_row0 = torch.tensor([0, 32], dtype=torch.int64, device=dev)
+    lib().symm_gather_rows(bases, routes, block_route, block_row0, 32, 32, dst, status(dev))
+    torch.cuda.synchronize()
+    assert bool((dst == -1.0).all())
     with pytest.raises(RuntimeError, match="timed out"):
         check_status(dev)
+    # with the status cleared the same gather copies every row
+    lib().symm_gather_rows(bases, routes, block_route, block_row0, 32, 32, dst, status(dev))
+    torch.cuda.synchronize()
+    assert torch.equal(dst, src)
     a = torch.randn(256, 256, device=dev)
     assert torch.allclose(a @ torch.eye(256, device=dev), a)

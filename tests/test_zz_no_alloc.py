@@ -4,8 +4,9 @@
 memory themselves (no caching allocator, or allocation forbidden mid-step);
 its working memory is a fixed array inside the library. This test calls it the
 way such a caller would - by symbol, with raw pointers and a stream - and
-checks two consecutive calls (the second one on different data, so stale
-scratch contents would show) against the regular PyTorch-facing entry point.
+checks consecutive calls (each on different data and sizes, so stale scratch
+contents would show) against the regular PyTorch-facing entry point and an
+fp32 PyTorch oracle.
 The file is named so that pytest collects it after every other test.
 """
 
@@ -47,11 +48,26 @@ def _case(rows, n, seed):
     return x, dy, w, rstd
 
 
+def _oracle(x, dy, w, rstd):
+    """fp32 PyTorch RMSNorm backward: dx and dw of y = x * rstd * w."""
+    xf, dyf, wf = x.float(), dy.float(), w.float()
+    xhat = xf * rstd[:, None]
+    g = dyf * wf
+    dx = rstd[:, None] * (g - xhat * (g * xhat).mean(-1, keepdim=True))
+    return dx, (dyf * xhat).sum(0)
+
+
+# (rows, n): the last case has n at the 8192 maximum and enough rows that the number of
+# partial-sum blocks is set by the scratch capacity (2^20 floats / 8192 = 128 blocks),
+# not by the SM count or the row count
+CASES = ((3000, 2048), (1500, 4096), (9000, 8192))
+
+
 def test_noalloc_rmsnorm_backward_matches_regular_entry_point():
     from prism_cp_b200.ops._lib import lib
     fn, msg = _library()
     stream = torch.cuda.current_stream()
-    for call, (rows, n) in enumerate(((3000, 2048), (1500, 4096))):
+    for call, (rows, n) in enumerate(CASES):
         x, dy, w, rstd = _case(rows, n, seed=call)
         dx_ref = torch.empty_like(x)
         dw_ref = lib().rownorm_bwd(dy, x, w, None, rstd, dx_ref, None, 1, n, 1.0 / n)
@@ -63,6 +79,9 @@ def test_noalloc_rmsnorm_backward_matches_regular_entry_point():
         torch.cuda.synchronize()
         assert rel_err(dx, dx_ref) < 1e-2
         assert rel_err(dw, dw_ref) < 1e-2
+        dx_f32, dw_f32 = _oracle(x, dy, w, rstd)
+        assert rel_err(dx, dx_f32) < 1e-2
+        assert rel_err(dw, dw_f32) < 1e-2
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():
@@ -73,3 +92,19 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     code = fn(dy.data_ptr(), x.data_ptr(), w.data_ptr(), rstd.data_ptr(), out.data_ptr(), dw.data_ptr(), 64, 16384,
               torch.cuda.current_stream().cuda_stream)
     assert code == 2 and b"8192" in msg(code)
+
+
+def test_noalloc_rejects_misaligned_fp32_pointers():
+    fn, msg = _library()
+    x, dy, w, rstd = _case(64, 1024, seed=9)
+    out = torch.empty_like(x)
+    dw = torch.empty(1024 + 4, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    # rstd and dw are read and written as fp32: a pointer that is not 4-byte aligned is refused
+    # before anything is launched
+    code = fn(dy.data_ptr(), x.data_ptr(), w.data_ptr(), rstd.data_ptr() + 2, out.data_ptr(), dw.data_ptr(), 64,
+              1024, stream)
+    assert code == 1, msg(code).decode()
+    code = fn(dy.data_ptr(), x.data_ptr(), w.data_ptr(), rstd.data_ptr(), out.data_ptr(), dw.data_ptr() + 1, 64,
+              1024, stream)
+    assert code == 1, msg(code).decode()
