@@ -64,3 +64,18 @@ def test_watchdog_reports_a_stall(capsys):
         assert not wd.reported
     finally:
         wd.close()
+
+
+def test_timeline_summary_separates_hidden_and_exposed_communication():
+    # compute 0..10 ms, NCCL 5..15 ms (5 ms hidden, 5 exposed), P2P 20..22 ms (exposed), idle 15..20
+    kernels = [("prism::gemm::gemm_kernel", 0.0, 10000.0), ("ncclDevKernel_AllGather", 5000.0, 15000.0),
+               ("prism::symm::gather_rows_kernel", 20000.0, 22000.0)]
+    s = tracing.timeline_summary(kernels, 22.0)
+    assert abs(s["span_ms"] - 22.0) < 1e-9 and abs(s["busy_ms"] - 17.0) < 1e-9
+    assert abs(s["exposed_comm_ms"] - 7.0) < 1e-9 and abs(s["idle_ms"] - 5.0) < 1e-9
+    assert s["categories"] == {"gemm": 10.0, "nccl": 10.0, "p2p": 2.0}
+    assert tracing.categorize("void prism::attnb::attn_bwd_kv_kernel<prism::NoPeers>") == "attention"
+    assert tracing.categorize("prism::gdnc::gdn_bwd_local_kernel") == "gdn"
+    text = tracing.format_breakdown([dict(s, top=[("gemm", 10.0)])],
+                                    dict(model="m", seqs=1, seq_len=8, world=1, impl="ring"))
+    assert "| 0 | 22.0 | 17.0 | 5.0 | 7.0 |" in text
