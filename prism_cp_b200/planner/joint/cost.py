@@ -1,31 +1,42 @@
 """Cost and whole forward/backward memory model of a joint plan.
 
-``Model`` holds the model shape, device bytes, external/margin reservations,
-throughput and link assumptions, and an optional hardware CP response
-profile. ``Evaluator`` prices a microbatch layer by layer: the operator time of
-each layout (analytic FLOPs and CP communication, replaced or corrected by the
-response profile), the transfer time of every layout change (forward route
-and its inverse in the backward), and a per-rank memory envelope that
-accumulates saved activations layer by layer and adds each step's workspace,
-both for the forward prefix and the matching backward point. All times are
-milliseconds of forward + backward.
+``Model`` holds the model shape, the device bytes and reservations, throughput
+and link assumptions and an optional hardware CP-response profile (the field
+set is the planner's config format, shared with the reference's
+joint_cp/model.py so its configs load unchanged). ``Evaluator`` prices one
+microbatch:
 
-Formulas and constants follow the reference evaluator
-(experiments/sequence_dynamic_cp/joint_cp/model.py:17-228) so predicted update
-times of identical plans agree; ``Model.byte_scale`` lets a measured B200
-profile rescale the activation terms of this framework's own kernels.
+* every operator call of a layout is described by a ``Sheet`` (useful FLOPs,
+  the causal-attention part of them, CP bytes on the wire, bytes saved for the
+  backward and transient workspace per rank) from a per-operator formula, then
+  priced by the response profile (``response.profile_of``);
+* a layout change is priced by its route: the busiest rank's injected or
+  received bytes per link class, the local pack/unpack copy, a latency, all
+  twice (the backward runs the inverse route);
+* memory is a per-rank walk: the residual stream and every layer's saved
+  activations accumulate, and at each step of a layer (route in, operator,
+  route to the MLP, MLP, route back) the step's workspace sits on top.
+
+Times are milliseconds of forward + backward. The formulas and constants are
+the reference's (joint_cp/model.py:56-228), evaluated in the same arithmetic
+order, so identical plans get identical predicted times in both tools.
+``byte_scale``, ``operator_calibration`` and ``cp_overhead`` fit the model to
+this framework's measured B200 kernels (``planner/calibrate.py``).
 """
 
 from __future__ import annotations
 
 import math
-from dataclasses import asdict, dataclass
+from dataclasses import dataclass, fields
 from functools import lru_cache
+from typing import NamedTuple
 
 from .ir import identity_route, route
-from .response import Response, operator_work, validate_response
+from .response import Parts, operator_work, profile_of, validate_response
 
 GIB = 1024 ** 3
+_POSITIVE = ("hidden", "ffn", "vocab", "q_heads", "kv_heads", "head_dim", "gdn_heads", "gdn_dim", "device_bytes",
+             "compute_tflops", "intra_gbps", "inter_gbps", "memory_gbps", "ranks_per_node", "byte_scale")
 
 
 @dataclass(frozen=True)
@@ -62,187 +73,231 @@ class Model:
     cp_overhead: dict | None = None
 
     def __post_init__(self):
-        for key, value in asdict(self).items():
-            if isinstance(value, (int, float)) and not isinstance(value, bool):
-                if not math.isfinite(value) or value < 0:
-                    raise ValueError(f"Invalid model field {key}")
-        for key in ("hidden", "ffn", "vocab", "q_heads", "kv_heads", "head_dim", "gdn_heads", "gdn_dim",
-                    "device_bytes", "compute_tflops", "intra_gbps", "inter_gbps", "memory_gbps",
-                    "ranks_per_node", "byte_scale"):
-            if getattr(self, key) <= 0:
-                raise ValueError(f"Model field must be positive: {key}")
+        numbers = {f.name: getattr(self, f.name) for f in fields(self)}
+        for key, value in numbers.items():
+            if isinstance(value, bool) or not isinstance(value, (int, float)):
+                continue
+            if not math.isfinite(value) or value < 0:
+                raise ValueError(f"Invalid model field {key}")
+        zero = next((k for k in _POSITIVE if numbers[k] <= 0), None)
+        if zero is not None:
+            raise ValueError(f"Model field must be positive: {zero}")
         if self.cp_response is not None:
             validate_response(self.cp_response, self)
-        for sym, cal in (self.operator_calibration or {}).items():
-            if sym not in ("G", "*", "M") or not (cal.get("linear", 0) > 0 and cal.get("quadratic", 1) > 0
-                                                  and cal.get("fixed_ms", 0) >= 0):
-                raise ValueError(f"invalid operator calibration for {sym!r}: {cal}")
+        for symbol, cal in (self.operator_calibration or {}).items():
+            sane = cal.get("linear", 0) > 0 and cal.get("quadratic", 1) > 0 and cal.get("fixed_ms", 0) >= 0
+            if symbol not in ("G", "*", "M") or not sane:
+                raise ValueError(f"invalid operator calibration for {symbol!r}: {cal}")
+
+    @property
+    def gdn_width(self) -> int:
+        return self.gdn_heads * self.gdn_dim
 
     @property
     def budget(self) -> int:
+        """Admission budget of one device: 90 % of it, and at least 8 GiB left free."""
         return min(int(0.9 * self.device_bytes), self.device_bytes - 8 * GIB)
 
     def params(self, pattern: str) -> int:
-        h, d = self.hidden, self.gdn_heads * self.gdn_dim
-        gqa = h * (self.q_heads + 2 * self.kv_heads) * self.head_dim + h * h
-        gdn = h * 5 * d + d * h + 4 * 3 * d + 2 * self.gdn_heads
-        return (2 * self.vocab * h + len(pattern) * (3 * h * self.ffn + 4 * h)
-                + pattern.count("*") * gqa + pattern.count("G") * gdn + h)
+        h, d = self.hidden, self.gdn_width
+        per_symbol = {"*": h * (self.q_heads + 2 * self.kv_heads) * self.head_dim + h * h,
+                      "G": h * 5 * d + d * h + 4 * 3 * d + 2 * self.gdn_heads}
+        mixers = sum(per_symbol[s] * pattern.count(s) for s in ("*", "G"))
+        return 2 * self.vocab * h + len(pattern) * (3 * h * self.ffn + 4 * h) + mixers + h
 
     def static(self, pattern: str, world: int) -> int:
+        """bf16 weights, fp32 gradients, fp32 master/m/v sharded over the world, a buffer reserve."""
         if self.static_bytes is not None:
             return self.static_bytes
-        # bf16 weights, fp32 gradients, fp32 master/m/v sharded over the world, buffer reserve
         return math.ceil(self.params(pattern) * (6 + 12 / world)) + 256 * 1024 ** 2
 
     def saved_per_token(self, pattern: str) -> float:
-        h, d = self.hidden, self.gdn_heads * self.gdn_dim
-        gqa_io = (self.q_heads + 2 * self.kv_heads) * self.head_dim
-        return self.byte_scale * (4 * h + pattern.count("G") * 2 * (8 * h + 5 * d)
-                                  + pattern.count("*") * (2 * (8 * h + gqa_io) + 4 * self.q_heads)
-                                  + len(pattern) * 2 * (4 * h + 3 * self.ffn))
+        h, d = self.hidden, self.gdn_width
+        qkv = (self.q_heads + 2 * self.kv_heads) * self.head_dim
+        per_layer = {"G": 2 * (8 * h + 5 * d), "*": 2 * (8 * h + qkv) + 4 * self.q_heads}
+        mixers = per_layer["G"] * pattern.count("G") + per_layer["*"] * pattern.count("*")
+        return self.byte_scale * (4 * h + mixers + len(pattern) * 2 * (4 * h + 3 * self.ffn))
 
     def token_capacity_upper_bound(self, pattern: str, world: int) -> int:
-        """Necessary (not sufficient) token ceiling from average live storage at the head."""
-        head = 4 * self.vocab + 4 * self.hidden
+        """Necessary (not sufficient) token ceiling: average live storage at the output head."""
         room = self.budget - self.static(pattern, world) - self.external_bytes - self.margin_bytes
-        return max(0, int(room * world // (self.saved_per_token(pattern) + head)))
+        per_token = self.saved_per_token(pattern) + 4 * self.vocab + 4 * self.hidden
+        return max(0, int(room * world // per_token))
 
 
-def _cp_factor(table: dict, cp: int) -> float:
-    """Measured CP overhead factor for degree ``cp``: its own entry, else the largest measured degree
-    below it, else the smallest measured degree."""
-    known = sorted(int(k) for k in table)
-    below = [k for k in known if k <= cp]
-    return float(table[str(cp if cp in known else (below[-1] if below else known[0]))])
+class Sheet(NamedTuple):
+    """One operator call of one CP group, per rank of the group."""
+
+    flops: float        # useful F+B FLOPs per rank
+    quadratic: float    # the causal-attention part of ``flops``
+    comm: float         # CP bytes per rank on the group's links
+    saved: int          # bytes kept for the backward
+    work: int           # transient workspace bytes
+
+
+def _mlp_sheet(m: Model, n: int, squares: int, nseq: int, cp: int) -> Sheet:
+    h, f = m.hidden, m.ffn
+    return Sheet(18 * n * h * f, 0, 0, n * 2 * (4 * h + 3 * f), n * 2 * (2 * h + 2 * f))
+
+
+def _gqa_sheet(m: Model, n: int, squares: int, nseq: int, cp: int) -> Sheet:
+    h, kv = m.hidden, m.kv_heads * m.head_dim
+    qkv = (m.q_heads + 2 * m.kv_heads) * m.head_dim
+    quadratic = 6 * m.q_heads * m.head_dim * squares / cp
+    return Sheet(6 * n * (h * qkv + h * h) + quadratic, quadratic,
+                 3 * (cp - 1) * n * 4 * kv,                      # K/V ring forward + K/V and dK/dV backward
+                 n * (2 * (8 * h + qkv) + 4 * m.q_heads),
+                 n * (4 * h + 8 * kv * max(1, cp - 1)))
+
+
+def _gdn_sheet(m: Model, n: int, squares: int, nseq: int, cp: int) -> Sheet:
+    h, d = m.hidden, m.gdn_width
+    state = 4 * m.gdn_heads * m.gdn_dim ** 2                    # one fp32 recurrent state
+    return Sheet(6 * n * (6 * h * d + state), 0,
+                 2 * (cp - 1) * nseq * (state + 6 * 3 * d),     # state pass + conv halo, F and B
+                 n * 2 * (8 * h + 5 * d),
+                 n * 4 * (h + 5 * d) + nseq * cp * state)
+
+
+SHEETS = {"M": _mlp_sheet, "*": _gqa_sheet, "G": _gdn_sheet}
+
+
+def cp_overhead_factor(table: dict, cp: int) -> float:
+    """Measured CP overhead factor for degree ``cp``: its own entry, else the largest measured
+    degree below it, else the smallest measured degree."""
+    measured = sorted(int(k) for k in table)
+    usable = [k for k in measured if k <= cp] or measured[:1]
+    return float(table[str(usable[-1])])
+
+
+def _plus(a, b) -> tuple:
+    return tuple(x + y for x, y in zip(a, b))
 
 
 class Evaluator:
+    """Prices microbatches of one batch (``lengths``) on ``world`` ranks for one layer ``pattern``."""
+
     def __init__(self, model: Model, lengths: dict, world: int, pattern: str):
         self.model, self.lengths, self.world, self.pattern = model, lengths, world, pattern
         self.base = model.static(pattern, world) + model.external_bytes + model.margin_bytes
-        self.response = Response(model)
-        self._zeros = (0,) * world
+        self.profile = profile_of(model)
+        self._none = (0,) * world
 
     @lru_cache(maxsize=4096)
     def tokens(self, layout) -> tuple[int, ...]:
         return layout.tokens(self.lengths, self.world)
 
+    def _scaled(self, nbytes) -> int:
+        return int(self.model.byte_scale * nbytes)
+
+    # ------------------------------------------------------------------ routes
     @lru_cache(maxsize=8192)
     def transfer(self, source, target):
-        """(ms forward+inverse, per-rank workspace bytes) of a layout change."""
-        m = self.model
+        """(ms of the route and its inverse, per-rank workspace bytes) of a layout change."""
         if source == target:
-            return 0.0, self._zeros
+            return 0.0, self._none
         edges = route(source, target, self.lengths, self.world)
         if identity_route(edges):
-            return 0.0, self._zeros
+            return 0.0, self._none
+        m = self.model
         row = 2 * m.hidden
-        out_intra, out_inter = [0] * self.world, [0] * self.world
-        in_intra, in_inter = [0] * self.world, [0] * self.world
-        for src, dst, _, _, n in edges:
+        # per rank: [sent intra, received intra, sent inter, received inter] bytes
+        load = [[0, 0, 0, 0] for _ in range(self.world)]
+        for src, dst, _, _, count in edges:
             if src == dst:
                 continue
-            cross = src // m.ranks_per_node != dst // m.ranks_per_node
-            (out_inter if cross else out_intra)[src] += n * row
-            (in_inter if cross else in_intra)[dst] += n * row
-        # the critical rank's injection/receive time, not the sum over GPUs
-        link_ms = max((max(a, b) / (m.intra_gbps * 1e6) + max(c, d) / (m.inter_gbps * 1e6)
-                       for a, b, c, d in zip(out_intra, in_intra, out_inter, in_inter)), default=0.0)
-        work = tuple(int(m.byte_scale * 2 * row * (a + b)) for a, b in zip(self.tokens(source), self.tokens(target)))
+            lane = 2 if src // m.ranks_per_node != dst // m.ranks_per_node else 0
+            load[src][lane] += count * row
+            load[dst][lane + 1] += count * row
+        # the busiest rank sets the pace: injection or reception, per link class
+        link_ms = max((max(r[0], r[1]) / (m.intra_gbps * 1e6) + max(r[2], r[3]) / (m.inter_gbps * 1e6)
+                       for r in load), default=0)
+        # the local pack and unpack copies (forward and inverse backward)
+        work = tuple(self._scaled(2 * row * (a + b)) for a, b in zip(self.tokens(source), self.tokens(target)))
         copy_ms = max(work) / (m.memory_gbps * 1e6)
         return 2 * (link_ms + copy_ms + m.latency_ms), work
 
+    # ------------------------------------------------------------------ operators
+    def _call_ms(self, symbol: str, cp: int, sheet: Sheet, tokens: int, squares: int, cross: bool) -> float:
+        m = self.model
+        rate = m.compute_tflops * 1e9
+        linear, quadratic = (sheet.flops - sheet.quadratic) / rate, sheet.quadratic / rate
+        cal = (m.operator_calibration or {}).get(symbol)
+        if cal is not None:
+            linear = linear / cal["linear"] + cal.get("fixed_ms", 0.0)
+            quadratic = quadratic / cal.get("quadratic", 1.0)
+        latency = 2 * m.latency_ms * (cp - 1) if symbol != "M" else 0.0
+        bandwidth = m.inter_gbps if cross else m.intra_gbps
+        parts = Parts(linear, quadratic, sheet.comm / (bandwidth * 1e6) + latency,
+                      sheet.comm / (m.intra_gbps * 1e6) + latency)
+        ms = self.profile.price(symbol, cp, parts, tokens, squares, cross)
+        if cp > 1 and symbol != "M" and m.cp_overhead:
+            ms *= cp_overhead_factor(m.cp_overhead, cp)
+        return ms
+
     @lru_cache(maxsize=4096)
     def operator(self, symbol: str, layout):
-        """(ms, saved bytes per rank, workspace bytes per rank) of one layer operator."""
+        """(ms of the slowest group, saved bytes per rank, workspace bytes per rank) of one operator."""
         m = self.model
-        times = []
         saved, work = [0] * self.world, [0] * self.world
-        h, f, d = m.hidden, m.ffn, m.gdn_heads * m.gdn_dim
-        bs = m.byte_scale
+        slowest = None
         for g in layout.groups:
             cp = len(g.ranks)
-            lens = [self.lengths[s] for s in g.samples]
-            n = sum(lens) // cp
-            squares = sum(x * x for x in lens)
-            quadratic = 0
-            if symbol == "M":
-                flops, comm = 18 * n * h * f, 0
-                save, ws = n * 2 * (4 * h + 3 * f), n * 2 * (2 * h + 2 * f)
-            elif symbol == "*":
-                proj = 6 * n * (h * (m.q_heads + 2 * m.kv_heads) * m.head_dim + h * h)
-                quadratic = 6 * m.q_heads * m.head_dim * squares / cp
-                flops = proj + quadratic
-                comm = 3 * (cp - 1) * n * 4 * m.kv_heads * m.head_dim
-                save = n * (2 * (8 * h + (m.q_heads + 2 * m.kv_heads) * m.head_dim) + 4 * m.q_heads)
-                ws = n * (4 * h + 8 * m.kv_heads * m.head_dim * max(1, cp - 1))
-            else:
-                flops = 6 * n * (6 * h * d + 4 * m.gdn_heads * m.gdn_dim ** 2)
-                comm = 2 * (cp - 1) * len(lens) * (4 * m.gdn_heads * m.gdn_dim ** 2 + 6 * 3 * d)
-                save = n * 2 * (8 * h + 5 * d)
-                ws = n * 4 * (h + 5 * d) + len(lens) * cp * 4 * m.gdn_heads * m.gdn_dim ** 2
+            sizes = [self.lengths[s] for s in g.samples]
+            total, squares = sum(sizes), sum(x * x for x in sizes)
+            sheet = SHEETS[symbol](m, total // cp, squares, len(sizes), cp)
             cross = g.ranks[0] // m.ranks_per_node != g.ranks[-1] // m.ranks_per_node
-            bandwidth = m.inter_gbps if cross else m.intra_gbps
-            latency = 2 * m.latency_ms * (cp - 1) if symbol != "M" else 0.0
-            rate = m.compute_tflops * 1e9
-            lin_ms, quad_ms = (flops - quadratic) / rate, quadratic / rate
-            cal = (m.operator_calibration or {}).get(symbol)
-            if cal is not None:
-                lin_ms = lin_ms / cal["linear"] + cal.get("fixed_ms", 0.0)
-                quad_ms = quad_ms / cal.get("quadratic", 1.0)
-            ms = self.response.cost(symbol, cp, lin_ms, quad_ms,
-                                    comm / (bandwidth * 1e6) + latency, comm / (m.intra_gbps * 1e6) + latency,
-                                    sum(lens), squares, cross_node=cross)
-            if cp > 1 and m.cp_overhead and symbol != "M":
-                ms *= _cp_factor(m.cp_overhead, cp)
-            times.append(ms)
+            ms = self._call_ms(symbol, cp, sheet, total, squares, cross)
+            slowest = ms if slowest is None else max(slowest, ms)
             for r in g.ranks:
-                saved[r], work[r] = int(bs * save), int(bs * ws)
-        return max(times), tuple(saved), tuple(work)
+                saved[r], work[r] = self._scaled(sheet.saved), self._scaled(sheet.work)
+        return slowest, tuple(saved), tuple(work)
 
+    # ------------------------------------------------------------------ memory walk
     def initial(self, ingress) -> tuple[int, ...]:
-        # the embedding output / residual stays alive through the whole stack
-        return tuple(self.base + int(self.model.byte_scale * n * 4 * self.model.hidden)
-                     for n in self.tokens(ingress))
+        """Live bytes before the first layer: static state plus the residual stream, which
+        stays alive through the whole stack."""
+        return tuple(self.base + self._scaled(n * 4 * self.model.hidden) for n in self.tokens(ingress))
 
     def layer(self, live, previous, attention, mlp, symbol):
-        a_ms, a_save, a_ws = self.operator(symbol, attention)
-        m_ms, m_save, m_ws = self.operator("M", mlp)
-        in_ms, in_ws = self.transfer(previous, attention)
-        out_ms, out_ws = self.transfer(attention, mlp)
-        after_a = tuple(x + y for x, y in zip(live, a_save))
-        after_m = tuple(x + y for x, y in zip(after_a, m_save))
-        points = (tuple(x + y for x, y in zip(live, in_ws)),
-                  tuple(x + y for x, y in zip(after_a, a_ws)),
-                  tuple(x + y for x, y in zip(after_a, out_ws)),
-                  tuple(x + y for x, y in zip(after_m, m_ws)),
-                  tuple(x + y for x, y in zip(after_m, out_ws)))
-        peak = tuple(max(col) for col in zip(*points))
+        """(ms, live bytes after, peak bytes) of one layer entered from layout ``previous``."""
+        a_ms, a_saved, a_work = self.operator(symbol, attention)
+        m_ms, m_saved, m_work = self.operator("M", mlp)
+        in_ms, in_work = self.transfer(previous, attention)
+        out_ms, out_work = self.transfer(attention, mlp)
+        after_mixer = _plus(live, a_saved)
+        after_mlp = _plus(after_mixer, m_saved)
+        # forward steps and their backward points: route in, mixer, route to the MLP, MLP, route back
+        peak = tuple(max(l0 + i, l1 + max(aw, ow), l2 + max(mw, ow))
+                     for l0, l1, l2, i, aw, ow, mw in zip(live, after_mixer, after_mlp, in_work, a_work, out_work,
+                                                          m_work))
         # the MLP output returns to the attention placement: two routes each in F and B
-        return in_ms + a_ms + m_ms + 2 * out_ms, after_m, peak
+        return in_ms + a_ms + m_ms + 2 * out_ms, after_mlp, peak
 
     def finish(self, live, previous, ingress):
-        back_ms, back_ws = self.transfer(previous, ingress)
-        m, tokens = self.model, self.tokens(ingress)
-        peak = tuple(a + max(b, int(m.byte_scale * n * (4 * m.vocab + 4 * m.hidden)))
-                     for a, b, n in zip(live, back_ws, tokens))
+        """(ms, peak bytes) of the return to the ingress layout, the head and the per-microbatch cost."""
+        m = self.model
+        back_ms, back_work = self.transfer(previous, ingress)
+        tokens = self.tokens(ingress)
+        logits = [self._scaled(n * (4 * m.vocab + 4 * m.hidden)) for n in tokens]
+        peak = tuple(x + max(w, lg) for x, w, lg in zip(live, back_work, logits))
         head_ms = max(tokens) * 6 * m.hidden * m.vocab / (m.compute_tflops * 1e9)
         return back_ms + head_ms + m.microbatch_ms, peak
 
     def evaluate(self, batch) -> dict:
         live, previous = self.initial(batch.ingress), batch.ingress
         peak, total, points = live, 0.0, []
-        for index, (symbol, (attention, mlp)) in enumerate(zip(self.pattern, batch.layers)):
-            cost, live, here = self.layer(live, previous, attention, mlp, symbol)
-            peak = tuple(max(a, b) for a, b in zip(peak, here))
-            total += cost
+        for index, symbol in enumerate(self.pattern):
+            attention, mlp = batch.layers[index]
+            ms, live, here = self.layer(live, previous, attention, mlp, symbol)
+            total += ms
+            peak = tuple(map(max, peak, here))
             points.append({"layer": index, "saved_live_bytes": list(live), "peak_bytes": list(here),
                            "attention_tokens": self.tokens(attention), "mlp_tokens": self.tokens(mlp)})
             previous = attention
-        cost, here = self.finish(live, previous, batch.ingress)
-        peak = tuple(max(a, b) for a, b in zip(peak, here))
-        return {"predicted_ms": total + cost, "peak_bytes": peak, "fits": max(peak) <= self.model.budget,
+        ms, here = self.finish(live, previous, batch.ingress)
+        peak = tuple(map(max, peak, here))
+        return {"predicted_ms": total + ms, "peak_bytes": peak, "fits": max(peak) <= self.model.budget,
                 "points": points, "head_peak_bytes": here, "includes_margin": True,
                 "memory_status": "structural_forward_backward_envelope_not_measured"}
 

@@ -13,37 +13,62 @@ from __future__ import annotations
 from .joint.ir import Group as JGroup, Layout, Microbatch, Plan as JointPlan
 
 
+def round_load(groups, lengths, world: int) -> tuple[list[int], list[int]]:
+    """Per-rank (tokens, packed sequences) one scheduling round puts on every rank."""
+    tokens, seqs = [0] * world, [0] * world
+    for g in groups:
+        share, rest = divmod(sum(lengths[i] for i in g.ids), len(g.ranks))
+        if rest:
+            raise ValueError("CP token count is not integral")
+        for r in g.ranks:
+            tokens[r] += share
+            seqs[r] += len(g.ids)
+    return tokens, seqs
+
+
+class _Window:
+    """Rounds merged into one microbatch so far, with their per-rank totals."""
+
+    def __init__(self, world: int):
+        self.rounds: list[int] = []
+        self.tokens, self.seqs = [0] * world, [0] * world
+
+    def admits(self, tokens, seqs, token_cap: int, max_sequences) -> bool:
+        if any(a + b > token_cap for a, b in zip(self.tokens, tokens)):
+            return False
+        return max_sequences is None or all(a + b <= max_sequences for a, b in zip(self.seqs, seqs))
+
+    def take(self, ordinal: int, tokens, seqs) -> None:
+        self.rounds.append(ordinal)
+        self.tokens = [a + b for a, b in zip(self.tokens, tokens)]
+        self.seqs = [a + b for a, b in zip(self.seqs, seqs)]
+
+
 def coalesce_rounds(plan, lengths, world, token_cap, max_sequences=None):
-    batches, current = [], []
-    tokens, counts = [0] * world, [0] * world
+    """Consecutive rounds of a 1-D plan merged greedily into windows (tuples of round
+    indices) whose per-rank token and sequence totals stay within the caps."""
+    windows, window = [], _Window(world)
     for ordinal, groups in enumerate(plan):
-        added, seqs = [0] * world, [0] * world
-        for g in groups:
-            total = sum(lengths[i] for i in g.ids)
-            if total % len(g.ranks):
-                raise ValueError("CP token count is not integral")
-            for r in g.ranks:
-                added[r] += total // len(g.ranks)
-                seqs[r] += len(g.ids)
-        if any(n > token_cap for n in added):
+        tokens, seqs = round_load(groups, lengths, world)
+        if max(tokens) > token_cap:
             raise ValueError("Original round exceeds token capacity")
-        over = any(a + b > token_cap for a, b in zip(tokens, added)) or (
-            max_sequences is not None and any(a + b > max_sequences for a, b in zip(counts, seqs)))
-        if current and over:
-            batches.append(tuple(current))
-            current, tokens, counts = [], [0] * world, [0] * world
-        current.append(ordinal)
-        tokens = [a + b for a, b in zip(tokens, added)]
-        counts = [a + b for a, b in zip(counts, seqs)]
-    if current:
-        batches.append(tuple(current))
-    return tuple(batches)
+        if window.rounds and not window.admits(tokens, seqs, token_cap, max_sequences):
+            windows.append(tuple(window.rounds))
+            window = _Window(world)
+        window.take(ordinal, tokens, seqs)
+    if window.rounds:
+        windows.append(tuple(window.rounds))
+    return tuple(windows)
 
 
 def local_execution_groups(state: dict, ordinal: int, rank: int):
-    rounds = state.get("execution_rounds")
-    indices = rounds[ordinal] if rounds is not None else (ordinal,)
-    return tuple(next(g for g in state["plan"][i] if rank in g.ranks) for i in indices)
+    """The groups ``rank`` runs in execution window ``ordinal`` (one per merged round)."""
+    windows = state.get("execution_rounds")
+    members = (ordinal,) if windows is None else windows[ordinal]
+    picked = []
+    for i in members:
+        picked.append(next(g for g in state["plan"][i] if rank in g.ranks))
+    return tuple(picked)
 
 
 def to_joint(plan, lengths, world: int, pattern: str, token_cap: int | None = None,
@@ -58,16 +83,13 @@ def to_joint(plan, lengths, world: int, pattern: str, token_cap: int | None = No
                else tuple((i,) for i in range(len(plan))))
     mbs = []
     for window in windows:
-        merged: dict[tuple, list[int]] = {}
         conflict = False
         owner: dict[int, tuple] = {}
         for i in window:
             for g in plan[i]:
                 for r in g.ranks:
-                    if r in owner and owner[r] != g.ranks:
+                    if owner.setdefault(r, g.ranks) != g.ranks:
                         conflict = True
-                    owner[r] = g.ranks
-                merged.setdefault(g.ranks, []).extend(g.ids)
         parts = [[i] for i in window] if conflict else [list(window)]
         for part in parts:
             groups: dict[tuple, list[int]] = {}

@@ -200,10 +200,10 @@ def test_cp_overhead_factor_lookup_and_measured_ratio():
     from prism_cp_b200.planner.calibrate import calibrated
     from prism_cp_b200.planner.cli import B200_ENVELOPE
     from prism_cp_b200.planner.fixed import uniform_plan
-    from prism_cp_b200.planner.joint.cost import Evaluator, _cp_factor, model_from_config
+    from prism_cp_b200.planner.joint.cost import Evaluator, cp_overhead_factor, model_from_config
     table = {"2": 1.1, "8": 1.3}
-    assert _cp_factor(table, 2) == 1.1 and _cp_factor(table, 4) == 1.1 and _cp_factor(table, 8) == 1.3
-    assert _cp_factor({"4": 1.2}, 2) == 1.2
+    assert cp_overhead_factor(table, 2) == 1.1 and cp_overhead_factor(table, 4) == 1.1 and cp_overhead_factor(table, 8) == 1.3
+    assert cp_overhead_factor({"4": 1.2}, 2) == 1.2
     cfg = PRESETS["hybrid-1.3b"]()
     m = calibrated(model_from_config(cfg, B200_ENVELOPE["device_bytes"],
                                      **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"}))
