@@ -84,8 +84,8 @@ class Analytic:
     def price(self, symbol, cp, parts: Parts, tokens, squares, cross_node) -> float:
         return parts.ideal + parts.comm
 
-    def max_attention_cp(self):
-        return None
+    def allows_attention_cp(self, cp: int) -> bool:
+        return True
 
     def coverage(self, plan, lengths) -> dict:
         return {"policy": self.name}
@@ -191,8 +191,8 @@ class Residual:
         value = ideal + residual + max(0.0, parts.comm - parts.comm_local)
         return value * self.gdn32 if cp == 32 else value
 
-    def max_attention_cp(self):
-        return None
+    def allows_attention_cp(self, cp: int) -> bool:
+        return True
 
     # ---------------------------------------------------------------- evidence
     def coverage(self, plan, lengths) -> dict:
@@ -305,9 +305,13 @@ class Anchors:
         at_anchor = operator_work(self.model, symbol, self.tokens, self.tokens * self.tokens)
         return self._anchor_ms(kind, cp, cross_node) * operator_work(self.model, symbol, tokens, squares) / at_anchor
 
-    def max_attention_cp(self):
-        """The reference limits attention CP to the H100 profile's largest measured degree."""
-        return max(map(int, self.anchors["GQA"]["milliseconds"])) if self.schema == H100_SCHEMA else None
+    def allows_attention_cp(self, cp: int) -> bool:
+        """Attention CP stays within the profile's largest measured degree (the reference's rule
+        for its H100 profile); the B200 profile also needs that exact degree measured."""
+        measured = self.anchors["GQA"]["milliseconds"]
+        if cp > max(map(int, measured)):
+            return False
+        return self.schema == H100_SCHEMA or str(cp) in measured
 
     def coverage(self, plan, lengths) -> dict:
         domain = tuple(int(c) for c in self.anchors["GQA"]["milliseconds"])

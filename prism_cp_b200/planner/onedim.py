@@ -1,19 +1,26 @@
 """One-dimensional CP planner: one set of CP groups for every layer of a microbatch.
 
-API (same names and semantics as the reference's planner,
-experiments/sequence_dynamic_cp/planner.py:18-475):
+A plan is a tuple of microbatches ("rounds"); a microbatch is a tuple of
+``Group(ranks, ids)``, each an aligned dyadic rank interval running some whole
+samples at CP = len(ranks). The API is the reference planner's
+(planner.py:18-475) so its callers and stored plans carry over:
 
-* ``Constraints(world, token_cap, min_cp, max_sequences, alignment)``
-* ``Group(ranks, ids)``; a plan is a tuple of microbatches, each a tuple of groups
-* ``from_rank_ids`` / ``to_rank_ids``: the executor's replicated sample-id codec
-* ``validate``: aligned dyadic groups, capacity, exactly-once coverage
-* ``ProxyCost(a, b)``: ``a * Q + b * L`` per group (Q in Ki^2/cp, L in Ki/cp);
-  ``beta_tokens = b / a * 1024`` is the weighted-native ablation
-* ``ExactCosts``: measured complete-plan table keyed by ``fingerprint``
-* ``native_plan``, ``pack_layout`` (LPT into a fixed CP-size vector), ``layouts``
-  (homogeneous + dyadic neighbours of native), local move/swap ``search`` with the
-  short-sequence refinement pass, ``select`` (measured > proxy opt-in > native),
-  ``export_plan`` and ``models`` (CP1 stack coefficients).
+* ``Constraints(world, token_cap, min_cp, max_sequences, alignment)``;
+* ``from_rank_ids`` / ``to_rank_ids``: the executor's replicated sample-id codec;
+* ``validate``: group legality, per-rank capacity, exactly-once coverage;
+* ``ProxyCost(a, b)``: ``a * Q + b * L`` per group (Q in Ki^2 / cp, L in Ki / cp);
+  ``beta_tokens = b / a * 1024`` weights the native scheduler's workload;
+* ``ExactCosts``: measured complete-plan times keyed by ``fingerprint``;
+* ``search``: a finite candidate pool - the native scheduler's plans, an LPT
+  packing of every layout in a small family, a budgeted local search of
+  sample moves and swaps around the best one, then the short-sequence split;
+  ``select`` (measured > proxy opt-in > native) and ``export_plan``.
+
+Design: a ``_Pool`` owns the candidates (deduplicated by fingerprint, first
+insertion wins numerical ties); ``_Lpt`` fills one round of a layout;
+``neighbours`` enumerates one-step changes of a plan in a fixed order, so the
+evaluation budget - not wall time - bounds the search and every rank computes
+the same schedule.
 """
 
 from __future__ import annotations
@@ -37,6 +44,10 @@ class Group:
 Plan = tuple  # tuple[tuple[Group, ...], ...]
 
 
+def _pow2(v: int) -> bool:
+    return v >= 1 and v & (v - 1) == 0
+
+
 @dataclass(frozen=True)
 class Constraints:
     world: int
@@ -46,67 +57,87 @@ class Constraints:
     alignment: int = 1
 
     def __post_init__(self):
-        for v in (self.world, self.min_cp):
-            if v < 1 or v & (v - 1):
-                raise ValueError("First version requires power-of-two world and min_cp")
-        if self.min_cp > self.world or self.token_cap < 1 or self.alignment < 1:
+        if not (_pow2(self.world) and _pow2(self.min_cp)):
+            raise ValueError("First version requires power-of-two world and min_cp")
+        if self.min_cp > self.world or min(self.token_cap, self.alignment) < 1:
             raise ValueError("Invalid CP/token/alignment constraint")
         if self.max_sequences is not None and self.max_sequences < 1:
             raise ValueError("max_sequences must be positive")
 
 
+# ------------------------------------------------------------------ codec
 def from_rank_ids(batches) -> Plan:
-    out = []
-    for batch in batches:
-        owners: dict[tuple, list[int]] = {}
-        for rank, ids in enumerate(batch):
-            owners.setdefault(tuple(ids), []).append(rank)
-        out.append(tuple(Group(tuple(r), ids) for ids, r in owners.items()))
-    return tuple(out)
+    """Per-rank sample lists (ranks sharing a list form one group) to a plan."""
+    plan = []
+    for per_rank in batches:
+        teams: dict[tuple, list[int]] = {}
+        for rank, ids in enumerate(per_rank):
+            teams.setdefault(tuple(ids), []).append(rank)
+        plan.append(tuple(Group(tuple(ranks), ids) for ids, ranks in teams.items()))
+    return tuple(plan)
 
 
 def to_rank_ids(plan: Plan, world: int):
+    """A plan to per-rank sample lists (every rank of a group lists the group's samples)."""
     out = []
     for batch in plan:
-        ranks: list[list[int]] = [[] for _ in range(world)]
-        for g in batch:
-            for r in g.ranks:
-                ranks[r] = list(g.ids)
-        out.append(ranks)
+        owner = {r: g.ids for g in batch for r in g.ranks}
+        out.append([list(owner.get(r, ())) for r in range(world)])
     return out
 
 
+# ------------------------------------------------------------------ legality
+def _group_problem(g: Group, lengths: dict, limits: Constraints):
+    """The first rule ``g`` breaks (as an error message), or None."""
+    cp = len(g.ranks)
+    if not _pow2(cp) or cp < limits.min_cp or not g.ids:
+        return "Empty or unsupported CP group"
+    if g.ranks[0] % cp or g.ranks != tuple(range(g.ranks[0], g.ranks[0] + cp)):
+        return "CP group must match a precreated aligned contiguous group"
+    if not all(i in lengths for i in g.ids):
+        return "Unknown sample ID"
+    if cp > 1 and any(lengths[i] % (2 * cp) for i in g.ids):
+        return "THD zigzag requires sequence padding divisible by 2*CP"
+    if sum(lengths[i] for i in g.ids) > limits.token_cap * cp:
+        return "Per-rank token capacity exceeded"
+    if limits.max_sequences is not None and len(g.ids) > limits.max_sequences:
+        return "Real packed-sequence capacity exceeded"
+    return None
+
+
 def validate(plan: Plan, lengths: dict, limits: Constraints) -> None:
-    if any(not isinstance(i, int) or not isinstance(n, int) or n <= 0 or n % limits.alignment
-           for i, n in lengths.items()):
-        raise ValueError("IDs/lengths must be integers; lengths must be positive and aligned")
+    """Raise ValueError unless every microbatch covers every rank with one legal group and
+    every sample runs exactly once in the step."""
+    for i, n in lengths.items():
+        if not isinstance(i, int) or not isinstance(n, int) or n <= 0 or n % limits.alignment:
+            raise ValueError("IDs/lengths must be integers; lengths must be positive and aligned")
     if not plan or not lengths:
         raise ValueError("Empty steps are unsupported")
-    seen = []
+    placed = []
     for batch in plan:
-        ranks = []
+        covered = []
         for g in batch:
-            cp = len(g.ranks)
-            if not cp or cp & (cp - 1) or cp < limits.min_cp or not g.ids:
-                raise ValueError("Empty or unsupported CP group")
-            if g.ranks[0] % cp or g.ranks != tuple(range(g.ranks[0], g.ranks[0] + cp)):
-                raise ValueError("CP group must match a precreated aligned contiguous group")
-            if any(i not in lengths for i in g.ids):
-                raise ValueError("Unknown sample ID")
-            if cp > 1 and any(lengths[i] % (2 * cp) for i in g.ids):
-                raise ValueError("THD zigzag requires sequence padding divisible by 2*CP")
-            if sum(lengths[i] for i in g.ids) > limits.token_cap * cp:
-                raise ValueError("Per-rank token capacity exceeded")
-            if limits.max_sequences is not None and len(g.ids) > limits.max_sequences:
-                raise ValueError("Real packed-sequence capacity exceeded")
-            ranks.extend(g.ranks)
-            seen.extend(g.ids)
-        if sorted(ranks) != list(range(limits.world)):
+            problem = _group_problem(g, lengths, limits)
+            if problem:
+                raise ValueError(problem)
+            covered += g.ranks
+            placed += g.ids
+        if sorted(covered) != list(range(limits.world)):
             raise ValueError("All ranks must execute exactly one nonempty group per microbatch")
-    if sorted(seen) != sorted(lengths):
+    if sorted(placed) != sorted(lengths):
         raise ValueError("Samples must appear exactly once at group level across the full step")
 
 
+def group_fits(ids, cp: int, lengths: dict, limits: Constraints) -> bool:
+    """Whether samples ``ids`` may form one CP-``cp`` group (capacity, count, zigzag split)."""
+    if not ids or sum(lengths[i] for i in ids) > cp * limits.token_cap:
+        return False
+    if limits.max_sequences is not None and len(ids) > limits.max_sequences:
+        return False
+    return cp == 1 or all(lengths[i] % (2 * cp) == 0 for i in ids)
+
+
+# ------------------------------------------------------------------ costs
 @dataclass(frozen=True)
 class ProxyCost:
     name: str
@@ -115,7 +146,8 @@ class ProxyCost:
     provenance: str = "conditional_CP1_compute_divided_by_CP"
 
     def __post_init__(self):
-        if not all(math.isfinite(v) and v >= 0 for v in (self.a, self.b)) or self.a + self.b == 0:
+        valid = all(math.isfinite(v) and v >= 0 for v in (self.a, self.b))
+        if not valid or self.a + self.b == 0:
             raise ValueError("Cost coefficients must be finite, nonnegative and nonzero")
 
     @property
@@ -126,12 +158,14 @@ class ProxyCost:
 
     def group(self, group: Group, lengths: dict) -> dict:
         cp = len(group.ranks)
-        q = sum((lengths[i] / 1024) ** 2 for i in group.ids) / cp
-        l = sum(lengths[i] / 1024 for i in group.ids) / cp
-        return {"q_ki2": q, "l_ki": l, "quadratic": self.a * q, "linear": self.b * l,
-                "cost": self.a * q + self.b * l}
+        ki = [lengths[i] / 1024 for i in group.ids]
+        q = sum(x ** 2 for x in ki) / cp
+        lin = sum(ki) / cp
+        return {"q_ki2": q, "l_ki": lin, "quadratic": self.a * q, "linear": self.b * lin,
+                "cost": self.a * q + self.b * lin}
 
     def evaluate(self, plan: Plan, lengths: dict) -> float:
+        """Sum over microbatches of the slowest group's cost."""
         return sum(max(self.group(g, lengths)["cost"] for g in batch) for batch in plan)
 
 
@@ -140,214 +174,249 @@ def fingerprint(plan: Plan, lengths: dict) -> str:
 
 
 class ExactCosts:
-    """Complete-plan timings frozen for one model/runtime/topology contract."""
+    """Complete-plan timings measured for one model / runtime / topology contract.
+    Only rows that ran ("ok") and passed their numerical gate can be selected."""
 
     def __init__(self, data: dict, contract: dict):
         if data["contract"] != contract:
             raise ValueError("Measured costs do not match model/backend/topology contract")
         self.scope = data["scope"]
+        keys = [row["fingerprint"] for row in data["records"]]
+        if len(set(keys)) != len(keys):
+            raise ValueError("Duplicate exact-plan measurement")
         self.records = {}
-        seen = set()
         for row in data["records"]:
-            key = row["fingerprint"]
-            if key in seen:
-                raise ValueError("Duplicate exact-plan measurement")
-            seen.add(key)
-            if row["status"] == "ok" and row["numerical_pass"] is True:
-                v = row["milliseconds"]
-                if not math.isfinite(v) or v <= 0:
-                    raise ValueError("Invalid complete-plan measurement")
-                self.records[key] = row
+            if row["status"] != "ok" or row["numerical_pass"] is not True:
+                continue
+            if not (math.isfinite(row["milliseconds"]) and row["milliseconds"] > 0):
+                raise ValueError("Invalid complete-plan measurement")
+            self.records[row["fingerprint"]] = row
 
     def evaluate(self, plan: Plan, lengths: dict):
         row = self.records.get(fingerprint(plan, lengths))
-        return row["milliseconds"] if row else None
+        return None if row is None else row["milliseconds"]
 
 
 def native_plan(lengths: dict, limits: Constraints, cost: ProxyCost) -> Plan:
-    plan = from_rank_ids(replay(list(lengths.items()), limits.world, limits.token_cap, limits.min_cp,
-                                cost.beta_tokens))
+    rank_ids = replay(list(lengths.items()), limits.world, limits.token_cap, limits.min_cp, cost.beta_tokens)
+    plan = from_rank_ids(rank_ids)
     validate(plan, lengths, limits)
     return plan
 
 
-def _fits(ids, cp, lengths, limits) -> bool:
-    return (bool(ids) and sum(lengths[i] for i in ids) <= cp * limits.token_cap
-            and (limits.max_sequences is None or len(ids) <= limits.max_sequences)
-            and (cp == 1 or all(lengths[i] % (2 * cp) == 0 for i in ids)))
+# ------------------------------------------------------------------ layout packing
+class _Lpt:
+    """One round of a fixed CP-size layout, filled longest sample first: each sample goes to the
+    group that keeps the round's slowest group fastest (then the cheaper group, then the lower index)."""
+
+    def __init__(self, sizes, lengths, limits, cost):
+        self.lengths, self.limits, self.cost = lengths, limits, cost
+        starts = [sum(sizes[:j]) for j in range(len(sizes))]
+        self.groups = [Group(tuple(range(a, a + cp)), ()) for a, cp in zip(starts, sizes)]
+        self.ms = [0.0] * len(sizes)
+
+    def _allowed(self, ids, cp) -> bool:
+        if not group_fits(ids, cp, self.lengths, self.limits):
+            return False
+        check = getattr(self.cost, "feasible_group", None)
+        return check is None or check(ids, cp, self.lengths)
+
+    def place(self, i) -> bool:
+        best = None
+        for j, g in enumerate(self.groups):
+            ids = g.ids + (i,)
+            if not self._allowed(ids, len(g.ranks)):
+                continue
+            new = self.cost.group(Group(g.ranks, ids), self.lengths)["cost"]
+            others = max((v for k, v in enumerate(self.ms) if k != j), default=0)
+            option = (max(new, others), self.ms[j], j, new)
+            best = option if best is None or option < best else best
+        if best is None:
+            return False
+        j, new = best[2], best[3]
+        self.groups[j] = Group(self.groups[j].ranks, self.groups[j].ids + (i,))
+        self.ms[j] = new
+        return True
 
 
 def pack_layout(lengths: dict, limits: Constraints, sizes: tuple[int, ...], cost) -> Plan:
-    """LPT-pack the whole step into a fixed CP-size vector; a partial tail is repacked
-    on one world-wide group instead of leaving ranks idle."""
+    """LPT-pack the whole step into rounds of the CP-size vector ``sizes``. A round that would
+    leave a group empty (ranks idle) is replaced by one world-wide group instead."""
     if sum(sizes) != limits.world:
         raise ValueError("Layout must cover the world")
-    remaining = sorted(lengths, key=lambda i: (-lengths[i], i))
-    out = []
-    while remaining:
-        groups, start = [], 0
-        for cp in sizes:
-            groups.append(Group(tuple(range(start, start + cp)), ()))
-            start += cp
-        costs = [0.0] * len(groups)
-        leftovers = []
-        for i in remaining:
-            options = []
-            for j, g in enumerate(groups):
-                ids = (*g.ids, i)
-                if _fits(ids, len(g.ranks), lengths, limits) and (
-                        not hasattr(cost, "feasible_group") or cost.feasible_group(ids, len(g.ranks), lengths)):
-                    new = cost.group(Group(g.ranks, ids), lengths)["cost"]
-                    worst = max(new, max((v for k, v in enumerate(costs) if k != j), default=0))
-                    options.append((worst, costs[j], j, new))
-            if not options:
-                leftovers.append(i)
-                continue
-            _, _, j, new = min(options)
-            groups[j] = Group(groups[j].ranks, (*groups[j].ids, i))
-            costs[j] = new
-        if any(not g.ids for g in groups):
-            picked, leftovers = [], []
-            for i in remaining:
-                (picked if _fits((*picked, i), limits.world, lengths, limits) else leftovers).append(i)
-            groups = [Group(tuple(range(limits.world)), tuple(picked))]
-        if len(leftovers) == len(remaining):
+    queue = sorted(lengths, key=lambda i: (-lengths[i], i))
+    rounds = []
+    while queue:
+        lpt = _Lpt(sizes, lengths, limits, cost)
+        rest = [i for i in queue if not lpt.place(i)]
+        groups = lpt.groups
+        if not all(g.ids for g in groups):
+            taken, rest = [], []
+            for i in queue:
+                if group_fits(tuple(taken) + (i,), limits.world, lengths, limits):
+                    taken.append(i)
+                else:
+                    rest.append(i)
+            groups = [Group(tuple(range(limits.world)), tuple(taken))]
+        if len(rest) == len(queue):
             raise ValueError("No feasible group for the next sequence")
-        out.append(tuple(groups))
-        remaining = leftovers
-    plan = tuple(out)
+        rounds.append(tuple(groups))
+        queue = rest
+    plan = tuple(rounds)
     validate(plan, lengths, limits)
     return plan
 
 
 def layouts(limits: Constraints, seeds) -> list[tuple[int, ...]]:
-    found = set()
-    cp = limits.min_cp
-    while cp <= limits.world:
-        found.add((cp,) * (limits.world // cp))
-        cp *= 2
+    """CP-size vectors to pack: every homogeneous layout, every layout a seed plan uses, and
+    each of those with one group halved or two equal aligned neighbours merged."""
+    family = {(cp,) * (limits.world // cp) for cp in (1 << e for e in range(limits.world.bit_length()))
+              if limits.min_cp <= cp <= limits.world}
     for plan in seeds:
         for batch in plan:
             sizes = tuple(len(g.ranks) for g in batch)
-            found.add(sizes)
+            family.add(sizes)
             for j, s in enumerate(sizes):
                 if s > limits.min_cp:
-                    found.add((*sizes[:j], s // 2, s // 2, *sizes[j + 1:]))
-                if j + 1 < len(sizes) and s == sizes[j + 1] and sum(sizes[:j]) % (2 * s) == 0:
-                    found.add((*sizes[:j], 2 * s, *sizes[j + 2:]))
-    return sorted(found)
+                    family.add(sizes[:j] + (s // 2, s // 2) + sizes[j + 1:])
+                mergeable = j + 1 < len(sizes) and sizes[j + 1] == s and sum(sizes[:j]) % (2 * s) == 0
+                if mergeable:
+                    family.add(sizes[:j] + (2 * s,) + sizes[j + 2:])
+    return sorted(family)
 
 
-def _neighbors(plan: Plan, lengths: dict, limits: Constraints):
-    locs = [(m, j) for m, batch in enumerate(plan) for j in range(len(batch))]
+# ------------------------------------------------------------------ local search
+def neighbours(plan: Plan, lengths: dict, limits: Constraints):
+    """Plans one step away from ``plan``, in a fixed order: first every move of one sample out of
+    a group that keeps another sample into any other group of the step, then every swap of two
+    samples of different lengths between two groups."""
+    sites = [(m, j) for m, batch in enumerate(plan) for j in range(len(batch))]
+    at = {site: plan[site[0]][site[1]] for site in sites}
 
-    def replace(changes):
+    def edited(changes: dict) -> Plan:
         return tuple(tuple(changes.get((m, j), g) for j, g in enumerate(batch)) for m, batch in enumerate(plan))
 
-    for src_loc in locs:
-        src = plan[src_loc[0]][src_loc[1]]
-        if len(src.ids) < 2:
+    def fits(g: Group, ids) -> bool:
+        return group_fits(ids, len(g.ranks), lengths, limits)
+
+    for src in sites:
+        a = at[src]
+        if len(a.ids) < 2:
             continue
-        for i in src.ids:
-            for dst_loc in locs:
-                if dst_loc == src_loc:
-                    continue
-                dst = plan[dst_loc[0]][dst_loc[1]]
-                ids = (*dst.ids, i)
-                if _fits(ids, len(dst.ranks), lengths, limits):
-                    yield replace({src_loc: Group(src.ranks, tuple(k for k in src.ids if k != i)),
-                                   dst_loc: Group(dst.ranks, ids)})
-    for x, src_loc in enumerate(locs):
-        src = plan[src_loc[0]][src_loc[1]]
-        for dst_loc in locs[x + 1:]:
-            dst = plan[dst_loc[0]][dst_loc[1]]
-            for i in src.ids:
-                for k in dst.ids:
+        for i in a.ids:
+            kept = tuple(k for k in a.ids if k != i)
+            for dst in sites:
+                b = at[dst]
+                if dst != src and fits(b, b.ids + (i,)):
+                    yield edited({src: Group(a.ranks, kept), dst: Group(b.ranks, b.ids + (i,))})
+    for x, src in enumerate(sites):
+        a = at[src]
+        for dst in sites[x + 1:]:
+            b = at[dst]
+            for i in a.ids:
+                for k in b.ids:
                     if lengths[i] == lengths[k]:
                         continue
-                    a = tuple(k if n == i else n for n in src.ids)
-                    b = tuple(i if n == k else n for n in dst.ids)
-                    if _fits(a, len(src.ranks), lengths, limits) and _fits(b, len(dst.ranks), lengths, limits):
-                        yield replace({src_loc: Group(src.ranks, a), dst_loc: Group(dst.ranks, b)})
+                    ids_a = tuple(k if n == i else n for n in a.ids)
+                    ids_b = tuple(i if n == k else n for n in b.ids)
+                    if fits(a, ids_a) and fits(b, ids_b):
+                        yield edited({src: Group(a.ranks, ids_a), dst: Group(b.ranks, ids_b)})
+
+
+def _improves(value: float, current: float) -> bool:
+    """Strictly better beyond a relative 1e-9, so 1-ULP differences never decide."""
+    return value < current - 1e-9 * max(1.0, abs(current))
+
+
+class _Pool:
+    """Legal candidate plans keyed by fingerprint; the first plan with a fingerprint keeps its name."""
+
+    def __init__(self, lengths, limits, cost):
+        self.lengths, self.limits, self.cost = lengths, limits, cost
+        self.rows: dict[str, dict] = {}
+        self.failures: list[dict] = []
+
+    def add(self, name: str, plan: Plan) -> dict:
+        validate(plan, self.lengths, self.limits)
+        key = fingerprint(plan, self.lengths)
+        if key not in self.rows:
+            self.rows[key] = {"name": name, "plan": plan, "proxy_cost": self.cost.evaluate(plan, self.lengths),
+                              "fingerprint": key}
+        return self.rows[key]
+
+    def attempt(self, name: str, make, label: str | None = None):
+        try:
+            return self.add(name, make())
+        except (ValueError, AssertionError) as error:
+            self.failures.append({"candidate": label or name, "reason": str(error)})
+            return None
+
+    def leader(self) -> dict:
+        """Lowest proxy cost; insertion order (native first) breaks numerical ties."""
+        rows = iter(self.rows.values())
+        best = next(rows)
+        for row in rows:
+            if _improves(row["proxy_cost"], best["proxy_cost"]):
+                best = row
+        return best
 
 
 def search(lengths: dict, limits: Constraints, cost, local_evaluations: int = 128, rounds: int = 2) -> dict:
-    """Finite legal candidates (native seeds, layout packings, local moves/swaps,
-    short-sequence split). A deterministic evaluation budget, not wall time, so
-    every rank computes the same schedule."""
+    """A finite pool of legal plans and the best one under ``cost`` (see the module docstring)."""
     started = time.perf_counter()
     if local_evaluations < 0 or rounds < 0:
         raise ValueError("Search budgets must be nonnegative")
-    candidates: dict[str, dict] = {}
-    failures = []
-
-    def add(name, plan):
-        validate(plan, lengths, limits)
-        key = fingerprint(plan, lengths)
-        if key not in candidates:
-            candidates[key] = {"name": name, "plan": plan, "proxy_cost": cost.evaluate(plan, lengths),
-                               "fingerprint": key}
-
+    pool = _Pool(lengths, limits, cost)
     seeds = []
-    for name, model in (("native_square", ProxyCost("square", 1, 0)),
+    for name, proxy in (("native_square", ProxyCost("square", 1, 0)),
                         ("native_weighted", getattr(cost, "seed_proxy", cost))):
-        try:
-            plan = native_plan(lengths, limits, model)
-            seeds.append(plan)
-            add(name, plan)
-        except (ValueError, AssertionError) as error:
-            failures.append({"candidate": name, "reason": str(error)})
+        row = pool.attempt(name, lambda proxy=proxy: native_plan(lengths, limits, proxy))
+        if row is not None:
+            seeds.append(row["plan"])
     for sizes in layouts(limits, seeds):
+        name = "layout_" + "x".join(map(str, sizes))
         try:
-            add("layout_" + "x".join(map(str, sizes)), pack_layout(lengths, limits, sizes, cost))
+            pool.add(name, pack_layout(lengths, limits, sizes, cost))
         except ValueError as error:
-            failures.append({"candidate": str(sizes), "reason": str(error)})
-    if not candidates:
+            pool.failures.append({"candidate": str(sizes), "reason": str(error)})
+    if not pool.rows:
         raise ValueError("No legal candidate for this complete step")
-
-    def better(v, cur):
-        return v < cur - 1e-9 * max(1.0, abs(cur))
-
-    best = next(iter(candidates.values()))
-    for c in candidates.values():
-        if better(c["proxy_cost"], best["proxy_cost"]):
-            best = c
-    used = 0
+    best, spent = pool.leader(), 0
     for _ in range(rounds):
-        prev = best
-        for plan in _neighbors(prev["plan"], lengths, limits):
-            if used >= local_evaluations:
+        centre = best
+        for plan in neighbours(centre["plan"], lengths, limits):
+            if spent >= local_evaluations:
                 break
-            used += 1
+            spent += 1
             try:
-                add("local_move_or_swap", plan)
+                row = pool.add("local_move_or_swap", plan)
             except ValueError as error:
-                failures.append({"candidate": "local_move_or_swap", "reason": str(error)})
+                pool.failures.append({"candidate": "local_move_or_swap", "reason": str(error)})
                 continue
-            v = cost.evaluate(plan, lengths)
-            if better(v, best["proxy_cost"]):
-                best = candidates[fingerprint(plan, lengths)]
-        if best is prev or used >= local_evaluations:
+            if _improves(cost.evaluate(plan, lengths), best["proxy_cost"]):
+                best = row
+        if best is centre or spent >= local_evaluations:
             break
+    # a separate pass: moves cannot split the winner's rank domains into smaller CP groups
     from .short_sequence import refine_short_sequences
     refinement = refine_short_sequences(best["plan"], lengths, limits, cost)
     if refinement["plan"] != best["plan"]:
-        add("short_sequence_split", refinement["plan"])
-        best = candidates[fingerprint(refinement["plan"], lengths)]
-    return {"selected": best, "candidates": list(candidates.values()), "failures": failures,
-            "local_evaluations": used,
+        best = pool.add("short_sequence_split", refinement["plan"])
+    return {"selected": best, "candidates": list(pool.rows.values()), "failures": pool.failures,
+            "local_evaluations": spent,
             "short_sequence_refinement": {k: v for k, v in refinement.items() if k != "plan"},
             "planning_ms": (time.perf_counter() - started) * 1000, "selection_provenance": cost.provenance,
             "parameter_sync_optimizer": "unknown"}
 
 
 def select(result: dict, lengths: dict, measured: ExactCosts | None = None, allow_proxy: bool = False):
+    """(candidate, basis): the fastest measured candidate when the table also measures the native
+    plan, else the proxy's choice if explicitly allowed, else the native plan."""
     native = next((c for c in result["candidates"] if c["name"] == "native_square"), None)
-    if measured:
-        known = [(measured.evaluate(c["plan"], lengths), j, c) for j, c in enumerate(result["candidates"])]
-        known = [(v, j, c) for v, j, c in known if v is not None]
-        if known and native and measured.evaluate(native["plan"], lengths) is not None:
-            return min(known, key=lambda r: (r[0], r[1]))[2], "measured_complete_plan"
+    if measured and native is not None and measured.evaluate(native["plan"], lengths) is not None:
+        timed = [(measured.evaluate(c["plan"], lengths), j) for j, c in enumerate(result["candidates"])]
+        timed = [t for t in timed if t[0] is not None]
+        return result["candidates"][min(timed)[1]], "measured_complete_plan"
     if allow_proxy:
         return result["selected"], "experimental_compute_proxy"
     if native is None:
@@ -356,19 +425,21 @@ def select(result: dict, lengths: dict, measured: ExactCosts | None = None, allo
 
 
 def export_plan(plan: Plan, lengths: dict, cost: ProxyCost, node_size: int) -> dict:
+    """Complete ownership, cost components and the per-rank Q / L imbalance of every microbatch."""
     batches = []
     for batch in plan:
-        groups, rq, rl = [], [], []
+        groups, per_rank_q, per_rank_l = [], [], []
         for g in batch:
             parts = cost.group(g, lengths)
-            rq.extend([parts["q_ki2"]] * len(g.ranks))
-            rl.extend([parts["l_ki"]] * len(g.ranks))
+            per_rank_q += [parts["q_ki2"]] * len(g.ranks)
+            per_rank_l += [parts["l_ki"]] * len(g.ranks)
+            nodes = {r // node_size for r in g.ranks}
             groups.append(dict(ranks=g.ranks, sample_ids=g.ids, padded_lengths=[lengths[i] for i in g.ids],
-                               cp=len(g.ranks),
-                               placement="intra_node" if len({r // node_size for r in g.ranks}) == 1 else "cross_node",
+                               cp=len(g.ranks), placement="intra_node" if len(nodes) == 1 else "cross_node",
                                local_tokens=sum(lengths[i] for i in g.ids) / len(g.ranks), **parts))
-        batches.append({"groups": groups, "cost": max(g["cost"] for g in groups),
-                        "r_q": max(rq) / (sum(rq) / len(rq)), "r_l": max(rl) / (sum(rl) / len(rl))})
+        imbalance = lambda xs: max(xs) / (sum(xs) / len(xs))  # noqa: E731
+        batches.append({"groups": groups, "cost": max(g["cost"] for g in groups), "r_q": imbalance(per_rank_q),
+                        "r_l": imbalance(per_rank_l)})
     return {"microbatches": batches, "compute_proxy_cost": sum(b["cost"] for b in batches),
             "fingerprint": fingerprint(plan, lengths), "provenance": cost.provenance,
             "memory": "token_cap_only; measured_peak_required", "parameter_sync_optimizer": "unknown"}
@@ -377,8 +448,8 @@ def export_plan(plan: Plan, lengths: dict, cost: ProxyCost, node_size: int) -> d
 def models(path: Path) -> dict[str, ProxyCost]:
     """Proxy models from a CP1 stack-coefficient table (gpt = 4 GQA, hybrid = 1 GQA + 3 GDN)."""
     rows = json.loads(Path(path).read_text())
-    chosen = {}
+    by_counts = {(r["gqa_layers"], r["gdn_layers"]): r for r in reversed(rows)}
+    out = {"square": ProxyCost("square", 1.0, 0.0, "quadratic_work_proxy_Ki2")}
     for name, counts in (("gpt", (4, 0)), ("hybrid", (1, 3))):
-        row = next(r for r in rows if (r["gqa_layers"], r["gdn_layers"]) == counts)
-        chosen[name] = ProxyCost(name, row["A_ms_per_ki2"], row["B_ms_per_ki"])
-    return {"square": ProxyCost("square", 1.0, 0.0, "quadratic_work_proxy_Ki2"), **chosen}
+        out[name] = ProxyCost(name, by_counts[counts]["A_ms_per_ki2"], by_counts[counts]["B_ms_per_ki"])
+    return out
