@@ -2,11 +2,15 @@
 """Training throughput benchmark of the hybrid GDN:GQA decoder.
 
 Default workload: the 1.3B hybrid (24 layers, 18 GDN + 6 GQA, hidden 2048,
-vocab 32000), bf16, global batch of 8 documents x 32768 tokens (synthetic
-token ids uniform over the vocabulary, random-init weights), fixed CP = N on
-N GPUs (one team over all ranks; at N = 1 this is CP = 1 with 8 microbatches).
-``--workload lognormal`` runs 1M-token batches of log-normal documents
-(median 4K, clipped 512..128K) instead.
+vocab 32000), bf16, one global batch of 1M tokens of variable-length
+documents (lengths log-normal with median 4K, clipped to 512..128K, seeded,
+multiples of 16 tokens so the same batch runs at every N; synthetic token ids
+uniform over the vocabulary, random-init weights). The online planner picks
+the CP degree of the GDN and of the GQA layers for the batch on N GPUs from
+the calibrated B200 cost model and packs the documents into microbatches;
+a microbatch that holds more than 32K tokens on a rank (a document too long
+for its team) recomputes its layers in the backward. ``--workload fixed
+--plan uniform`` runs 8 documents x 32768 tokens at CP = N instead.
 
 Measured: W warm-up steps, then exactly K steps between barrier +
 synchronize, timed with CUDA events on the launching stream, max over ranks.
@@ -21,6 +25,7 @@ from __future__ import annotations
 
 import argparse
 import json
+from dataclasses import replace
 import os
 import statistics
 import subprocess
@@ -38,8 +43,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("native", "reference"), default="native")
     ap.add_argument("--model", default="hybrid-1.3b")
-    ap.add_argument("--workload", choices=("fixed", "lognormal"), default="fixed")
-    ap.add_argument("--plan", choices=("uniform", "online"), default="uniform",
+    ap.add_argument("--workload", choices=("fixed", "lognormal"), default="lognormal")
+    ap.add_argument("--plan", choices=("uniform", "online"), default="online",
                     help="uniform: CP = N for every layer; online: per-batch (cp_gdn, cp_gqa) from the "
                          "calibrated B200 cost model")
     ap.add_argument("--seqs", type=int, default=8)
@@ -50,6 +55,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--overlap-grad-reduce", action="store_true",
                     help="reduce-scatter gradient buckets during the last backward (side stream)")
+    ap.add_argument("--recompute-tokens", type=int, default=32768,
+                    help="microbatches with more tokens than this on a rank recompute their layers in the backward "
+                         "(0: never)")
     return ap.parse_args()
 
 
@@ -152,11 +160,13 @@ def main():
         lengths = fixed_lengths(args.seqs, args.seq_len)
         workload = {"global_batch": args.seqs, "seq_len": args.seq_len}
     else:
-        lengths = lognormal_lengths(args.total_tokens, 4096, 1.0, 512, 131072, 2 * world, args.seed)
-        workload = {"global_batch_tokens": sum(lengths), "documents": len(lengths), "seq_len": max(lengths),
+        # multiples of 16 tokens (the zigzag split of CP <= 8) at every N: one batch for the whole scaling curve
+        lengths = lognormal_lengths(args.total_tokens, 4096, 1.0, 512, 131072, 2 * max(world, 8), args.seed)
+        workload = {"global_batch": len(lengths), "global_batch_tokens": sum(lengths), "seq_len": max(lengths),
                     "lengths": "log-normal median 4096 sigma 1.0 clipped 512..131072"}
     batch = make_batch(lengths, cfg.vocab_size, args.seed, pin=True)
     plan_desc = f"cp{world}"
+    predicted_ms = None
     if args.plan == "online":
         from prism_cp_b200.planner.calibrate import calibrated
         from prism_cp_b200.planner.cli import B200_ENVELOPE
@@ -164,6 +174,7 @@ def main():
         from prism_cp_b200.planner.online import select
         pm = calibrated(model_from_config(cfg, B200_ENVELOPE["device_bytes"],
                                           **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"}))
+        pm = replace(pm, recompute_tokens=args.recompute_tokens or None)
         try:
             sel = select(batch.lengths, world, cfg.pattern, pm)
         except ValueError as err:
@@ -171,12 +182,14 @@ def main():
                              f"the calibrated memory model ({err}); use more GPUs or shorter documents")
         plan = sel.plan
         plan_desc = f"online cp_gdn{sel.cp_gdn} cp_gqa{sel.cp_gqa} over {world}"
+        predicted_ms = sel.predicted_update_ms
     else:
         plan = uniform_plan(batch.lengths, world, world, args.tokens_per_rank, cfg.pattern)
 
     model = HybridModel(cfg, dtype=torch.bfloat16, device=device, seed=0)
     teams = Teams(world)
-    trainer = Trainer(model, teams, device, overlap_grad_reduce=args.overlap_grad_reduce)
+    trainer = Trainer(model, teams, device, overlap_grad_reduce=args.overlap_grad_reduce,
+                      recompute_tokens=args.recompute_tokens or None)
     host_inputs = trainer.prepare(batch, plan, pin=True)
     dev_inputs = [h.to(device) for h in host_inputs]
     torch.cuda.synchronize()
@@ -243,6 +256,7 @@ def main():
                                  f"{cfg.pattern.count('*')} GQA, h{cfg.hidden_size}, "
                                  f"{cfg.parameter_count() / 1e9:.2f}B params)",
                            parallelism=plan_desc, workload=args.workload, microbatches=len(plan.microbatches),
+                           planner_predicted_ms_per_step=predicted_ms, recompute_tokens=args.recompute_tokens,
                            l2="per-step working set (32K-token activations) far exceeds the 126 MB L2",
                            **workload),
             "clocks": clocks.summary(), "e2e": e2e, "gpu_launches": launches * args.steps,

@@ -69,18 +69,25 @@ __global__ void gather_rows_kernel(const int64_t* peer_bases, const RouteEntry* 
   // a bounded wait before this launch gave up (peer missing or late): copy nothing rather than rows a
   // peer may not have finished writing; the host sees the status at its next check
   if (*reinterpret_cast<volatile int*>(status) != 0) return;
-  const int b = blockIdx.x;
-  const RouteEntry e = routes[block_route[b]];
-  const int64_t r0 = block_row0[b];
+  const RouteEntry e = routes[block_route[blockIdx.x]];
+  const int64_t r0 = block_row0[blockIdx.x];
   const int64_t r1 = min(e.rows, r0 + rows_per_block);
-  const uint8_t* src = reinterpret_cast<const uint8_t*>(peer_bases[e.src_rank]) + e.src_off;
-  const int64_t vec_per_row = row_bytes / 16;
-  const int64_t total = (r1 - r0) * vec_per_row;
-  for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
-    const int64_t row = r0 + i / vec_per_row, v = i % vec_per_row;
-    const uint4 val = *reinterpret_cast<const uint4*>(src + row * row_bytes + v * 16);
-    *reinterpret_cast<uint4*>(dst + e.dst_off + row * row_bytes + v * 16) = val;
+  // the block's rows are contiguous on both sides: copy them as one run of 16-byte vectors, four
+  // independent loads in flight per thread (NVLink reads have a long latency)
+  const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(peer_bases[e.src_rank]) +
+                                                    e.src_off + r0 * row_bytes);
+  uint4* out = reinterpret_cast<uint4*>(dst + e.dst_off + r0 * row_bytes);
+  const int64_t n = (r1 - r0) * row_bytes / 16;
+  const int64_t stride = (int64_t)blockDim.x * 4;
+  int64_t i = threadIdx.x;
+  for (; i + 3 * blockDim.x < n; i += stride) {
+    uint4 v0 = src[i], v1 = src[i + blockDim.x], v2 = src[i + 2 * blockDim.x], v3 = src[i + 3 * blockDim.x];
+    out[i] = v0;
+    out[i + blockDim.x] = v1;
+    out[i + 2 * blockDim.x] = v2;
+    out[i + 3 * blockDim.x] = v3;
   }
+  for (; i < n; i += blockDim.x) out[i] = src[i];
 }
 
 }  // namespace symm

@@ -2,8 +2,9 @@
 
 Every rank of the team stages the tensors the attention kernels need in a
 symmetric heap (``symm.SymmetricHeap``); after a bounded ready signal each rank
-pulls the team's slabs into local memory with one P2P gather kernel (16-byte
-loads over NVLink, every byte crosses NVLink once), and the tcgen05 attention
+pulls the peers' slabs into local memory with one P2P gather kernel (16-byte
+loads over NVLink, every byte crosses NVLink once; its own slab is read in
+place), and the tcgen05 attention
 kernels then run over the whole sequence in global positions
 (``csrc/attention_peer.cuh``), reading the slab of the rank that owns each tile:
 
@@ -80,33 +81,39 @@ class TeamHeap:
         dev = self.heap.device.index
         return [lib().symm_tensor(base + offset, list(shape), code, dev) for base in self.heap.bases]
 
-    def gather(self, offset: int, shape, dtype, rows_per_block: int = 64) -> list[torch.Tensor]:
-        """Copy every team rank's region [offset, offset + size) into one local buffer
-        (one P2P gather launch); returns the per-rank slabs in team order."""
+    def gather(self, offset: int, shape, dtype, local: torch.Tensor | None = None,
+               rows_per_block: int = 64) -> list[torch.Tensor]:
+        """Every team rank's region [offset, offset + size) as a list of slabs in team order:
+        the peers' regions copied into one local buffer by a single P2P gather launch, and this
+        rank's own slab taken as ``local`` (no copy) when given."""
         n = len(self.ranks)
         rows = shape[0]
-        row_bytes = 1
+        row_bytes = torch.tensor([], dtype=dtype).element_size()
         for x in shape[1:]:
             row_bytes *= x
-        row_bytes *= torch.tensor([], dtype=dtype).element_size()
-        out = torch.empty((n,) + tuple(shape), dtype=dtype, device=self.heap.device)
-        key = (offset, tuple(shape), dtype, rows_per_block)
+        sources = [r for r in range(n) if local is None or r != self.index]
+        out = torch.empty((len(sources),) + tuple(shape), dtype=dtype, device=self.heap.device)
+        key = (offset, tuple(shape), dtype, rows_per_block, local is None)
         plan = self._gather_plans.get(key)
         if plan is None:
             routes, block_route, block_row0 = [], [], []
-            for r in range(n):
-                routes.append((r, offset, r * rows * row_bytes, rows))
+            for slot, r in enumerate(sources):
+                routes.append((r, offset, slot * rows * row_bytes, rows))
                 for r0 in range(0, rows, rows_per_block):
-                    block_route.append(r)
+                    block_route.append(slot)
                     block_row0.append(r0)
             dev = self.heap.device
             plan = (torch.tensor(routes, dtype=torch.int64, device=dev),
                     torch.tensor(block_route, dtype=torch.int64, device=dev),
                     torch.tensor(block_row0, dtype=torch.int64, device=dev))
             self._gather_plans[key] = plan
-        lib().symm_gather_rows(self.heap.bases_dev, plan[0], plan[1], plan[2], rows_per_block, row_bytes, out,
-                               status(self.heap.device))
-        return list(out.unbind(0))
+        if sources:
+            lib().symm_gather_rows(self.heap.bases_dev, plan[0], plan[1], plan[2], rows_per_block, row_bytes, out,
+                                   status(self.heap.device))
+        slabs = list(out.unbind(0))
+        if local is not None:
+            slabs.insert(self.index, local)
+        return slabs
 
 
 def team_heap(ctx, need: int) -> TeamHeap:
@@ -157,8 +164,8 @@ class PeerAttention:
         heap.local(base, (T, Hkv, D), torch.bfloat16).copy_(k)
         heap.local(base + kv_bytes, (T, Hkv, D), torch.bfloat16).copy_(v)
         heap.ready()
-        k_all = heap.gather(base, (T, Hkv, D), torch.bfloat16)
-        v_all = heap.gather(base + kv_bytes, (T, Hkv, D), torch.bfloat16)
+        k_all = heap.gather(base, (T, Hkv, D), torch.bfloat16, local=k)
+        v_all = heap.gather(base + kv_bytes, (T, Hkv, D), torch.bfloat16, local=v)
         heap.done()
         out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=q.device)
         lse = torch.empty((Hq, T), dtype=torch.float32, device=q.device)
@@ -190,7 +197,8 @@ class PeerAttention:
         views["lse"].copy_(lse)
         lib().attention_bwd_dsum(out, views["do"], views["dsum"])
         heap.ready()
-        slabs = {name: heap.gather(base + offs[name], shape, dt) for name, shape, dt in sizes}
+        # this rank's own slabs are read in place from the heap (local memory); only peers' cross NVLink
+        slabs = {name: heap.gather(base + offs[name], shape, dt, local=views[name]) for name, shape, dt in sizes}
         heap.done()
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
         lib().attention_bwd_peer(slabs["q"], slabs["k"], slabs["v"], slabs["do"], slabs["lse"], slabs["dsum"],

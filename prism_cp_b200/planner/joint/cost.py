@@ -71,6 +71,9 @@ class Model:
     # measured step-time factor of CP > 1 operators over the analytic CP terms, keyed by CP degree
     # ("2": 1.07); degrees without an entry use the largest measured degree's factor
     cp_overhead: dict | None = None
+    # microbatches with more tokens than this on some rank (in any of their layouts) keep only
+    # every layer's input and recompute the layer's forward in the backward; None: never
+    recompute_tokens: int | None = None
 
     def __post_init__(self):
         numbers = {f.name: getattr(self, f.name) for f in fields(self)}
@@ -284,7 +287,44 @@ class Evaluator:
         head_ms = max(tokens) * 6 * m.hidden * m.vocab / (m.compute_tflops * 1e9)
         return back_ms + head_ms + m.microbatch_ms, peak
 
+    def recomputes(self, batch) -> bool:
+        """Whether ``batch`` runs with per-layer recompute (``Model.recompute_tokens``)."""
+        limit = self.model.recompute_tokens
+        if limit is None:
+            return False
+        layouts = [batch.ingress] + [x for pair in batch.layers for x in pair]
+        return max(max(self.tokens(x)) for x in layouts) > limit
+
+    def _evaluate_recompute(self, batch) -> dict:
+        """Per-layer recompute: between forward and backward every layer keeps only its input
+        (bf16 rows of its attention layout); in the backward one layer at a time is rebuilt, so
+        the peak is the checkpoints plus the largest single layer's own walk on top of them, and
+        each layer pays its forward (a third of its F+B time) once more."""
+        m = self.model
+        start, previous = self.initial(batch.ingress), batch.ingress
+        checkpoints = [0] * self.world
+        for attention, _ in batch.layers:
+            checkpoints = [c + self._scaled(n * 2 * m.hidden) for c, n in zip(checkpoints, self.tokens(attention))]
+        held = _plus(start, checkpoints)
+        peak, total, points = held, 0.0, []
+        for index, symbol in enumerate(self.pattern):
+            attention, mlp = batch.layers[index]
+            ms, _, here = self.layer(held, previous, attention, mlp, symbol)
+            rebuild = (self.operator(symbol, attention)[0] + self.operator("M", mlp)[0]) / 3
+            total += ms + rebuild
+            peak = tuple(map(max, peak, here))
+            points.append({"layer": index, "saved_live_bytes": list(held), "peak_bytes": list(here),
+                           "attention_tokens": self.tokens(attention), "mlp_tokens": self.tokens(mlp)})
+            previous = attention
+        ms, here = self.finish(held, previous, batch.ingress)
+        peak = tuple(map(max, peak, here))
+        return {"predicted_ms": total + ms, "peak_bytes": peak, "fits": max(peak) <= m.budget, "points": points,
+                "head_peak_bytes": here, "includes_margin": True, "recompute": True,
+                "memory_status": "structural_forward_backward_envelope_not_measured"}
+
     def evaluate(self, batch) -> dict:
+        if self.recomputes(batch):
+            return self._evaluate_recompute(batch)
         live, previous = self.initial(batch.ingress), batch.ingress
         peak, total, points = live, 0.0, []
         for index, symbol in enumerate(self.pattern):

@@ -12,7 +12,9 @@ response profile). Candidates:
   teams, GQA layers ``world / cp_gqa`` zigzag teams over the same samples, so
   every GDN<->GQA boundary with different degrees is a CP-transition reshard;
 * documents longer than a team can hold at a degree raise that degree for the
-  batch (the degree is the minimum that fits the longest document).
+  batch (the degree is the minimum that fits the longest document); with
+  ``Model.recompute_tokens`` set, such a document may instead run alone in a
+  microbatch that recomputes every layer in the backward, priced as such.
 
 The selection is deterministic (same lengths -> same plan on every rank), costs
 milliseconds of CPU per batch, and returns the plan with its predicted update
@@ -76,8 +78,11 @@ def _split(samples, lengths, parts: int):
     return [tuple(sorted(b)) for b in bins]
 
 
-def candidate_plan(lengths: dict, world: int, pattern: str, cp_gdn: int, cp_gqa: int, capacity: int):
-    """Plan with GDN teams of ``cp_gdn`` and GQA teams of ``cp_gqa`` ranks, or None."""
+def candidate_plan(lengths: dict, world: int, pattern: str, cp_gdn: int, cp_gqa: int, capacity: int,
+                   oversize: bool = False):
+    """Plan with GDN teams of ``cp_gdn`` and GQA teams of ``cp_gqa`` ranks, or None. With
+    ``oversize`` a document longer than a team's capacity still gets a microbatch of its own
+    (the evaluator then prices it with per-layer recompute, if the model allows that)."""
     coarse = max(cp_gdn, cp_gqa)
     fine = min(cp_gdn, cp_gqa)
     for n in lengths.values():
@@ -86,7 +91,7 @@ def candidate_plan(lengths: dict, world: int, pattern: str, cp_gdn: int, cp_gqa:
         if fine > 1 and n % (2 * fine):
             return None
     order = sorted(lengths, key=lambda s: (-lengths[s], s))
-    if max(lengths.values()) > capacity * coarse:
+    if max(lengths.values()) > capacity * coarse and not oversize:
         return None
     mbs = []
     for coarse_bins in _pack(lengths, order, capacity * coarse, world // coarse):
@@ -96,7 +101,9 @@ def candidate_plan(lengths: dict, world: int, pattern: str, cp_gdn: int, cp_gqa:
         ratio = coarse // fine
         for b in coarse_bins:
             parts = _split(b, lengths, ratio) if ratio > 1 else [b]
-            if parts is None or any(sum(lengths[s] for s in p) > capacity * fine for p in parts):
+            if parts is None:
+                return None
+            if not oversize and any(sum(lengths[s] for s in p) > capacity * fine for p in parts):
                 return None
             fine_bins.extend(parts)
         def lay(cp, bins, mode):
@@ -121,6 +128,10 @@ def select(lengths: dict, world: int, pattern: str, model: Model, degrees=(1, 2,
         # the memory model's token ceiling is necessary, not sufficient (CP workspaces come on top):
         # shrink the per-rank capacity until some candidate fits
         top = max(1, model.token_capacity_upper_bound(pattern, world) // world)
+        if model.recompute_tokens is not None:
+            # pack ordinary microbatches below the recompute threshold; only documents longer than
+            # a team's share run alone with recompute
+            top = min(top, model.recompute_tokens)
         last = None
         for frac in (1.0, 0.9, 0.8, 0.7, 0.6, 0.5, 0.4, 0.3):
             try:
@@ -134,7 +145,8 @@ def select(lengths: dict, world: int, pattern: str, model: Model, degrees=(1, 2,
     for cg in degrees:
         for ca in degrees:
             try:
-                plan = candidate_plan(lengths, world, pattern, cg, ca, capacity)
+                plan = candidate_plan(lengths, world, pattern, cg, ca, capacity,
+                                      oversize=model.recompute_tokens is not None)
             except ValueError:
                 plan = None
             if plan is None:
@@ -145,7 +157,8 @@ def select(lengths: dict, world: int, pattern: str, model: Model, degrees=(1, 2,
                 continue
             ms = sum(e["predicted_ms"] for e in evid) + model.update_ms
             rows.append({"cp_gdn": cg, "cp_gqa": ca, "fits": True, "predicted_update_ms": ms,
-                         "microbatches": len(plan.microbatches)})
+                         "microbatches": len(plan.microbatches),
+                         "recomputed_microbatches": sum(bool(e.get("recompute")) for e in evid)})
             key = (ms, cg, ca)
             if best is None or key < best[0]:
                 best = (key, plan, cg, ca, ms)

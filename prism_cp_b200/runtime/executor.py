@@ -12,6 +12,7 @@ monkeypatching). Local layouts are cached per (layout, lengths).
 from __future__ import annotations
 
 import torch
+import torch.utils.checkpoint
 
 from ..parallel.layout import LocalLayout
 from ..parallel.transport import move
@@ -37,13 +38,20 @@ class LayoutCache:
 
 
 class MicrobatchRun:
+    """One microbatch of a plan on this rank. With ``recompute_tokens`` set, a microbatch that
+    holds more tokens than that on some rank (in any of its layouts) keeps only each layer's input
+    and recomputes the layer's forward in the backward (the cost model prices the same rule,
+    ``joint.cost.Model.recompute_tokens``)."""
+
     def __init__(self, mb: Microbatch, lengths: dict, cache: LayoutCache, first_layer: int = 0,
-                 num_layers: int | None = None):
+                 num_layers: int | None = None, recompute_tokens: int | None = None):
         self.lengths = {s: lengths[s] for g in mb.ingress.groups for s in g.samples}
         self.ingress = cache.get(mb.ingress, self.lengths)
         layers = mb.layers[first_layer:first_layer + num_layers] if num_layers else mb.layers[first_layer:]
         self.contexts = [cache.get(a, self.lengths) for a, _ in layers]
         self.mlp_contexts = [None if m == a else cache.get(m, self.lengths) for a, m in layers]
+        self.recompute = recompute_tokens is not None and recomputes(mb, self.lengths, cache.world,
+                                                                     recompute_tokens)
 
     def forward_layers(self, model, x, start_ctx=None):
         prev = start_ctx or self.ingress
@@ -54,7 +62,10 @@ class MicrobatchRun:
             if watchdog._ACTIVE is not None and x.requires_grad:
                 x.register_hook(lambda g, i=i: watchdog.beat(f"layer {i} backward done"))
             with nvtx(f"layer {i} {type(layer).__name__} cp{getattr(ctx, 'cp', '?')}"):
-                x = layer(x, ctx, mctx)
+                if self.recompute and x.requires_grad:
+                    x = torch.utils.checkpoint.checkpoint(layer, x, ctx, mctx, use_reentrant=False)
+                else:
+                    x = layer(x, ctx, mctx)
             watchdog.beat(f"layer {i} forward done")
             prev = ctx
         return x, prev
@@ -64,3 +75,9 @@ class MicrobatchRun:
         x, prev = self.forward_layers(model, x)
         x = move(x, prev, self.ingress)
         return model.loss(x, labels, weights)
+
+
+def recomputes(mb: Microbatch, lengths: dict, world: int, limit: int) -> bool:
+    """Whether some rank holds more than ``limit`` tokens of ``mb`` in one of its layouts."""
+    layouts = [mb.ingress] + [x for pair in mb.layers for x in pair]
+    return max(max(x.tokens(lengths, world)) for x in layouts) > limit

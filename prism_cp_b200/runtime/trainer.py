@@ -56,7 +56,7 @@ class Trainer:
     def __init__(self, model, teams, device, lr=3e-4, min_lr=3e-5, weight_decay=0.1, clip_grad=1.0,
                  warmup_steps=0, decay_steps=1000, group=None, hbm_guard=True, records: str | None = None,
                  numerics=None, audit: bool = False, overlap_grad_reduce: bool = False,
-                 bucket_bytes: int = 256 << 20, logical=None):
+                 bucket_bytes: int = 256 << 20, logical=None, recompute_tokens: int | None = None):
         self.model, self.teams, self.device = model, teams, device
         self.world = teams.world
         self.rank = teams.rank
@@ -87,6 +87,8 @@ class Trainer:
         self.audit = AccumulationAudit() if audit else None
         self.step_index = 0
         self.watchdog = watchdog.from_env()
+        # microbatches above this many tokens on a rank recompute their layers in the backward
+        self.recompute_tokens = recompute_tokens
 
     # ------------------------------------------------------------------ inputs
     def prepare(self, batch: GlobalBatch, plan: Plan, pin: bool = True) -> list[HostInputs]:
@@ -99,7 +101,7 @@ class Trainer:
         last = len(plan.microbatches) - 1
         for index, (mb, host) in enumerate(zip(plan.microbatches, inputs)):
             dev = host.to(self.device) if host.tokens.device != self.device else host
-            run = MicrobatchRun(mb, batch_lengths, self.cache)
+            run = MicrobatchRun(mb, batch_lengths, self.cache, recompute_tokens=self.recompute_tokens)
             watchdog.beat(f"step {self.step_index + 1} microbatch {index} forward")
             logical = self.logical is not None and self.logical.active(self.step_index + 1)
             with nvtx(f"microbatch {index} forward"):

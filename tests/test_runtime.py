@@ -194,3 +194,43 @@ def test_launcher_writes_its_run_configuration(tmp_path):
     cfg = json.loads((rec / "launch_config.json").read_text())
     assert cfg["argv"] == argv and cfg["args"]["train_iters"] == 1 and cfg["model"]["pattern"] == "GGG*"
     assert (rec / "steps_rank0.jsonl").exists()
+
+
+def test_recomputed_microbatches_match_stored_activations():
+    """A microbatch above the recompute threshold keeps only layer inputs and rebuilds each
+    layer in the backward: loss and every gradient equal the stored-activation run."""
+    from prism_cp_b200.runtime.executor import recomputes
+    grads = {}
+    for limit in (None, 128):
+        cfg = hybrid_tiny()
+        model = HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0)
+        batch = make_batch([256, 128, 128], cfg.vocab_size, seed=1)
+        plan = uniform_plan(batch.lengths, 1, 1, 256, cfg.pattern)
+        tr = Trainer(model, Teams(1), torch.device("cpu"), recompute_tokens=limit)
+        if limit is not None:
+            assert all(recomputes(mb, batch.lengths, 1, limit) for mb in plan.microbatches)
+        tr.flat.zero_grad()
+        loss = tr.forward_backward(batch.lengths, plan, tr.prepare(batch, plan, pin=False))
+        tr.flat.fold_param_grads()
+        grads[limit] = (float(loss), tr.flat.grad.clone())
+    assert grads[None][0] == pytest.approx(grads[128][0], rel=1e-6)
+    assert torch.allclose(grads[None][1], grads[128][1], rtol=1e-5, atol=1e-7)
+
+
+def test_planner_prices_recompute_for_oversize_documents():
+    from dataclasses import replace
+    from prism_cp_b200.models.config import PRESETS
+    from prism_cp_b200.planner.joint.cost import Evaluator, Model
+    from prism_cp_b200.planner.online import select
+    cfg = PRESETS["hybrid-1.3b"]()
+    base = Model(hidden=cfg.hidden_size, ffn=cfg.ffn_hidden_size, vocab=cfg.vocab_size, q_heads=16, kv_heads=4,
+                 head_dim=128, gdn_heads=16, gdn_dim=128, device_bytes=180 * 10 ** 9, compute_tflops=1400.0)
+    lengths = {0: 131072, **{i: 4096 for i in range(1, 17)}}
+    with pytest.raises(ValueError):
+        select(lengths, 1, cfg.pattern, base, degrees=(1,))
+    sel = select(lengths, 1, cfg.pattern, replace(base, recompute_tokens=32768), degrees=(1,))
+    ev = Evaluator(replace(base, recompute_tokens=32768), lengths, 1, cfg.pattern)
+    rows = [ev.evaluate(mb) for mb in sel.plan.microbatches]
+    assert [bool(r.get("recompute")) for r in rows].count(True) == 1 and all(r["fits"] for r in rows)
+    long_mb = next(mb for mb, r in zip(sel.plan.microbatches, rows) if r.get("recompute"))
+    assert 0 in long_mb.ingress.groups[0].samples
