@@ -52,6 +52,7 @@ void gdn_chunk_bwd_state(const at::Tensor& Wn, const at::Tensor& Kd, const at::T
                          const at::Tensor& seq_chunks, const c10::optional<at::Tensor>& dS_final,
                          const c10::optional<at::Tensor>& dS0, at::Tensor& states, at::Tensor& rows,
                          at::Tensor& status);
+bool gdn_local_tc_enabled(int64_t set);
 std::vector<at::Tensor> gdn_chunk_bwd_local(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                             const at::Tensor& g, const at::Tensor& beta, const at::Tensor& tok0,
                                             const at::Tensor& len, const at::Tensor& Gc, const at::Tensor& aux,
@@ -105,6 +106,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_chunk_prep", &prism::gdn_chunk_prep, py::call_guard<py::gil_scoped_release>(), "GDN chunk prep: WY form, decays, Aqk (CUDA cores)");
   m.def("gdn_chunk_fwd", &prism::gdn_chunk_fwd, py::call_guard<py::gil_scoped_release>(), "GDN tcgen05 state pass with the output fused");
   m.def("gdn_chunk_bwd_state", &prism::gdn_chunk_bwd_state, py::call_guard<py::gil_scoped_release>(), "GDN tcgen05 reverse state pass");
+  m.def("gdn_local_tc_enabled", &prism::gdn_local_tc_enabled, "select (1) or query (-1) the tcgen05 GDN local backward");
   m.def("gdn_chunk_bwd_local", &prism::gdn_chunk_bwd_local, py::call_guard<py::gil_scoped_release>(), "GDN chunk-local backward (tcgen05 + CUDA cores)");
   m.def("attention_fwd_peer", &prism::attention_fwd_peer, py::call_guard<py::gil_scoped_release>(),
         "context-parallel attention forward reading every KV tile from its owner's symmetric buffer");

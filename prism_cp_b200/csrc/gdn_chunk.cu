@@ -26,11 +26,16 @@
 //                            G^T     <- gamma G^T + dO^T Qg + dDelta^T Wn
 //   gdn_bwd_dv_kernel      tcgen05, one CTA per (chunk, head): every product that
 //                          contracts over dv (dWn, dKd, dQg, dAqk, dDelta V^T, dgamma).
-//   gdn_bwd_local_kernel   CUDA cores, one CTA per (chunk, head): the WY backward,
-//                          decay gradients and dq, dk, dv, dg, dbeta.
+//   gdn_bwd_local_tc_kernel tcgen05, one CTA per (chunk, head): the WY backward, decay
+//                          gradients and dq, dk, dv, dg, dbeta, every product on the
+//                          tensor cores (gdn_bwd_local_kernel: the same on CUDA cores,
+//                          kept as the reference form behind PRISM_GDN_LOCAL_TC=0).
 // Sequences are padded to whole chunks (padded rows have q = k = v = 0, g = beta = 0,
 // which leave the state unchanged). Every mbarrier wait is bounded; a kernel that
 // gives up records an error code in the status word and returns.
+#include <cstdlib>
+#include <cstring>
+
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -1313,6 +1318,438 @@ __global__ void __launch_bounds__(LB_THREADS, 1) gdn_bwd_local_kernel(LocalArgs 
   }
 }
 
+// ============================================================================ chunk-local backward (tcgen05)
+// Same WY / decay backward as gdn_bwd_local_kernel, with every product on the tensor cores.
+// One CTA (4 warps) per (chunk, head); warps 0-1 own the chunk's 64 rows (TMEM lanes 0..63,
+// one row per thread) for every epilogue, all warps stage operands. With T = (I + L)^-1 and
+// dW = -dWn, the products are (each M = 128 with rows 64..127 of the A operand reading the
+// next tile into TMEM lanes that are never read):
+//   D1 = T^T dW                 [i, a]   -> dBk; dk starts as beta e^G D1 (stored back)
+//   D2 = dW k^T                 [i, j]   -> X2 = beta_j (e^G_j D2 + dDelta V^T)
+//   D3 = T^T X2                 [i, m]   -> Z
+//   D4 = Z T^T                  [i, j]   -> dL = -D4 (strictly lower), X1, X3 = s dAqk o E
+//   D5 = dk + (X1 + X1^T) k + X3^T q     -> dk (plus e^(G_L - G) dKd)
+//   D6 = X3 k                   [i, a]   -> dq (plus s e^G dQg)
+//   D7 = T^T dDelta             [i, col] -> dv = beta D7
+// Operands are bf16 in 128-byte-swizzled shared memory; accumulation is fp32 in TMEM.
+namespace lt {
+constexpr int THREADS = 128;
+constexpr int TMEM_COLS = 512;  // D1/D5 [0,128) D2 [128,192) D3 [192,256) D4 [256,320) D6 [384,512) D7 [128,128+DV)
+constexpr int OFF_K = 0, OFF_Q = 2 * BLK, OFF_T = 4 * BLK, OFF_W = 5 * BLK, OFF_X2 = 7 * BLK, OFF_Z = 8 * BLK;
+constexpr int OFF_XS = 9 * BLK, OFF_X3 = 10 * BLK, OFF_DD = 11 * BLK, OFF_F = 15 * BLK;
+constexpr int FT = C * C;  // one fp32 64 x 64 tile (rows skewed: element (r, j) at r * 64 + ((j + r) & 63))
+constexpr int SMEM = OFF_F + 5 * FT * 4 + 4 * C * 4 + 64 + 1024;
+
+// fp32 tile element (r, j) with the row skew that keeps row-per-thread and column-per-thread
+// accesses free of bank conflicts
+PRISM_DEVICE int sk(int r, int j) { return r * 64 + ((j + r) & 63); }
+
+// Writes 8 consecutive bf16 (columns 8cc..8cc+7) of row r into a swizzled tile of 64-column blocks.
+PRISM_DEVICE void put8(uint8_t* tile, int r, int cc, uint4 v) {
+  *reinterpret_cast<uint4*>(tile + (cc >> 3) * BLK + swz(r, cc & 7)) = v;
+}
+
+PRISM_DEVICE void get_row_f(const uint8_t* tile, int r, int cc, float* f) {
+  unpack8(*reinterpret_cast<const uint4*>(tile + (cc >> 3) * BLK + swz(r, cc & 7)), f);
+}
+
+PRISM_DEVICE uint64_t kmaj(uint32_t base, int k) { return make_smem_desc_sw128(base + (k >> 2) * BLK + (k & 3) * 32, 16, 1024); }
+PRISM_DEVICE uint64_t mnmaj(uint32_t base, int k) { return make_smem_desc_sw128(base + k * 2048, BLK, 1024); }
+
+PRISM_DEVICE void ld32(uint32_t taddr, float* f) {
+  uint32_t r[32];
+  tmem_ld_32x32b_x32(taddr, r);
+  tmem_wait_ld();
+#pragma unroll
+  for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(r[e]);
+}
+}  // namespace lt
+
+struct LocalTcArgs {
+  LocalArgs a;
+  int* status;
+};
+
+__global__ void __launch_bounds__(lt::THREADS, 1)
+    gdn_bwd_local_tc_kernel(const __grid_constant__ CUtensorMap mQ, const __grid_constant__ CUtensorMap mK,
+                            const __grid_constant__ CUtensorMap mDD, LocalTcArgs args) {
+  using namespace lt;
+  const LocalArgs& a = args.a;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t *sK = smem + OFF_K, *sQ = smem + OFF_Q, *sT = smem + OFF_T, *sW = smem + OFF_W;
+  uint8_t *sX2 = smem + OFF_X2, *sZ = smem + OFF_Z, *sXS = smem + OFF_XS, *sX3 = smem + OFF_X3;
+  uint8_t* sDD = smem + OFF_DD;
+  float* X1s = reinterpret_cast<float*>(smem + OFF_F);
+  float* Mc = X1s + FT;   // -(dG contributions) per (row, column): summed over rows by warps 2-3
+  float* KKs = Mc + FT;
+  float* QKs = KKs + FT;
+  float* dAs = QKs + FT;
+  float* Gs = dAs + FT;
+  float* Bs = Gs + C;
+  float* dGc = Bs + C;
+  float* misc = dGc + C;  // [0]: dG of the last row from the dKd terms
+  uint64_t* bars = reinterpret_cast<uint64_t*>(misc + C);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
+  const int H = a.H, DV = a.DV, nvb = DV / 64;
+  const long ch = blockIdx.x;
+  const int c = (int)(ch / H), h = (int)(ch % H);
+  const int t0 = a.tok0[c], n = a.len[c];
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const bool owner = warp < 2;  // threads 0..63: one chunk row each (TMEM lanes 0..63)
+  const int i = tid;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int b = 0; b < 6; ++b) mbar_init(&bars[b], 1);
+    misc[0] = 0.f;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bars[0], (4 + nvb) * BLK);
+    tma_load_2d(sK, &mK, &bars[0], h * DK, t0);
+    tma_load_2d(sK + BLK, &mK, &bars[0], h * DK + 64, t0);
+    tma_load_2d(sQ, &mQ, &bars[0], h * DK, t0);
+    tma_load_2d(sQ + BLK, &mQ, &bars[0], h * DK + 64, t0);
+    for (int b = 0; b < nvb; ++b) tma_load_2d(sDD + b * BLK, &mDD, &bars[0], 0, (int)(ch * DV) + b * 64);
+  }
+  if (warp == 0) {
+    const int l = tid;
+    float x0 = l < n ? a.g[(long)(t0 + l) * H + h] : 0.f;
+    float x1 = l + 32 < n ? a.g[(long)(t0 + l + 32) * H + h] : 0.f;
+    Bs[l] = l < n ? a.beta[(long)(t0 + l) * H + h] : 0.f;
+    Bs[l + 32] = l + 32 < n ? a.beta[(long)(t0 + l + 32) * H + h] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
+      const float y1 = __shfl_up_sync(0xffffffffu, x1, o);
+      if (l >= o) {
+        x0 += y0;
+        x1 += y1;
+      }
+    }
+    x1 += __shfl_sync(0xffffffffu, x0, 31);
+    Gs[l] = x0;
+    Gs[l + 32] = x1;
+  }
+  // operands staged by all threads: T (rows l, cols i), dW = -dWn (rows i, cols a), and the fp32
+  // k.k, s q.k and dAqk tiles the dL epilogue reads row-wise
+  const float* aux = a.aux + ch * 3 * C * C;
+  for (int e = tid; e < C * 8; e += THREADS) {
+    const int l = e >> 3, cc = e & 7;
+    const float4 x = reinterpret_cast<const float4*>(aux + 2 * C * C + l * C)[2 * cc];
+    const float4 y = reinterpret_cast<const float4*>(aux + 2 * C * C + l * C)[2 * cc + 1];
+    const float f[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+    put8(sT, l, cc, pack8(f));
+  }
+  for (int e = tid; e < C * 16; e += THREADS) {
+    const int r = e & 63, a8 = (e >> 6) * 8;
+    float f[8];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) f[m] = -a.dWnT[(ch * DK + a8 + m) * C + r];
+    put8(sW, r, a8 >> 3, pack8(f));
+  }
+  for (int e = tid; e < C * C; e += THREADS) {
+    const int r = e >> 6, j = e & 63;
+    KKs[sk(r, j)] = aux[e];
+    QKs[sk(r, j)] = aux[C * C + e];
+    dAs[sk(r, j)] = a.dAqk[ch * C * C + e];
+  }
+  bool ok = __syncthreads_and(mbar_wait_bounded(&bars[0], 0, nullptr, args.status, kTimeoutProducer));
+  if (ok && n < C) {
+    // rows past the end of the sequence hold the next sequence's tokens: zero them
+    const int per = (C - n) * 8;
+    for (int e = tid; e < 4 * per; e += THREADS) {
+      const int b = e / per, rem = e % per;
+      *reinterpret_cast<uint4*>(smem + b * BLK + swz(n + rem / 8, rem % 8)) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  fence_proxy_async();
+  ok = __syncthreads_and(ok);
+
+  const uint32_t aK = smem_u32(sK), aQ = smem_u32(sQ), aT = smem_u32(sT), aW = smem_u32(sW);
+  const uint32_t aX2 = smem_u32(sX2), aZ = smem_u32(sZ), aXS = smem_u32(sXS), aX3 = smem_u32(sX3);
+  const uint32_t aDD = smem_u32(sDD);
+  const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+  const float Gi = Gs[i & 63], Bi = Bs[i & 63], egi = __expf(Gi), GL = Gs[C - 1];
+  float dB_own = 0.f, dG_own = 0.f;
+
+  // ---- D1 = T^T dW, D2 = dW k^T
+  if (ok && tid == 0) {
+    tc_fence_after();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) umma_bf16_ss(tmem, mnmaj(aT, k), mnmaj(aW, k), make_idesc_bf16(128, 128, 1, 1), k > 0);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      umma_bf16_ss(tmem + 128, kmaj(aW, k), kmaj(aK, k), make_idesc_bf16(128, 64, 0, 0), k > 0);
+    umma_commit(&bars[1]);
+  }
+  if (owner) {
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_bounded(&bars[1], 0, nullptr, args.status, kTimeoutEpilogue));
+    if (ok) {
+      tc_fence_after();
+      float part = 0.f;
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float f[32], kf[32];
+        ld32(tl + q4 * 32, f);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) get_row_f(sK, i, q4 * 4 + m, kf + 8 * m);
+        uint32_t r[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          part = fmaf(f[e], kf[e], part);
+          r[e] = __float_as_uint(Bi * egi * f[e]);
+        }
+        tmem_st_32x32b_x32(tl + q4 * 32, r);  // dk accumulates on top of beta e^G T^T dW
+      }
+      tmem_wait_st();
+      dB_own += egi * part;
+      dG_own += Bi * egi * part;
+#pragma unroll 1
+      for (int h2 = 0; h2 < 2; ++h2) {
+        float f[32], x[32];
+        ld32(tl + 128 + h2 * 32, f);
+        const float4* dd = reinterpret_cast<const float4*>(a.dDV + (ch * C + i) * C + h2 * 32);
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const float4 v4 = dd[m];
+          const float dv4[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int j = h2 * 32 + 4 * m + u;
+            x[4 * m + u] = Bs[j] * (__expf(Gs[j]) * f[4 * m + u] + dv4[u]);
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < 4; ++m) put8(sX2, i, h2 * 4 + m, pack8(x + 8 * m));
+      }
+    }
+  }
+  fence_proxy_async();
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+
+  // ---- D3 = T^T X2 -> Z
+  if (ok && tid == 0) {
+    tc_fence_after();
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      umma_bf16_ss(tmem + 192, mnmaj(aT, k), mnmaj(aX2, k), make_idesc_bf16(128, 64, 1, 1), k > 0);
+    umma_commit(&bars[2]);
+  }
+  if (owner) {
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_bounded(&bars[2], 0, nullptr, args.status, kTimeoutEpilogue));
+    if (ok) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int h2 = 0; h2 < 2; ++h2) {
+        float f[32];
+        ld32(tl + 192 + h2 * 32, f);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) put8(sZ, i, h2 * 4 + m, pack8(f + 8 * m));
+      }
+    }
+  }
+  fence_proxy_async();
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+
+  // ---- D4 = Z T^T -> dL (strictly lower), X1 = dL beta_i E, X3 = s dAqk o E
+  if (ok && tid == 0) {
+    tc_fence_after();
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      umma_bf16_ss(tmem + 256, kmaj(aZ, k), kmaj(aT, k), make_idesc_bf16(128, 64, 0, 0), k > 0);
+    umma_commit(&bars[3]);
+  }
+  if (owner) {
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_bounded(&bars[3], 0, nullptr, args.status, kTimeoutEpilogue));
+    if (ok) {
+      tc_fence_after();
+      float rb = 0.f, rg = 0.f;
+#pragma unroll 1
+      for (int h2 = 0; h2 < 2; ++h2) {
+        float f[32], x3[32];
+        ld32(tl + 256 + h2 * 32, f);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int j = h2 * 32 + e;
+          const float dl = j < i ? -f[e] : 0.f;
+          const float ex = j <= i ? __expf(Gi - Gs[j]) : 0.f;
+          const float kk = KKs[sk(i, j)];
+          const float x1 = dl * Bi * ex;
+          rb = fmaf(dl * ex, kk, rb);
+          const float m = x1 * kk;
+          const float daq = j <= i ? dAs[sk(i, j)] : 0.f;
+          const float xq = daq * ex;
+          const float pq = xq * QKs[sk(i, j)];
+          rg += m + pq;
+          Mc[sk(i, j)] = -(m + pq);
+          X1s[sk(i, j)] = x1;
+          x3[e] = a.scale * xq;
+        }
+#pragma unroll
+        for (int m = 0; m < 4; ++m) put8(sX3, i, h2 * 4 + m, pack8(x3 + 8 * m));
+      }
+      dB_own += rb;
+      dG_own += rg;
+    }
+    named_bar_sync(1, 64);
+    if (ok) {
+      // symmetric part of dKK: X1 + X1^T
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        float x[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const int j = cc * 8 + m;
+          x[m] = X1s[sk(i, j)] + X1s[sk(j, i)];
+        }
+        put8(sXS, i, cc, pack8(x));
+      }
+    }
+  }
+  fence_proxy_async();
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+
+  // ---- D5 += (X1 + X1^T) k + X3^T q, D6 = X3 k, D7 = T^T dDelta
+  if (ok && tid == 0) {
+    tc_fence_after();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) umma_bf16_ss(tmem, kmaj(aXS, k), mnmaj(aK, k), make_idesc_bf16(128, 128, 0, 1), 1);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) umma_bf16_ss(tmem, mnmaj(aX3, k), mnmaj(aQ, k), make_idesc_bf16(128, 128, 1, 1), 1);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      umma_bf16_ss(tmem + 384, kmaj(aX3, k), mnmaj(aK, k), make_idesc_bf16(128, 128, 0, 1), k > 0);
+    umma_commit(&bars[4]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      umma_bf16_ss(tmem + 128, mnmaj(aT, k), kmaj(aDD, k), make_idesc_bf16(128, DV, 1, 0), k > 0);
+    umma_commit(&bars[5]);
+  }
+  if (!owner && ok) {
+    // column sums of the dG contributions (rows of Mc are complete after the last barrier)
+    const int j = tid - 64;
+    float s = 0.f;
+#pragma unroll 8
+    for (int r = 0; r < C; ++r) s += Mc[sk(r, j)];
+    dGc[j] = s;
+  }
+  if (owner) {
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_bounded(&bars[4], 0, nullptr, args.status, kTimeoutEpilogue));
+    if (ok) {
+      tc_fence_after();
+      const float ed = __expf(GL - Gi);
+      float qpart = 0.f, kpart = 0.f;
+      const long off = ((long)(t0 + i) * H + h) * DK;
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float d5[32], d6[32], kf[32], qf[32];
+        ld32(tl + q4 * 32, d5);
+        ld32(tl + 384 + q4 * 32, d6);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          get_row_f(sK, i, q4 * 4 + m, kf + 8 * m);
+          get_row_f(sQ, i, q4 * 4 + m, qf + 8 * m);
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const long col = (ch * DK + q4 * 32 + e) * C + i;
+          const float wk = a.dKdT[col], wq = a.dQgT[col];
+          kpart = fmaf(wk, kf[e], kpart);
+          qpart = fmaf(wq, qf[e], qpart);
+          d5[e] = fmaf(ed, wk, d5[e]);
+          d6[e] = fmaf(a.scale * egi, wq, d6[e]);
+        }
+        if (i < n) {
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            reinterpret_cast<uint4*>(a.dk + off + q4 * 32)[m] = pack8(d5 + 8 * m);
+            reinterpret_cast<uint4*>(a.dq + off + q4 * 32)[m] = pack8(d6 + 8 * m);
+          }
+        }
+      }
+      dG_own += egi * a.scale * qpart;
+      kpart *= ed;
+      dG_own -= kpart;
+      atomicAdd(&misc[0], kpart);
+    }
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_bounded(&bars[5], 0, nullptr, args.status, kTimeoutEpilogue));
+    if (ok) {
+      tc_fence_after();
+      const long off = ((long)(t0 + i) * H + h) * DV;
+#pragma unroll 1
+      for (int q = 0; q < DV / 32; ++q) {
+        float d7[32];
+        ld32(tl + 128 + q * 32, d7);
+        if (i < n) {
+          float vv[32], o[32];
+#pragma unroll
+          for (int m = 0; m < 4; ++m) unpack8(reinterpret_cast<const uint4*>(a.v + off + q * 32)[m], vv + 8 * m);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            dB_own = fmaf(d7[e], vv[e], dB_own);
+            o[e] = Bi * d7[e];
+          }
+#pragma unroll
+          for (int m = 0; m < 4; ++m) reinterpret_cast<uint4*>(a.dv + off + q * 32)[m] = pack8(o + 8 * m);
+        }
+      }
+    }
+  }
+  ok = __syncthreads_and(ok);
+  // ---- dg = reverse cumulative sum of dG over the chunk; dbeta
+  float* dGt = X1s;
+  float* dBt = X1s + C;
+  if (owner) {
+    float t = dG_own + dGc[i];
+    if (i == C - 1) t += misc[0] + __expf(GL) * a.dgam[ch];
+    dGt[i] = t;
+    dBt[i] = dB_own;
+  }
+  __syncthreads();
+  if (ok && tid < 32) {
+    float x0 = dGt[tid], x1 = dGt[tid + 32];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y0 = __shfl_down_sync(0xffffffffu, x0, o);
+      const float y1 = __shfl_down_sync(0xffffffffu, x1, o);
+      if (tid + o < 32) {
+        x0 += y0;
+        x1 += y1;
+      }
+    }
+    x0 += __shfl_sync(0xffffffffu, x1, 0);
+    if (tid < n) {
+      a.dg[(long)(t0 + tid) * H + h] = x0;
+      a.dbeta[(long)(t0 + tid) * H + h] = dBt[tid];
+    }
+    if (tid + 32 < n) {
+      a.dg[(long)(t0 + tid + 32) * H + h] = x1;
+      a.dbeta[(long)(t0 + tid + 32) * H + h] = dBt[tid + 32];
+    }
+  }
+  if (tid == 0 && !ok) mbar_wait_bounded(&bars[0], 0, nullptr, nullptr, 0);  // no TMA copy outlives the CTA
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
 // ============================================================================ host
 CUtensorMap map2d(const at::Tensor& t, int64_t rows, int64_t cols, int64_t row_stride) {
   TORCH_CHECK(t.scalar_type() == at::kBFloat16, "gdn: bf16 tensor expected");
@@ -1473,6 +1910,17 @@ void gdn_chunk_bwd_state(const at::Tensor& Wn, const at::Tensor& Kd, const at::T
   launch_state<true>(Wn, Qg, Kd, Aqk, dout.view({dout.size(0), (int64_t)H * DV}), p, nseq, Nc);
 }
 
+// Which chunk-local backward runs: the tensor-core kernel (default) or the CUDA-core kernel
+// (PRISM_GDN_LOCAL_TC=0, or gdn_local_tc_enabled(0)); `set` < 0 only queries.
+bool gdn_local_tc_enabled(int64_t set) {
+  static int state = [] {
+    const char* e = getenv("PRISM_GDN_LOCAL_TC");
+    return (e == nullptr || strcmp(e, "0") != 0) ? 1 : 0;
+  }();
+  if (set >= 0) state = set != 0;
+  return state != 0;
+}
+
 // Chunk-local backward: dv-contractions on tcgen05, then the WY/decay backward.
 std::vector<at::Tensor> gdn_chunk_bwd_local(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                             const at::Tensor& g, const at::Tensor& beta, const at::Tensor& tok0,
@@ -1516,6 +1964,19 @@ std::vector<at::Tensor> gdn_chunk_bwd_local(const at::Tensor& q, const at::Tenso
                reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()),
                reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()), dg.data_ptr<float>(), dbeta.data_ptr<float>(),
                (float)scale, H, DV};
+  if (gdn_local_tc_enabled(-1)) {
+    const int64_t T = q.size(0);
+    CUtensorMap mQ = map2d(q, T, (int64_t)H * DK, (int64_t)H * DK), mK = map2d(k, T, (int64_t)H * DK, (int64_t)H * DK);
+    static bool attr_tc = false;
+    if (!attr_tc) {
+      C10_CUDA_CHECK(
+          cudaFuncSetAttribute(gdn_bwd_local_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lt::SMEM));
+      attr_tc = true;
+    }
+    gdn_bwd_local_tc_kernel<<<Nc * H, lt::THREADS, lt::SMEM, stream>>>(mQ, mK, mDD, LocalTcArgs{la, status.data_ptr<int>()});
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return {dq, dk, dv, dg, dbeta};
+  }
   static bool attr_lb = false;
   if (!attr_lb) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(gdn_bwd_local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LB_SMEM));

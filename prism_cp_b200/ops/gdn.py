@@ -304,13 +304,14 @@ class _FusedChunkRule(torch.autograd.Function):
     def backward(ctx, do, dS_final):
         L = lib()
         lay = ctx.layout
-        main = torch.cuda.current_stream(ctx.saved_tensors[0].device)
+        saved = ctx.saved_tensors  # unpacked once (activation checkpointing allows a single unpack)
+        main = torch.cuda.current_stream(saved[0].device)
         side = main
         if ctx.kept:
-            qb, kb, vb, gf, bt, s0, Wn, U, Kd, Qg, Aqk, gam, Gc, aux, states, rows = ctx.saved_tensors
+            qb, kb, vb, gf, bt, s0, Wn, U, Kd, Qg, Aqk, gam, Gc, aux, states, rows = saved
             st = status(qb.device)
         else:
-            qb, kb, vb, gf, bt, s0 = ctx.saved_tensors
+            qb, kb, vb, gf, bt, s0 = saved
             st = status(qb.device)
             Wn, U, Kd, Qg, Aqk, gam, Gc, aux = L.gdn_chunk_prep(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev,
                                                                 ctx.scale, True, st)

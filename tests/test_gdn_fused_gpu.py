@@ -87,3 +87,26 @@ def test_module_bench_gates_and_records(module, tmp_path):
     doc = json.loads(out.read_text())
     assert {"repeat", "packed", "reference"} <= set(doc["gates"])
     assert len(doc["records"]) == 2 and all(r["fb_ms"] > 0 for r in doc["records"])
+
+
+@pytest.mark.parametrize("lens,dv", [((150, 70, 300), 128), ((384, 128, 64), 256)])
+def test_tensor_core_local_backward_matches_cuda_core_kernel(lens, dv):
+    """The tcgen05 chunk-local backward and the CUDA-core one compute the same gradients
+    (bf16 operands on the tensor cores: agreement to 2e-2 relative)."""
+    from prism_cp_b200.ops._lib import check_status, lib
+    from prism_cp_b200.ops.gdn import ChunkLayout, fused_gated_delta_rule
+    q, k, v, gl, beta, _ = _inputs(lens, 3, dv, 5, False)
+    w = torch.randn(sum(lens), 3, dv, generator=torch.Generator().manual_seed(3)).to(DEV)
+    grads = {}
+    for tc in (1, 0):
+        lib().gdn_local_tc_enabled(tc)
+        ts = [t.detach().clone().to(DEV).requires_grad_(True) for t in (q, k, v, gl, beta)]
+        o, _ = fused_gated_delta_rule(*ts, ChunkLayout(lens, torch.device(DEV)))
+        (o.float() * w).sum().backward()
+        grads[tc] = [t.grad.float().cpu() for t in ts]
+    lib().gdn_local_tc_enabled(1)
+    torch.cuda.synchronize()
+    check_status(torch.device(DEV))
+    for name, a, b in zip(("q", "k", "v", "g", "beta"), grads[1], grads[0]):
+        assert torch.isfinite(a).all(), name
+        assert rel_err(a, b) < 2e-2, f"d{name}: {rel_err(a, b)}"

@@ -271,6 +271,36 @@ def test_model_step_gpu_matches_fp32_cpu_direction():
     assert abs(losses[0] - losses[1]) / abs(losses[0]) < 2e-2
 
 
+def test_recomputed_layers_on_cuda_match_stored_activations():
+    """Per-layer recompute on the CUDA kernels (GDN fused rule, attention, GEMMs): the loss and
+    every gradient equal the run that keeps its activations."""
+    from prism_cp_b200.models.config import HybridConfig
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.parallel.teams import Teams
+    from prism_cp_b200.planner.fixed import uniform_plan
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.trainer import Trainer
+    cfg = HybridConfig(num_layers=4, hidden_size=256, ffn_hidden_size=512, vocab_size=4096,
+                       num_attention_heads=4, num_query_groups=2, kv_channels=128,
+                       linear_num_key_heads=2, linear_key_head_dim=128, linear_value_head_dim=256)
+    dev = torch.device(DEV, torch.cuda.current_device())
+    out = {}
+    for limit in (None, 256):
+        model = HybridModel(cfg, dtype=torch.bfloat16, device=dev, seed=0)
+        batch = make_batch([640, 384], cfg.vocab_size, seed=2)
+        plan = uniform_plan(batch.lengths, 1, 1, 1024, cfg.pattern)
+        tr = Trainer(model, Teams(1), dev, recompute_tokens=limit)
+        tr.flat.zero_grad()
+        loss = tr.forward_backward(batch.lengths, plan, [h.to(dev) for h in tr.prepare(batch, plan)])
+        tr.flat.fold_param_grads()
+        torch.cuda.synchronize()
+        out[limit] = (float(loss), tr.flat.grad.clone())
+    assert abs(out[None][0] - out[256][0]) <= 1e-3 * abs(out[None][0])
+    g0, g1 = out[None][1], out[256][1]
+    assert torch.isfinite(g1).all()
+    assert ((g0 - g1).norm() / g0.norm()).item() < 1e-2
+
+
 # ------------------------------------------------------------------ bounded device waits
 def test_a_device_wait_that_runs_out_reports_an_error_and_the_context_survives():
     """A flag nothing sets: the bounded wait gives up after its limit, records an error status the
