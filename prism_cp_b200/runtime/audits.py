@@ -130,3 +130,110 @@ def check_packet_inputs(source, update: int, ingress_layout, world: int, rank: i
             raise AssertionError(f"input integrity: {name} differ from the deterministic content rule")
     if not torch.equal(weights.cpu().float() > 0, w > 0):
         raise AssertionError("input integrity: loss mask differs from the content rule")
+
+
+def _in_backward() -> bool:
+    """True while the autograd engine runs a backward (e.g. a checkpointed layer recomputing)."""
+    return torch._C._current_graph_task_id() != -1
+
+
+class TokenwiseFusionAudit:
+    """Every tokenwise operator (a layer's mixer projections and its MLP) runs exactly once per
+    executed microbatch on all of the rank's rows, whatever mix of CP teams the microbatch uses
+    (the executor never splits a tokenwise GEMM per CP segment). Counts forward calls of the
+    layers' mixer and MLP modules; recomputation inside a backward is not a new call. The
+    reference enforces the same on the first step of a mixed-CP run (runtime.py:372-391, 423-426)."""
+
+    def __init__(self, model):
+        self.calls: dict[str, int] = {}
+        self.handles = []
+        for index, layer in enumerate(getattr(model, "layers", [])):
+            for name in ("mixer", "mlp"):
+                module = getattr(layer, name, None)
+                if module is None:
+                    continue
+                key = f"layer{index}.{name}"
+                self.calls[key] = 0
+                self.handles.append(module.register_forward_hook(self._counter(key)))
+
+    def _counter(self, key: str):
+        def hook(module, inputs, output):
+            if not _in_backward():
+                self.calls[key] += 1
+        return hook
+
+    def reset(self) -> None:
+        for key in self.calls:
+            self.calls[key] = 0
+
+    def check(self, microbatches: int) -> None:
+        wrong = {k: v for k, v in self.calls.items() if v != microbatches}
+        if wrong:
+            raise ValueError(f"Tokenwise operators were not fused per microbatch (expected {microbatches}): {wrong}")
+
+    def close(self) -> None:
+        for h in self.handles:
+            h.remove()
+        self.handles = []
+
+
+class PacketAccounting:
+    """Forward/backward accounting of one update's microbatches (the reference's packet F/B
+    checks, mixed_packet_integrity.py:21-47,99-101):
+
+    * the parameter version (optimizer steps taken) must not change between the first forward
+      and the last backward of an update;
+    * every microbatch runs exactly one forward and one backward (counted at the embedding
+      output, so recomputed layers do not count twice);
+    * with ``memory_samples``, allocator state is sampled at forward end, before and after the
+      loss and at backward end, for microbatches 1, 2, every 8th and the last."""
+
+    def __init__(self, memory_samples: bool = False):
+        self.memory_samples = memory_samples
+        self.samples: list[dict] = []
+        self.version = None
+        self.forwards = self.backwards = 0
+        self.expected = 0
+
+    def begin(self, version: int, microbatches: int) -> None:
+        self.version, self.expected = version, microbatches
+        self.forwards = self.backwards = 0
+        self.samples = []
+
+    def _wanted(self, ordinal: int) -> bool:
+        return ordinal <= 2 or ordinal % 8 == 0 or ordinal == self.expected
+
+    def sample(self, phase: str, ordinal: int) -> None:
+        if not (self.memory_samples and torch.cuda.is_available() and torch.cuda.is_initialized()):
+            return
+        if self._wanted(ordinal):
+            stats = torch.cuda.memory_stats()
+            self.samples.append({"phase": phase, "microbatch": ordinal, "allocated": torch.cuda.memory_allocated(),
+                                 "reserved": torch.cuda.memory_reserved(),
+                                 "active": stats.get("active_bytes.all.current", 0),
+                                 "inactive_split": stats.get("inactive_split_bytes.all.current", 0),
+                                 "free_total": list(torch.cuda.mem_get_info())})
+
+    def forward(self, embedded: torch.Tensor, version: int) -> torch.Tensor:
+        """Count a microbatch forward at its embedding output and arm the backward count."""
+        if version != self.version:
+            raise ValueError("Parameter version changed inside packet")
+        self.forwards += 1
+        ordinal = self.forwards
+        if embedded.requires_grad:
+            def on_backward(grad, ordinal=ordinal):
+                self.backwards += 1
+                if version != self.version:
+                    raise ValueError("Parameter version changed during backward")
+                self.sample("B_end", ordinal)
+                return grad
+            embedded.register_hook(on_backward)
+        return embedded
+
+    def finish(self, version: int) -> dict:
+        if version != self.version:
+            raise ValueError("Parameter version changed inside packet")
+        if self.forwards != self.expected or self.backwards != self.expected:
+            raise ValueError(f"Packet F/B mismatch {self.forwards}/{self.backwards}/{self.expected}")
+        return {"forwards": self.forwards, "backwards": self.backwards, "parameter_version": self.version,
+                "memory_boundary_samples": list(self.samples)}

@@ -70,11 +70,21 @@ class MicrobatchRun:
             prev = ctx
         return x, prev
 
-    def forward(self, model, tokens, labels, weights):
+    def forward(self, model, tokens, labels, weights, packet=None, version: int = 0):
+        """Loss of this microbatch; ``packet`` (an ``audits.PacketAccounting``) counts the forward
+        at the embedding output and samples memory at forward end and around the loss."""
         x = model.embed(tokens)
+        if packet is not None:
+            x = packet.forward(x, version)
         x, prev = self.forward_layers(model, x)
         x = move(x, prev, self.ingress)
-        return model.loss(x, labels, weights)
+        if packet is None:
+            return model.loss(x, labels, weights)
+        packet.sample("F_end", packet.forwards)
+        packet.sample("CE_before", packet.forwards)
+        out = model.loss(x, labels, weights)
+        packet.sample("CE_after", packet.forwards)
+        return out
 
 
 def recomputes(mb: Microbatch, lengths: dict, world: int, limit: int) -> bool:

@@ -22,7 +22,7 @@ import torch
 import torch.distributed as dist
 
 from ..planner.joint.ir import Plan
-from .audits import AccumulationAudit
+from .audits import AccumulationAudit, PacketAccounting, TokenwiseFusionAudit
 from .batch import GlobalBatch, HostInputs, local_inputs
 from .executor import LayoutCache, MicrobatchRun
 from .optimizer import DistributedAdamW, FlatParameters
@@ -85,6 +85,9 @@ class Trainer:
             # rebuild logical samples from the ranks of this TP index only (the others hold copies)
             logical.group = self.group
         self.audit = AccumulationAudit() if audit else None
+        # audited steps also check tokenwise fusion and per-microbatch F/B accounting
+        self.fusion = TokenwiseFusionAudit(model) if audit else None
+        self.packets = PacketAccounting(memory_samples=audit and device.type == "cuda") if audit else None
         self.step_index = 0
         self.watchdog = watchdog.from_env()
         # microbatches above this many tokens on a rank recompute their layers in the backward
@@ -113,7 +116,8 @@ class Trainer:
                     y = move(y, prev, run.ingress)
                     loss, ce = self.model.loss(y, dev.labels, dev.weights)
                 else:
-                    loss, _ = run.forward(self.model, dev.tokens, dev.labels, dev.weights)
+                    loss, _ = run.forward(self.model, dev.tokens, dev.labels, dev.weights, self.packets,
+                                          self.optimizer.step_count)
             self._debug_point(index, "forward")
             if self.overlap is not None:
                 # the last backward reduce-scatters each finished bucket while it runs
@@ -177,11 +181,17 @@ class Trainer:
         if self.audit is not None:
             self.audit.events.clear()
             self.audit.times.clear()
+            self.fusion.reset()
+            self.packets.begin(self.optimizer.step_count, len(plan.microbatches))
         self.flat.zero_grad()
         loss = self.forward_backward(batch.lengths, plan, inputs)
         if self.logical is not None:
             self.logical.finish(self.step_index + 1)
         if self.audit is not None:
+            logical = self.logical is not None and self.logical.active(self.step_index + 1)
+            self.fusion.check(len(plan.microbatches))
+            if not logical:
+                self.last_packet = self.packets.finish(self.optimizer.step_count)
             self.optimizer.audit = self.audit
         lr = self.optimizer.step()
         self.step_index += 1
@@ -207,7 +217,8 @@ class Trainer:
                 peak_reserved=torch.cuda.max_memory_reserved(self.device) if cuda else 0,
                 memory_budget=mem.get("budget", 0), memory_required=mem.get("required", 0), admitted=admitted,
                 external_before=external_before, external_after=mem.get("external", 0),
-                sync=dict(self.optimizer.stats), finite=finite_ok))
+                sync=dict(self.optimizer.stats), finite=finite_ok,
+                **self._packet_counts()))
         if self.run_records is not None:
             self.run_records.step(self.step_index, self, plan)
         if not finite_ok:
@@ -217,6 +228,11 @@ class Trainer:
         return StepResult(value, loss, batch.total_tokens, len(plan.microbatches), lr,
                           elapsed_ms=float(elapsed.item()), grad_norm=grad_norm,
                           peak_allocated=mem.get("peak_allocated"), admitted=admitted, extra=mem)
+
+    def _packet_counts(self) -> dict:
+        """Observed forward/backward counts of the last audited step (the planned count otherwise)."""
+        packet = getattr(self, "last_packet", None)
+        return {} if packet is None else {"forwards": packet["forwards"], "backwards": packet["backwards"]}
 
     def _external(self) -> int:
         free, total = torch.cuda.mem_get_info(self.device)

@@ -463,8 +463,11 @@ def _mixed_case(rank, world):
     plan = Plan(4, cfg.pattern, (Microbatch(gqa, tuple((gdn, gdn) if c == "G" else (gqa, gqa)
                                                        for c in cfg.pattern)),))
     tr = Trainer(HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0), Teams(world), torch.device("cpu"),
-                 lr=1e-3)
+                 lr=1e-3, audit=True)
     losses = [tr.train_step(batch, plan).loss for _ in range(2)]
+    # tokenwise operators ran once per microbatch over all segments (CP2 + CP1 + CP1 attention teams)
+    assert tr.fusion.calls and all(v == 1 for v in tr.fusion.calls.values()), tr.fusion.calls
+    assert tr.last_packet["forwards"] == tr.last_packet["backwards"] == 1
     if rank == 0:
         one = Layout((Group((0,), (0, 1, 2)),), "zigzag")
         ref_plan = Plan(1, cfg.pattern, (Microbatch(one, tuple((one.with_mode("contiguous"),) * 2 if c == "G"

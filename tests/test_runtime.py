@@ -234,3 +234,36 @@ def test_planner_prices_recompute_for_oversize_documents():
     assert [bool(r.get("recompute")) for r in rows].count(True) == 1 and all(r["fits"] for r in rows)
     long_mb = next(mb for mb, r in zip(sel.plan.microbatches, rows) if r.get("recompute"))
     assert 0 in long_mb.ingress.groups[0].samples
+
+
+def test_tokenwise_fusion_and_packet_accounting():
+    """Audited steps: every mixer / MLP runs once per microbatch (not per CP segment), every
+    microbatch runs one forward and one backward, and the parameter version holds within the update."""
+    from prism_cp_b200.runtime.audits import PacketAccounting, TokenwiseFusionAudit
+    tr, batch, plan = _trainer(None, audit=True)
+    tr.train_step(batch, plan)
+    assert all(v == len(plan.microbatches) for v in tr.fusion.calls.values()) and tr.fusion.calls
+    assert tr.last_packet["forwards"] == tr.last_packet["backwards"] == len(plan.microbatches)
+    # a mixer called twice in one microbatch (split per segment) is caught
+    tr.fusion.reset()
+    tr.fusion.calls["layer0.mixer"] = 2 * len(plan.microbatches)
+    with pytest.raises(ValueError, match="not fused"):
+        tr.fusion.check(len(plan.microbatches))
+    # a parameter update between forward and backward is caught
+    acct = PacketAccounting()
+    acct.begin(version=3, microbatches=1)
+    x = torch.ones(2, requires_grad=True)
+    y = acct.forward(x * 2, 3)
+    acct.version = 4
+    with pytest.raises(ValueError, match="during backward"):
+        y.sum().backward()
+    acct2 = PacketAccounting()
+    acct2.begin(version=0, microbatches=2)
+    acct2.forward(torch.ones(2, requires_grad=True) * 1, 0).sum().backward()
+    with pytest.raises(ValueError, match="F/B mismatch"):
+        acct2.finish(0)
+    # recomputed layers are not counted twice
+    cfg_tr = Trainer(HybridModel(hybrid_tiny(), dtype=torch.float32, device="cpu", seed=0), Teams(1),
+                     torch.device("cpu"), audit=True, recompute_tokens=64)
+    cfg_tr.train_step(batch, plan)
+    assert all(v == len(plan.microbatches) for v in cfg_tr.fusion.calls.values())
