@@ -1334,11 +1334,17 @@ __global__ void __launch_bounds__(LB_THREADS, 1) gdn_bwd_local_kernel(LocalArgs 
 // Operands are bf16 in 128-byte-swizzled shared memory; accumulation is fp32 in TMEM.
 namespace lt {
 constexpr int THREADS = 128;
-constexpr int TMEM_COLS = 512;  // D1/D5 [0,128) D2 [128,192) D3 [192,256) D4 [256,320) D6 [384,512) D7 [128,128+DV)
+// 256 TMEM columns and under 100 KB of shared memory per CTA, so two CTAs share an SM and
+// one CTA's loads and epilogues hide the other's MMA and barrier latency:
+//   TMEM: D1/D5 [0,128), D2 [128,192), D3 [192,256), D4 [128,192), D6 [128,256), D7 [0,DV)
+//   smem blocks (8 KB each): K 0-1, Q 2-3, T 4, dW 5-6, X2 7, Z 8, X1+X1^T 9, s X3 10, slack 11
+//   (read as the unused rows 64..127 of M = 128 operands). Blocks 5-8 are reused: fp32 X1 and
+//   the dG column terms while the dL epilogue runs, then dDelta^T for D7.
+constexpr int TMEM_COLS = 256;
 constexpr int OFF_K = 0, OFF_Q = 2 * BLK, OFF_T = 4 * BLK, OFF_W = 5 * BLK, OFF_X2 = 7 * BLK, OFF_Z = 8 * BLK;
-constexpr int OFF_XS = 9 * BLK, OFF_X3 = 10 * BLK, OFF_DD = 11 * BLK, OFF_F = 15 * BLK;
+constexpr int OFF_XS = 9 * BLK, OFF_X3 = 10 * BLK, OFF_DD = OFF_W, OFF_F = OFF_W, OFF_END = 12 * BLK;
 constexpr int FT = C * C;  // one fp32 64 x 64 tile (rows skewed: element (r, j) at r * 64 + ((j + r) & 63))
-constexpr int SMEM = OFF_F + 5 * FT * 4 + 4 * C * 4 + 64 + 1024;
+constexpr int SMEM = OFF_END + 4 * C * 4 + 64 + 1024;
 
 // fp32 tile element (r, j) with the row skew that keeps row-per-thread and column-per-thread
 // accesses free of bank conflicts
@@ -1382,15 +1388,12 @@ __global__ void __launch_bounds__(lt::THREADS, 1)
   uint8_t* sDD = smem + OFF_DD;
   float* X1s = reinterpret_cast<float*>(smem + OFF_F);
   float* Mc = X1s + FT;   // -(dG contributions) per (row, column): summed over rows by warps 2-3
-  float* KKs = Mc + FT;
-  float* QKs = KKs + FT;
-  float* dAs = QKs + FT;
-  float* Gs = dAs + FT;
+  float* Gs = reinterpret_cast<float*>(smem + OFF_END);
   float* Bs = Gs + C;
   float* dGc = Bs + C;
   float* misc = dGc + C;  // [0]: dG of the last row from the dKd terms
   uint64_t* bars = reinterpret_cast<uint64_t*>(misc + C);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
   const int H = a.H, DV = a.DV, nvb = DV / 64;
   const long ch = blockIdx.x;
   const int c = (int)(ch / H), h = (int)(ch % H);
@@ -1401,7 +1404,7 @@ __global__ void __launch_bounds__(lt::THREADS, 1)
 
   if (tid == 0) {
 #pragma unroll
-    for (int b = 0; b < 6; ++b) mbar_init(&bars[b], 1);
+    for (int b = 0; b < 7; ++b) mbar_init(&bars[b], 1);
     misc[0] = 0.f;
     fence_barrier_init();
   }
@@ -1415,12 +1418,11 @@ __global__ void __launch_bounds__(lt::THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (tid == 0) {
-    mbar_arrive_expect_tx(&bars[0], (4 + nvb) * BLK);
+    mbar_arrive_expect_tx(&bars[0], 4 * BLK);
     tma_load_2d(sK, &mK, &bars[0], h * DK, t0);
     tma_load_2d(sK + BLK, &mK, &bars[0], h * DK + 64, t0);
     tma_load_2d(sQ, &mQ, &bars[0], h * DK, t0);
     tma_load_2d(sQ + BLK, &mQ, &bars[0], h * DK + 64, t0);
-    for (int b = 0; b < nvb; ++b) tma_load_2d(sDD + b * BLK, &mDD, &bars[0], 0, (int)(ch * DV) + b * 64);
   }
   if (warp == 0) {
     const int l = tid;
@@ -1441,9 +1443,10 @@ __global__ void __launch_bounds__(lt::THREADS, 1)
     Gs[l] = x0;
     Gs[l + 32] = x1;
   }
-  // operands staged by all threads: T (rows l, cols i), dW = -dWn (rows i, cols a), and the fp32
-  // k.k, s q.k and dAqk tiles the dL epilogue reads row-wise
+  // operands staged by all threads: T (rows l, cols i) and dW = -dWn (rows i, cols a); the loops
+  // are unrolled so that each thread's global loads are in flight together
   const float* aux = a.aux + ch * 3 * C * C;
+#pragma unroll 4
   for (int e = tid; e < C * 8; e += THREADS) {
     const int l = e >> 3, cc = e & 7;
     const float4 x = reinterpret_cast<const float4*>(aux + 2 * C * C + l * C)[2 * cc];
@@ -1451,18 +1454,13 @@ __global__ void __launch_bounds__(lt::THREADS, 1)
     const float f[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
     put8(sT, l, cc, pack8(f));
   }
+#pragma unroll 8
   for (int e = tid; e < C * 16; e += THREADS) {
     const int r = e & 63, a8 = (e >> 6) * 8;
     float f[8];
 #pragma unroll
     for (int m = 0; m < 8; ++m) f[m] = -a.dWnT[(ch * DK + a8 + m) * C + r];
     put8(sW, r, a8 >> 3, pack8(f));
-  }
-  for (int e = tid; e < C * C; e += THREADS) {
-    const int r = e >> 6, j = e & 63;
-    KKs[sk(r, j)] = aux[e];
-    QKs[sk(r, j)] = aux[C * C + e];
-    dAs[sk(r, j)] = a.dAqk[ch * C * C + e];
   }
   bool ok = __syncthreads_and(mbar_wait_bounded(&bars[0], 0, nullptr, args.status, kTimeoutProducer));
   if (ok && n < C) {
@@ -1569,7 +1567,7 @@ __global__ void __launch_bounds__(lt::THREADS, 1)
     tc_fence_after();
 #pragma unroll
     for (int k = 0; k < 4; ++k)
-      umma_bf16_ss(tmem + 256, kmaj(aZ, k), kmaj(aT, k), make_idesc_bf16(128, 64, 0, 0), k > 0);
+      umma_bf16_ss(tmem + 128, kmaj(aZ, k), kmaj(aT, k), make_idesc_bf16(128, 64, 0, 0), k > 0);
     umma_commit(&bars[3]);
   }
   if (owner) {
@@ -1579,20 +1577,31 @@ __global__ void __launch_bounds__(lt::THREADS, 1)
       float rb = 0.f, rg = 0.f;
 #pragma unroll 1
       for (int h2 = 0; h2 < 2; ++h2) {
-        float f[32], x3[32];
-        ld32(tl + 256 + h2 * 32, f);
+        // this row's k.k, s q.k (from the prep) and dAqk: independent 16-byte loads, all in flight
+        float f[32], x3[32], kkr[32], qkr[32], dar[32];
+        const float4* pk = reinterpret_cast<const float4*>(aux + i * C + h2 * 32);
+        const float4* pq4 = reinterpret_cast<const float4*>(aux + C * C + i * C + h2 * 32);
+        const float4* pa = reinterpret_cast<const float4*>(a.dAqk + (ch * C + i) * C + h2 * 32);
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const float4 x = pk[m], y = pq4[m], z = pa[m];
+          kkr[4 * m] = x.x; kkr[4 * m + 1] = x.y; kkr[4 * m + 2] = x.z; kkr[4 * m + 3] = x.w;
+          qkr[4 * m] = y.x; qkr[4 * m + 1] = y.y; qkr[4 * m + 2] = y.z; qkr[4 * m + 3] = y.w;
+          dar[4 * m] = z.x; dar[4 * m + 1] = z.y; dar[4 * m + 2] = z.z; dar[4 * m + 3] = z.w;
+        }
+        ld32(tl + 128 + h2 * 32, f);
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int j = h2 * 32 + e;
           const float dl = j < i ? -f[e] : 0.f;
           const float ex = j <= i ? __expf(Gi - Gs[j]) : 0.f;
-          const float kk = KKs[sk(i, j)];
+          const float kk = kkr[e];
           const float x1 = dl * Bi * ex;
           rb = fmaf(dl * ex, kk, rb);
           const float m = x1 * kk;
-          const float daq = j <= i ? dAs[sk(i, j)] : 0.f;
+          const float daq = j <= i ? dar[e] : 0.f;
           const float xq = daq * ex;
-          const float pq = xq * QKs[sk(i, j)];
+          const float pq = xq * qkr[e];
           rg += m + pq;
           Mc[sk(i, j)] = -(m + pq);
           X1s[sk(i, j)] = x1;
@@ -1623,7 +1632,7 @@ __global__ void __launch_bounds__(lt::THREADS, 1)
   tc_fence_before();
   ok = __syncthreads_and(ok);
 
-  // ---- D5 += (X1 + X1^T) k + X3^T q, D6 = X3 k, D7 = T^T dDelta
+  // ---- D5 += (X1 + X1^T) k + X3^T q, D6 = X3 k
   if (ok && tid == 0) {
     tc_fence_after();
 #pragma unroll
@@ -1632,12 +1641,8 @@ __global__ void __launch_bounds__(lt::THREADS, 1)
     for (int k = 0; k < 4; ++k) umma_bf16_ss(tmem, mnmaj(aX3, k), mnmaj(aQ, k), make_idesc_bf16(128, 128, 1, 1), 1);
 #pragma unroll
     for (int k = 0; k < 4; ++k)
-      umma_bf16_ss(tmem + 384, kmaj(aX3, k), mnmaj(aK, k), make_idesc_bf16(128, 128, 0, 1), k > 0);
+      umma_bf16_ss(tmem + 128, kmaj(aX3, k), mnmaj(aK, k), make_idesc_bf16(128, 128, 0, 1), k > 0);
     umma_commit(&bars[4]);
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-      umma_bf16_ss(tmem + 128, mnmaj(aT, k), kmaj(aDD, k), make_idesc_bf16(128, DV, 1, 0), k > 0);
-    umma_commit(&bars[5]);
   }
   if (!owner && ok) {
     // column sums of the dG contributions (rows of Mc are complete after the last barrier)
@@ -1658,7 +1663,7 @@ __global__ void __launch_bounds__(lt::THREADS, 1)
       for (int q4 = 0; q4 < 4; ++q4) {
         float d5[32], d6[32], kf[32], qf[32];
         ld32(tl + q4 * 32, d5);
-        ld32(tl + 384 + q4 * 32, d6);
+        ld32(tl + 128 + q4 * 32, d6);
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
           get_row_f(sK, i, q4 * 4 + m, kf + 8 * m);
@@ -1686,6 +1691,26 @@ __global__ void __launch_bounds__(lt::THREADS, 1)
       dG_own -= kpart;
       atomicAdd(&misc[0], kpart);
     }
+  }
+  // ---- D7 = T^T dDelta, once D5 / D6 are read and blocks 5-8 are free: dDelta^T arrives there
+  fence_proxy_async();
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  bool dd_issued = false;
+  if (ok && tid == 0) {
+    mbar_arrive_expect_tx(&bars[6], nvb * BLK);
+    for (int b = 0; b < nvb; ++b) tma_load_2d(sDD + b * BLK, &mDD, &bars[6], 0, (int)(ch * DV) + b * 64);
+    dd_issued = true;
+    if (mbar_wait_bounded(&bars[6], 0, nullptr, args.status, kTimeoutProducer)) {
+      dd_issued = false;
+      tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        umma_bf16_ss(tmem, mnmaj(aT, k), kmaj(aDD, k), make_idesc_bf16(128, DV, 1, 0), k > 0);
+      umma_commit(&bars[5]);
+    }
+  }
+  if (owner) {
     ok = __all_sync(0xffffffffu, ok && mbar_wait_bounded(&bars[5], 0, nullptr, args.status, kTimeoutEpilogue));
     if (ok) {
       tc_fence_after();
@@ -1693,7 +1718,7 @@ __global__ void __launch_bounds__(lt::THREADS, 1)
 #pragma unroll 1
       for (int q = 0; q < DV / 32; ++q) {
         float d7[32];
-        ld32(tl + 128 + q * 32, d7);
+        ld32(tl + q * 32, d7);
         if (i < n) {
           float vv[32], o[32];
 #pragma unroll
@@ -1741,7 +1766,11 @@ __global__ void __launch_bounds__(lt::THREADS, 1)
       a.dbeta[(long)(t0 + tid + 32) * H + h] = dBt[tid + 32];
     }
   }
-  if (tid == 0 && !ok) mbar_wait_bounded(&bars[0], 0, nullptr, nullptr, 0);  // no TMA copy outlives the CTA
+  if (tid == 0 && !ok) {
+    // no TMA copy may outlive the CTA
+    mbar_wait_bounded(&bars[0], 0, nullptr, nullptr, 0);
+    if (dd_issued) mbar_wait_bounded(&bars[6], 0, nullptr, nullptr, 0);
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {

@@ -12,8 +12,9 @@ rank ``j = (i - t) mod c`` and, per sample:
 Partial results are merged with their log-sum-exp. The backward repeats the
 ring with the merged output and LSE (so every step's P is the globally
 normalised probability) and passes each KV block's dK/dV accumulator along
-with it, so after ``c`` hops it arrives back at its owner. The send/receive of
-the next block is issued before the current block's kernels run.
+with it, so after ``c`` hops it arrives back at its owner. In both directions
+the send/receive of the next block is issued before the current block's
+kernels run, so the exchange overlaps the attention kernels.
 
 Reference behaviour: TransformerEngine ``cp_comm_type=p2p`` ring with zigzag
 (``attn_forward_func_with_cp``) as driven by the reference's launcher.
@@ -121,42 +122,51 @@ class _ZigzagRingFn(torch.autograd.Function):
         dout = dout.contiguous()
         dq = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
         kv = torch.stack([k, v]).contiguous()
-        dkv = torch.zeros(kv.shape, dtype=torch.float32, device=q.device)
         sec = ring.second
         q2, o2, do2, lse2 = q.index_select(0, sec), out.index_select(0, sec), dout.index_select(0, sec), \
             lse.index_select(1, sec)
+        # Both exchanges overlap the kernels: the next KV block is requested before this step's
+        # kernels run, and the dK/dV accumulator of the block that arrives next is received while
+        # this step computes its own contribution, which is added when the accumulator lands.
+        acc_req = acc_in = None
         for t in range(ring.c):
+            kv_req = nkv = None
+            if t + 1 < ring.c:
+                nkv = torch.empty_like(kv)
+                kv_req = ring.exchange(kv, nkv)
             kind = ring.step_kind(t)
             kk, vv = kv[0], kv[1]
+            part = torch.zeros(kv.shape, dtype=torch.float32, device=q.device)
             if kind == "diag":
                 a, b, c = attention_backward(q, kk, vv, out, lse, dout, ring.meta_diag, scale)
                 dq += a.float()
-                dkv[0] += b.float()
-                dkv[1] += c.float()
+                part[0] += b.float()
+                part[1] += c.float()
             elif kind == "low":
                 kf, vf = kk.index_select(0, ring.first), vv.index_select(0, ring.first)
                 a, b, c = attention_backward(q, kf, vf, out, lse, dout, ring.meta_low, scale)
                 dq += a.float()
-                dkv[0].index_add_(0, ring.first, b.float())
-                dkv[1].index_add_(0, ring.first, c.float())
+                part[0].index_add_(0, ring.first, b.float())
+                part[1].index_add_(0, ring.first, c.float())
             else:
                 a, b, c = attention_backward(q2, kk, vv, o2, lse2, do2, ring.meta_high, scale)
                 dq.index_add_(0, sec, a.float())
-                dkv[0] += b.float()
-                dkv[1] += c.float()
-            # the KV block moves on (not needed after the last step); its gradient
-            # accumulator follows it and finally returns to the block's owner
-            if t + 1 < ring.c:
-                nkv, ndkv = torch.empty_like(kv), torch.empty_like(dkv)
-                reqs = ring.exchange(kv, nkv) + ring.exchange(dkv, ndkv)
-                for r in reqs:
+                part[0] += b.float()
+                part[1] += c.float()
+            if acc_req is not None:
+                for r in acc_req:
                     r.wait()
-                kv, dkv = nkv, ndkv
-        if ring.c > 1:
-            back = torch.empty_like(dkv)
-            for r in ring.exchange(dkv, back):
-                r.wait()
-            dkv = back
+                part += acc_in
+            # the accumulator follows its KV block around the ring and finally returns to the owner
+            acc_in = torch.empty_like(part)
+            acc_req = ring.exchange(part, acc_in)
+            if kv_req is not None:
+                for r in kv_req:
+                    r.wait()
+                kv = nkv
+        for r in acc_req:
+            r.wait()
+        dkv = acc_in
         return dq.to(q.dtype), dkv[0].to(k.dtype), dkv[1].to(v.dtype), None, None
 
 

@@ -7,9 +7,10 @@ may continue on the next one. Two things cross ranks:
 * conv halo - the 3 tokens before a continuing segment, sent by the previous
   rank (forward) with the matching gradient sent back (backward);
 * recurrent state - the state a continuing sample carries into this rank.
-  Every rank runs its chunk-parallel prep once, then a cheap zero-start state
-  pass giving its tail segment's final state ``F`` and, when one sample spans
-  the whole rank, the tail's transition matrix ``M`` (``S_out = M S_in + F``).
+  Every rank runs a zero-start state pass over its last segment only (the one
+  that continues on the next rank), giving that segment's final state ``F``,
+  and, when one sample spans the whole rank, the tail's transition matrix
+  ``M`` (``S_out = M S_in + F``).
   ``(F, M)`` are all-gathered over the team (differentiable), each rank folds
   the prefix of its chain of predecessors and then runs the real state pass
   from that state. Forward and backward are parallel across the team (no rank
@@ -164,8 +165,19 @@ def delta_rule_cp(ctx, q, k, v, g, beta):
         # tail state from zero, and (for a single continuing segment) the linear
         # map of the incoming state: the recurrence with zero values from I
         # these passes only feed a small state: recomputed in the backward rather than kept
-        _, S_zero = fused_gated_delta_rule(q, k, v, g, beta, layout, keep_intermediates=False)
-        F_tail = S_zero[nseg - 1]
+        n_last = ctx.segment_lengths[-1]
+        if nseg > 1 and n_last >= 64:
+            # only the last segment continues on the next rank: run the tail pass over its rows alone
+            if getattr(ctx, "_tail_layout", None) is None:
+                from ..ops.gdn import ChunkLayout
+                ctx._tail_layout = ChunkLayout((n_last,), q.device)
+            rows = slice(q.shape[0] - n_last, None)
+            _, S_last = fused_gated_delta_rule(q[rows], k[rows], v[rows], g[rows], beta[rows], ctx._tail_layout,
+                                               keep_intermediates=False)
+            F_tail = S_last[0]
+        else:
+            _, S_zero = fused_gated_delta_rule(q, k, v, g, beta, layout, keep_intermediates=False)
+            F_tail = S_zero[nseg - 1]
         if first_cont and single:
             eye = torch.eye(DK, dtype=f32, device=q.device).expand(nseg, H, DK, DK).contiguous()
             _, M_all = fused_gated_delta_rule(q, k, torch.zeros_like(q), g, beta, layout, initial_state=eye,

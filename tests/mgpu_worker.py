@@ -105,8 +105,10 @@ def main():
         assert err < 3e-2, f"peer attention {name} rel err {err}"
 
     # 3. chunkwise GDN CP on the GPU state kernels vs one GPU
-    glen = {0: 2560 * world // 2, 1: 640 * world // 2}
-    gctx = LocalLayout(Layout((Group(ranks, (0, 1)),), "contiguous"), glen, world, rank, dev, teams)
+    # sample 1 spans a rank boundary, so a rank holds a finished sample and a continuing one (the
+    # tail pass then runs over the continuing segment alone)
+    glen = {0: 640 * world // 2, 1: 2560 * world // 2, 2: 640 * world // 2}
+    gctx = LocalLayout(Layout((Group(ranks, (0, 1, 2)),), "contiguous"), glen, world, rank, dev, teams)
     Tg, H, dk, dv = sum(glen.values()), 4, 128, 256
     g2 = torch.Generator(device="cuda").manual_seed(5)
     qq = F.normalize(torch.randn(Tg, H, dk, device=dev, generator=g2), dim=-1)
@@ -115,10 +117,10 @@ def main():
     gg = -torch.rand(Tg, H, device=dev, generator=g2) * 0.2
     bb = torch.rand(Tg, H, device=dev, generator=g2)
     ins = [t.clone().requires_grad_(True) for t in (qq, kk, vv, gg, bb)]
-    ref, _ = chunk_gated_delta_rule(*ins, ChunkLayout((glen[0], glen[1]), dev))
+    ref, _ = chunk_gated_delta_rule(*ins, ChunkLayout((glen[0], glen[1], glen[2]), dev))
     gout = torch.randn_like(ref)
     (ref * gout).sum().backward()
-    rows = rows_of(gctx, {0: 0, 1: glen[0]})
+    rows = rows_of(gctx, {0: 0, 1: glen[0], 2: glen[0] + glen[1]})
     loc = [t[rows].clone().requires_grad_(True) for t in (qq, kk, vv, gg, bb)]
     o = gctx.delta_rule(*loc)
     (o * gout[rows]).sum().backward()
