@@ -29,10 +29,12 @@ from ..ops.gdn import ChunkLayout, chunk_gated_delta_rule, fused_gated_delta_rul
 from ..planner.joint.ir import Layout, spans
 
 
-# "peer": kernels read the team's tiles from symmetric memory over NVLink
-# (layouts whose sequences split into whole 128-token chunks); "ring": NCCL
-# point-to-point ring with LSE merge. Override with PRISM_CP_ATTENTION.
-CP_ATTENTION = {"impl": os.environ.get("PRISM_CP_ATTENTION", "ring")}
+# "peer" (default): the team's K/V (Q/dO in the backward) are staged in symmetric memory, pulled
+# over NVLink by one P2P gather kernel and read by the tcgen05 kernels in global positions; it
+# applies to layouts whose sequences split into whole 128-token chunks (measured 2.3 % faster per
+# 1.3B step than the ring at CP = 2). Other layouts, and "ring", use the NCCL point-to-point ring
+# with LSE merges. Override with PRISM_CP_ATTENTION.
+CP_ATTENTION = {"impl": os.environ.get("PRISM_CP_ATTENTION", "peer")}
 
 
 class LocalLayout:

@@ -255,7 +255,7 @@ def distributed_breakdown(model_name: str, seqs: int, seq_len: int, tokens_per_r
     if rank != 0:
         return None
     return format_breakdown(gathered, dict(model=model_name, seqs=seqs, seq_len=seq_len, world=world,
-                                           impl=os.environ.get("PRISM_CP_ATTENTION", "ring")))
+                                           impl=os.environ.get("PRISM_CP_ATTENTION", "peer")))
 
 
 def format_breakdown(ranks: list, meta: dict) -> str:

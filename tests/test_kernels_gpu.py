@@ -301,6 +301,33 @@ def test_recomputed_layers_on_cuda_match_stored_activations():
     assert ((g0 - g1).norm() / g0.norm()).item() < 1e-2
 
 
+@pytest.mark.parametrize("j", [5, 200, 511])
+def test_cuda_model_is_causal(j):
+    """Changing token j changes no hidden state before position j on the CUDA kernels (GEMMs,
+    conv, fused GDN chunks, flash attention); states from j on do change."""
+    from prism_cp_b200.models.config import HybridConfig
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.parallel.layout import LocalLayout, single_rank_layout
+    cfg = HybridConfig(num_layers=4, hidden_size=256, ffn_hidden_size=512, vocab_size=4096,
+                       num_attention_heads=4, num_query_groups=2, kv_channels=128,
+                       linear_num_key_heads=2, linear_key_head_dim=128, linear_value_head_dim=256)
+    lengths = {0: 640}
+    dev = torch.device(DEV, torch.cuda.current_device())
+    model = HybridModel(cfg, dtype=torch.bfloat16, device=dev, seed=0)
+    lay = LocalLayout(single_rank_layout(lengths), lengths, 1, 0, dev)
+    flat = LocalLayout(single_rank_layout(lengths, "contiguous"), lengths, 1, 0, dev)
+    ctxs = [lay if s == "*" else flat for s in cfg.pattern]
+    tokens = torch.randint(0, cfg.vocab_size, (640,), generator=torch.Generator().manual_seed(4)).to(dev)
+    other = tokens.clone()
+    other[j] = (other[j] + 1) % cfg.vocab_size
+    with torch.no_grad():
+        a = model.run_layers(model.embed(tokens), ctxs)
+        b = model.run_layers(model.embed(other), ctxs)
+    torch.cuda.synchronize()
+    assert torch.equal(a[:j], b[:j]), "a hidden state before the changed token moved"
+    assert not torch.equal(a[j:], b[j:])
+
+
 # ------------------------------------------------------------------ bounded device waits
 def test_a_device_wait_that_runs_out_reports_an_error_and_the_context_survives():
     """A flag nothing sets: the bounded wait gives up after its limit, records an error status the
