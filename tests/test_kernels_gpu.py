@@ -328,6 +328,40 @@ def test_cuda_model_is_causal(j):
     assert not torch.equal(a[j:], b[j:])
 
 
+def test_repeated_random_batch_is_memorised_not_leaked():
+    """The benchmark trains on one synthetic batch of uniform random tokens every step, and its loss
+    falls far below ln(vocab). That is memorisation of the repeated batch, not a view of the future:
+    the same trained model scores an unseen random batch at about ln(vocab)."""
+    import math
+    from prism_cp_b200.models.config import HybridConfig
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.parallel.teams import Teams
+    from prism_cp_b200.planner.fixed import uniform_plan
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.trainer import Trainer
+    cfg = HybridConfig(num_layers=4, hidden_size=256, ffn_hidden_size=512, vocab_size=4096,
+                       num_attention_heads=4, num_query_groups=2, kv_channels=128,
+                       linear_num_key_heads=2, linear_key_head_dim=128, linear_value_head_dim=256)
+    dev = torch.device(DEV, torch.cuda.current_device())
+    model = HybridModel(cfg, dtype=torch.bfloat16, device=dev, seed=0)
+    tr = Trainer(model, Teams(1), dev, lr=3e-3, warmup_steps=0)
+    seen = make_batch([512, 512], cfg.vocab_size, seed=11)
+    unseen = make_batch([512, 512], cfg.vocab_size, seed=12)
+    plan = uniform_plan(seen.lengths, 1, 1, 1024, cfg.pattern)
+    first = tr.train_step(seen, plan).loss
+    for _ in range(40):
+        last = tr.train_step(seen, plan).loss
+    with torch.no_grad():
+        from prism_cp_b200.runtime.executor import MicrobatchRun
+        inputs = tr.prepare(unseen, plan)[0].to(dev)
+        run = MicrobatchRun(plan.microbatches[0], unseen.lengths, tr.cache)
+        held_out, _ = run.forward(model, inputs.tokens, inputs.labels, inputs.weights)
+    ln_v = math.log(cfg.vocab_size)
+    assert abs(first - ln_v) < 1.0
+    assert last < 0.5 * ln_v, (first, last)
+    assert float(held_out) > 0.9 * ln_v, float(held_out)
+
+
 # ------------------------------------------------------------------ bounded device waits
 def test_a_device_wait_that_runs_out_reports_an_error_and_the_context_survives():
     """A flag nothing sets: the bounded wait gives up after its limit, records an error status the
