@@ -25,7 +25,6 @@ from __future__ import annotations
 
 import argparse
 import json
-from dataclasses import replace
 import os
 import statistics
 import subprocess
@@ -146,9 +145,8 @@ def main():
     from prism_cp_b200.models.config import PRESETS
     from prism_cp_b200.models.hybrid import HybridModel
     from prism_cp_b200.parallel.teams import Teams
-    from prism_cp_b200.planner.fixed import uniform_plan
-    from prism_cp_b200.runtime.batch import fixed_lengths, lognormal_lengths, make_batch
     from prism_cp_b200.runtime.trainer import Trainer
+    from prism_cp_b200.runtime.workload import build as build_workload
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -156,35 +154,14 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=600))
     cfg = PRESETS[args.model]()
-    if args.workload == "fixed":
-        lengths = fixed_lengths(args.seqs, args.seq_len)
-        workload = {"global_batch": args.seqs, "seq_len": args.seq_len}
-    else:
-        # multiples of 16 tokens (the zigzag split of CP <= 8) at every N: one batch for the whole scaling curve
-        lengths = lognormal_lengths(args.total_tokens, 4096, 1.0, 512, 131072, 2 * max(world, 8), args.seed)
-        workload = {"global_batch": len(lengths), "global_batch_tokens": sum(lengths), "seq_len": max(lengths),
-                    "lengths": "log-normal median 4096 sigma 1.0 clipped 512..131072"}
-    batch = make_batch(lengths, cfg.vocab_size, args.seed, pin=True)
-    plan_desc = f"cp{world}"
-    predicted_ms = None
-    if args.plan == "online":
-        from prism_cp_b200.planner.calibrate import calibrated
-        from prism_cp_b200.planner.cli import B200_ENVELOPE
-        from prism_cp_b200.planner.joint.cost import model_from_config
-        from prism_cp_b200.planner.online import select
-        pm = calibrated(model_from_config(cfg, B200_ENVELOPE["device_bytes"],
-                                          **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"}))
-        pm = replace(pm, recompute_tokens=args.recompute_tokens or None)
-        try:
-            sel = select(batch.lengths, world, cfg.pattern, pm)
-        except ValueError as err:
-            raise SystemExit(f"--plan online: no (cp_gdn, cp_gqa) plan of this batch fits {world} GPU(s) under "
-                             f"the calibrated memory model ({err}); use more GPUs or shorter documents")
-        plan = sel.plan
-        plan_desc = f"online cp_gdn{sel.cp_gdn} cp_gqa{sel.cp_gqa} over {world}"
-        predicted_ms = sel.predicted_update_ms
-    else:
-        plan = uniform_plan(batch.lengths, world, world, args.tokens_per_rank, cfg.pattern)
+    try:
+        wl = build_workload(cfg, world, args.workload, args.plan, seqs=args.seqs, seq_len=args.seq_len,
+                            tokens_per_rank=args.tokens_per_rank, total_tokens=args.total_tokens, seed=args.seed,
+                            recompute_tokens=args.recompute_tokens or None)
+    except ValueError as err:
+        raise SystemExit(f"--plan {args.plan}: {err}")
+    batch, plan, workload, plan_desc, predicted_ms = wl.batch, wl.plan, wl.description, wl.parallelism, \
+        wl.predicted_ms
 
     model = HybridModel(cfg, dtype=torch.bfloat16, device=device, seed=0)
     teams = Teams(world)

@@ -193,9 +193,10 @@ def _kernels_of(prof):
 
 
 def distributed_breakdown(model_name: str, seqs: int, seq_len: int, tokens_per_rank: int, warmup: int,
-                          timed: int, top: int = 12) -> str | None:
-    """Per-rank category breakdown of one CP = world training step (torchrun ranks, NCCL);
-    returns the markdown report on rank 0, None elsewhere."""
+                          timed: int, top: int = 12, workload: str = "fixed", plan_kind: str = "uniform",
+                          recompute_tokens: int | None = 32768) -> str | None:
+    """Per-rank category breakdown of one training step of a benchmark workload (torchrun ranks,
+    NCCL); returns the markdown report on rank 0, None elsewhere."""
     import datetime
     import torch.distributed as dist
     from torch.profiler import ProfilerActivity, profile
@@ -203,9 +204,8 @@ def distributed_breakdown(model_name: str, seqs: int, seq_len: int, tokens_per_r
     from ..models.config import PRESETS
     from ..models.hybrid import HybridModel
     from ..parallel.teams import Teams
-    from ..planner.fixed import uniform_plan
-    from ..runtime.batch import make_batch
     from ..runtime.trainer import Trainer
+    from ..runtime.workload import build
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -216,9 +216,10 @@ def distributed_breakdown(model_name: str, seqs: int, seq_len: int, tokens_per_r
     rank = dist.get_rank() if world > 1 else 0
     cfg = PRESETS[model_name]()
     model = HybridModel(cfg, dtype=torch.bfloat16, device=dev, seed=0)
-    trainer = Trainer(model, Teams(world), dev)
-    batch = make_batch([seq_len] * seqs, cfg.vocab_size, seed=1, pin=True)
-    plan = uniform_plan(batch.lengths, world, world, tokens_per_rank, cfg.pattern)
+    trainer = Trainer(model, Teams(world), dev, recompute_tokens=recompute_tokens)
+    wl = build(cfg, world, workload, plan_kind, seqs=seqs, seq_len=seq_len, tokens_per_rank=tokens_per_rank,
+               recompute_tokens=recompute_tokens)
+    batch, plan = wl.batch, wl.plan
     inputs = [h.to(dev) for h in trainer.prepare(batch, plan)]
     for _ in range(warmup):
         trainer.train_step(batch, plan, inputs, read_loss=False)
@@ -254,14 +255,16 @@ def distributed_breakdown(model_name: str, seqs: int, seq_len: int, tokens_per_r
         gathered = [summary]
     if rank != 0:
         return None
-    return format_breakdown(gathered, dict(model=model_name, seqs=seqs, seq_len=seq_len, world=world,
-                                           impl=os.environ.get("PRISM_CP_ATTENTION", "peer")))
+    return format_breakdown(gathered, dict(model=model_name, seqs=len(batch.lengths), seq_len=max(batch.lengths),
+                                           world=world, impl=os.environ.get("PRISM_CP_ATTENTION", "peer"),
+                                           plan=wl.parallelism, workload=workload))
 
 
 def format_breakdown(ranks: list, meta: dict) -> str:
     cats = sorted({c for r in ranks for c in r["categories"]})
-    lines = [f"step breakdown: {meta['model']}, {meta['seqs']} x {meta['seq_len']} tokens, CP = {meta['world']} "
-             f"on {meta['world']} GPU(s), CP attention {meta['impl']}",
+    lines = [f"step breakdown: {meta['model']}, {meta.get('workload', 'fixed')} workload, {meta['seqs']} documents "
+             f"(longest {meta['seq_len']} tokens), plan {meta.get('plan', 'cp%d' % meta['world'])} on "
+             f"{meta['world']} GPU(s), CP attention {meta['impl']} where the layout allows it",
              f"device step time (CUDA events, max over ranks): {ranks[0]['step_ms']:.1f} ms", "",
              "| rank | span ms | busy ms | idle ms | comm not under compute ms | " + " | ".join(cats) + " |",
              "|" + "---|" * (5 + len(cats))]
@@ -287,10 +290,13 @@ def main(argv=None) -> int:
                     help="CP = world over torchrun ranks: per-rank categories, exposed communication, idle time")
     ap.add_argument("--tokens-per-rank", type=int, default=32768)
     ap.add_argument("--timed", type=int, default=2)
+    ap.add_argument("--workload", choices=("fixed", "lognormal"), default="fixed",
+                    help="with --distributed: the benchmark workload to break down")
+    ap.add_argument("--plan", choices=("uniform", "online"), default="uniform")
     args = ap.parse_args(argv)
     if args.distributed:
         report = distributed_breakdown(args.model, args.seqs, args.seq_len, args.tokens_per_rank, args.warmup,
-                                       args.timed)
+                                       args.timed, workload=args.workload, plan_kind=args.plan)
         if report is not None:
             if args.output:
                 with open(args.output, "w") as f:

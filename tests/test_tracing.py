@@ -77,5 +77,5 @@ def test_timeline_summary_separates_hidden_and_exposed_communication():
     assert tracing.categorize("void prism::attnb::attn_bwd_kv_kernel<prism::NoPeers>") == "attention"
     assert tracing.categorize("prism::gdnc::gdn_bwd_local_kernel") == "gdn"
     text = tracing.format_breakdown([dict(s, top=[("gemm", 10.0)])],
-                                    dict(model="m", seqs=1, seq_len=8, world=1, impl="ring"))
+                                    dict(model="m", seqs=1, seq_len=8, world=1, impl="ring", plan="cp1", workload="fixed"))
     assert "| 0 | 22.0 | 17.0 | 5.0 | 7.0 |" in text
