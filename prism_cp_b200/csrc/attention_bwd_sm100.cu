@@ -55,6 +55,7 @@ __device__ __forceinline__ void write_chunk_sw128(uint8_t* base, int row, int ch
 }
 
 __device__ __forceinline__ void named_sync_compute() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void named_sync_kv() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // K-major operand (rows x 128 dims as two 64-dim boxes); k = 16-element step.
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t base, int k) {
@@ -75,6 +76,12 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int k) {
 // Src = PeerTiles: this rank's keys of a zigzag team; tiles hold (seq, global
 // position of the first key, its local row); Q / dO tiles and their LSE / D rows
 // are read from the rank that owns each query tile.
+// The dK/dV kernel runs eight compute warps: warps w and w + 4 share TMEM lanes (key rows) 32(w % 4)..
+// and split the 64 query columns of each iteration, so every SM sub-partition has two warps of
+// P^T / dS^T math to interleave (the math, not the tensor cores, bounds an iteration). Warp 8 is the
+// TMA producer, warp 9 issues the MMAs.
+constexpr int KV_THREADS = 320;
+constexpr int KV_COMPUTE = 256;
 constexpr int KV_QT = 64;                    // query rows per iteration
 constexpr int KV_QBYTES = KV_QT * D * 2;     // 16 KiB: 64 rows x 128 dims (two 64-dim boxes)
 constexpr int KV_QHALF = KV_QBYTES / 2;
@@ -87,7 +94,7 @@ constexpr int KV_OFF_STAT = KV_OFF_DST + KV_PBYTES;      // lse[2][64], dsum[2][
 constexpr int KV_OFF_BAR = KV_OFF_STAT + 4 * KV_QT * 4;
 
 template <class Src>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(KV_THREADS, 1)
     attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                        Params p, const __grid_constant__ Src src) {
@@ -141,15 +148,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&q_full[b], 1);
       mbar_init(&q_empty[b], 1);
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], 128);
+      mbar_init(&s_free[b], KV_COMPUTE);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, KV_COMPUTE);
     mbar_init(mma_done, 1);
     mbar_init(acc_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -158,7 +165,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------------------------------------------------------- producer
     if (lane == 0 && n_it > 0) {
       mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
@@ -196,7 +203,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int it = issued > 2 ? issued - 2 : 0; it < issued; ++it)
         mbar_wait_bounded(&q_full[it & 1], (it >> 1) & 1, nullptr, nullptr, 0);
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0 && n_it > 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(128, KV_QT, 0, 0);   // K/V K-major x Q/dO K-major
@@ -247,9 +254,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ---------------------------------------------------------------- P^T / dS^T rows
-    const int r = threadIdx.x;  // key row == TMEM lane
+    const int r = threadIdx.x & 127;   // key row == TMEM lane
+    const int half = threadIdx.x >> 7; // which 32 of the 64 query columns
     const int kk = k0 + r;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const float c_log2 = p.scale * kLog2e;
     const bool row_ok = kk < k_len;
     bool ok = true;
@@ -258,7 +266,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int h = kv_head * rep + it / per_head;
       const int i = i_start + it % per_head;
       const int q0 = i * KV_QT;
-      if (r < KV_QT) {
+      if (half == 0 && r < KV_QT) {
         const int qq = q0 + r;
         const bool v = qq < q_len;
         const float* lse_src = p.lse;
@@ -273,39 +281,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         lse_s[b * KV_QT + r] = v ? lse_src[(long)h * p.tq + row] * kLog2e : INFINITY;
         dsum_s[b * KV_QT + r] = v ? dsum_src[(long)h * p.tq + row] : 0.f;
       }
-      named_sync_compute();
+      named_sync_kv();
       ok = named_barrier_and(mbar_wait_bounded(&s_full[b], (it >> 1) & 1, abort_flag, p.status, kTimeoutEpilogue),
-                             1, 128);
+                             1, KV_COMPUTE);
       if (!ok) break;
       tc_fence_after();
-      uint32_t s_raw[64], dp_raw[64];
-      tmem_ld_32x32b_x32(lane_base + b * KV_QT, *reinterpret_cast<uint32_t(*)[32]>(s_raw));
-      tmem_ld_32x32b_x32(lane_base + b * KV_QT + 32, *reinterpret_cast<uint32_t(*)[32]>(s_raw + 32));
-      tmem_ld_32x32b_x32(lane_base + 128 + b * KV_QT, *reinterpret_cast<uint32_t(*)[32]>(dp_raw));
-      tmem_ld_32x32b_x32(lane_base + 128 + b * KV_QT + 32, *reinterpret_cast<uint32_t(*)[32]>(dp_raw + 32));
+      const int col0 = half * 32;
+      uint32_t s_raw[32], dp_raw[32];
+      tmem_ld_32x32b_x32(lane_base + b * KV_QT + col0, s_raw);
+      tmem_ld_32x32b_x32(lane_base + 128 + b * KV_QT + col0, dp_raw);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[b]);
       // P^T and dS^T overwrite the loaded S^T / dP^T values in place (keeps register use flat)
 #pragma unroll
-      for (int e = 0; e < KV_QT; ++e) {
-        const int qq = q0 + e;
+      for (int e = 0; e < 32; ++e) {
+        const int qq = q0 + col0 + e;
         const bool valid = row_ok && qq < q_len && (!p.causal || kk <= qq);
-        const float pe = valid ? exp2f(__uint_as_float(s_raw[e]) * c_log2 - lse_s[b * KV_QT + e]) : 0.f;
+        const float pe = valid ? exp2f(__uint_as_float(s_raw[e]) * c_log2 - lse_s[b * KV_QT + col0 + e]) : 0.f;
         s_raw[e] = __float_as_uint(pe);
-        dp_raw[e] = __float_as_uint(pe * (__uint_as_float(dp_raw[e]) - dsum_s[b * KV_QT + e]));
+        dp_raw[e] = __float_as_uint(pe * (__uint_as_float(dp_raw[e]) - dsum_s[b * KV_QT + col0 + e]));
       }
       const float* pv = reinterpret_cast<const float*>(s_raw);
       const float* dsv = reinterpret_cast<const float*>(dp_raw);
       // P^T / dS^T of the previous query tile must have been consumed
       if (it > 0) {
         ok = named_barrier_and(mbar_wait_bounded(mma_done, (it - 1) & 1, abort_flag, p.status, kTimeoutEpilogue),
-                               1, 128);
+                               1, KV_COMPUTE);
         if (!ok) break;
       }
 #pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        const int off = r * 128 + ((g ^ (r & 7)) << 4);
+      for (int g = 0; g < 4; ++g) {
+        const int off = r * 128 + (((half * 4 + g) ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(sPT + off) =
             make_uint4(pack_bf16x2(pv[8 * g], pv[8 * g + 1]), pack_bf16x2(pv[8 * g + 2], pv[8 * g + 3]),
                        pack_bf16x2(pv[8 * g + 4], pv[8 * g + 5]), pack_bf16x2(pv[8 * g + 6], pv[8 * g + 7]));
@@ -327,7 +334,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __nv_bfloat16* dv_row = p.out2 + (long)(k_seg + kk) * p.out_stride + (long)kv_head * D;
       __nv_bfloat16* dk_row = p.out + (long)(k_seg + kk) * p.out_stride + (long)kv_head * D;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 2 * half; c < 2 * half + 2; ++c) {  // each half of the compute warps stores 64 columns
         uint32_t a[32], bb[32];
         if (loaded) {
           tmem_ld_32x32b_x32(lane_base + 256 + c * 32, a);
@@ -356,15 +363,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
 }
 
 // ------------------------------------------------------------------ dQ
+// Eight compute warps as in the dK/dV kernel (warps w and w + 4 split the 128 key columns of a tile),
+// warp 8 the TMA producer, warp 9 the MMA issuer. The compute warps release S / dP as soon as they
+// are in registers, so S and dP of the next key tile are computed while dS of this one is formed.
+constexpr int Q_THREADS = 320;
+constexpr int Q_COMPUTE = 256;
+
 template <class Src>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(Q_THREADS, 1)
     attn_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, Params p,
                       const __grid_constant__ Src src) {
@@ -383,8 +396,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* s_full = bars + 5;
   uint64_t* ds_full = bars + 6;
   uint64_t* acc_done = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 9);
+  uint64_t* s_free = bars + 8;    // S / dP of the current tile are in the compute warps' registers
+  uint64_t* ds_free = bars + 9;   // the dQ product has read the dS tile
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 11);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y;
@@ -414,12 +429,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&kv_empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(ds_full, 128);
+    mbar_init(ds_full, Q_COMPUTE);
     mbar_init(acc_done, 1);
+    mbar_init(s_free, Q_COMPUTE);
+    mbar_init(ds_free, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -428,7 +445,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0 && n_kv > 0) {
       mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
       tma_load_3d(sQ, &tmQ, q_full, 0, head, q_seg + q0);
@@ -456,38 +473,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tma_load_3d(vd + HALF, mv, &kv_full[s], 64, kv_head, krow);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0 && n_kv > 0) {
       constexpr uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t idesc_km = make_idesc_bf16(128, 128, 0, 1);
       const uint32_t aQ = smem_u32(sQ), adO = smem_u32(sdO), adS = smem_u32(sdS);
       bool ok = mbar_wait_bounded(q_full, 0, abort_flag, p.status, kTimeoutMma);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait_bounded(&kv_full[s], (j >> 1) & 1, abort_flag, p.status, kTimeoutMma)) break;
-        tc_fence_after();
-        const uint32_t aK = smem_u32(sK + s * TILE_BYTES), aV = smem_u32(sV + s * TILE_BYTES);
+      // step j issues S_j, dP_j (once the compute warps hold S_{j-1}, dP_{j-1} in registers), then
+      // dQ += dS_{j-1} K_{j-1}
+      for (int j = 0; ok && j <= n_kv; ++j) {
+        if (j < n_kv) {
+          const int s = j & 1;
+          if (!mbar_wait_bounded(&kv_full[s], (j >> 1) & 1, abort_flag, p.status, kTimeoutMma)) break;
+          if (j >= 1 && !mbar_wait_bounded(s_free, (j - 1) & 1, abort_flag, p.status, kTimeoutMma)) break;
+          tc_fence_after();
+          const uint32_t aK = smem_u32(sK + s * TILE_BYTES), aV = smem_u32(sV + s * TILE_BYTES);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_bf16_ss(tmem + 0, desc_kmajor(aQ, k), desc_kmajor(aK, k), idesc_kk, k > 0);
+          for (int k = 0; k < 8; ++k)
+            umma_bf16_ss(tmem + 0, desc_kmajor(aQ, k), desc_kmajor(aK, k), idesc_kk, k > 0);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_bf16_ss(tmem + 128, desc_kmajor(adO, k), desc_kmajor(aV, k), idesc_kk, k > 0);
-        umma_commit(s_full);
-        if (!mbar_wait_bounded(ds_full, j & 1, abort_flag, p.status, kTimeoutMma)) break;
-        tc_fence_after();
+          for (int k = 0; k < 8; ++k)
+            umma_bf16_ss(tmem + 128, desc_kmajor(adO, k), desc_kmajor(aV, k), idesc_kk, k > 0);
+          umma_commit(s_full);
+        }
+        if (j >= 1) {
+          const int jt = j - 1, s = jt & 1;
+          if (!mbar_wait_bounded(ds_full, jt & 1, abort_flag, p.status, kTimeoutMma)) break;
+          tc_fence_after();
+          const uint32_t aK = smem_u32(sK + s * TILE_BYTES);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_bf16_ss(tmem + 256, desc_kmajor(adS, k), desc_mnmajor(aK, k), idesc_km, (j > 0 || k > 0));
-        umma_commit(&kv_empty[s]);
+          for (int k = 0; k < 8; ++k)
+            umma_bf16_ss(tmem + 256, desc_kmajor(adS, k), desc_mnmajor(aK, k), idesc_km, (jt > 0 || k > 0));
+          umma_commit(&kv_empty[s]);
+          umma_commit(ds_free);
+        }
       }
       umma_commit(acc_done);
     }
   } else {
-    const int r = threadIdx.x;
+    const int r = threadIdx.x & 127;
+    const int half = threadIdx.x >> 7;   // which 64 of the tile's 128 key columns
     const int qq = q0 + r;
     const bool row_ok = qq < q_len;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const float c_log2 = p.scale * kLog2e;
     const float lse2 = row_ok ? p.lse[(long)head * p.tq + q_seg + qq] * kLog2e : INFINITY;
     const float dsum = row_ok ? p.dsum[(long)head * p.tq + q_seg + qq] : 0.f;
@@ -496,29 +524,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(s_full, j & 1, abort_flag, p.status, kTimeoutEpilogue));
       if (!ok) break;
       tc_fence_after();
-      const int kbase = j * TILE;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t s_raw[32], dp_raw[32];
-        tmem_ld_32x32b_x32(lane_base + c * 32, s_raw);
-        tmem_ld_32x32b_x32(lane_base + 128 + c * 32, dp_raw);
-        tmem_wait_ld();
-        float dsv[32];
+      const int col0 = half * 64;
+      uint32_t s_raw[64], dp_raw[64];
+      tmem_ld_32x32b_x32(lane_base + col0, *reinterpret_cast<uint32_t(*)[32]>(s_raw));
+      tmem_ld_32x32b_x32(lane_base + col0 + 32, *reinterpret_cast<uint32_t(*)[32]>(s_raw + 32));
+      tmem_ld_32x32b_x32(lane_base + 128 + col0, *reinterpret_cast<uint32_t(*)[32]>(dp_raw));
+      tmem_ld_32x32b_x32(lane_base + 128 + col0 + 32, *reinterpret_cast<uint32_t(*)[32]>(dp_raw + 32));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(s_free);
+      const int kbase = j * TILE + col0;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int kk = kbase + c * 32 + e;
-          const bool valid = row_ok && kk < k_len && (!p.causal || kk <= qq);
-          const float pe = valid ? exp2f(__uint_as_float(s_raw[e]) * c_log2 - lse2) : 0.f;
-          dsv[e] = pe * (__uint_as_float(dp_raw[e]) - dsum);
-        }
-#pragma unroll
-        for (int g = 0; g < 4; ++g)
-          write_chunk_sw128(sdS, r, c * 4 + g,
-                            make_uint4(pack_bf16x2(dsv[8 * g], dsv[8 * g + 1]),
-                                       pack_bf16x2(dsv[8 * g + 2], dsv[8 * g + 3]),
-                                       pack_bf16x2(dsv[8 * g + 4], dsv[8 * g + 5]),
-                                       pack_bf16x2(dsv[8 * g + 6], dsv[8 * g + 7])));
+      for (int e = 0; e < 64; ++e) {
+        const int kk = kbase + e;
+        const bool valid = row_ok && kk < k_len && (!p.causal || kk <= qq);
+        const float pe = valid ? exp2f(__uint_as_float(s_raw[e]) * c_log2 - lse2) : 0.f;
+        dp_raw[e] = __float_as_uint(pe * (__uint_as_float(dp_raw[e]) - dsum));
       }
+      const float* dsv = reinterpret_cast<const float*>(dp_raw);
+      // the dQ product of the previous tile must have read the dS tile before it is rewritten
+      if (j >= 1) {
+        ok = named_barrier_and(mbar_wait_bounded(ds_free, (j - 1) & 1, abort_flag, p.status, kTimeoutEpilogue),
+                               1, Q_COMPUTE);
+        if (!ok) break;
+      }
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        write_chunk_sw128(sdS, r, half * 8 + g,
+                          make_uint4(pack_bf16x2(dsv[8 * g], dsv[8 * g + 1]),
+                                     pack_bf16x2(dsv[8 * g + 2], dsv[8 * g + 3]),
+                                     pack_bf16x2(dsv[8 * g + 4], dsv[8 * g + 5]),
+                                     pack_bf16x2(dsv[8 * g + 6], dsv[8 * g + 7])));
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       mbar_arrive(ds_full);
@@ -530,7 +566,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool loaded = __all_sync(0xffffffffu, n_kv > 0 && ok);
       __nv_bfloat16* dq_row = p.out + (long)(q_seg + qq) * p.out_stride + (long)head * D;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 2 * half; c < 2 * half + 2; ++c) {  // each half of the compute warps stores 64 columns
         uint32_t a[32];
         if (loaded) {
           tmem_ld_32x32b_x32(lane_base + 256 + c * 32, a);
@@ -552,7 +588,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -581,6 +617,7 @@ __global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ dO, long d
 
 constexpr int SMEM_KV = KV_OFF_BAR + 256 + 1024;
 constexpr int SMEM_Q = 7 * TILE_BYTES + 256 + 1024;
+static_assert(12 * 8 <= 256, "dQ barriers fit their shared-memory slot");
 
 }  // namespace attnb
 
@@ -631,7 +668,7 @@ void attention_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Ten
     pk.out = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
     pk.out2 = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
     pk.out_stride = dk.stride(0);
-    attn_bwd_kv_kernel<NoPeers><<<dim3(tiles_k.size(0), hkv), NUM_THREADS, SMEM_KV, stream>>>(tq64, tk, tv, tdo64,
+    attn_bwd_kv_kernel<NoPeers><<<dim3(tiles_k.size(0), hkv), KV_THREADS, SMEM_KV, stream>>>(tq64, tk, tv, tdo64,
                                                                                              pk, NoPeers{0});
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
@@ -641,7 +678,7 @@ void attention_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Ten
     pq.out = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
     pq.out2 = nullptr;
     pq.out_stride = dq.stride(0);
-    attn_bwd_q_kernel<NoPeers><<<dim3(tiles_q.size(0), hq), NUM_THREADS, SMEM_Q, stream>>>(tq, tk, tv, tdo, pq,
+    attn_bwd_q_kernel<NoPeers><<<dim3(tiles_q.size(0), hq), Q_THREADS, SMEM_Q, stream>>>(tq, tk, tv, tdo, pq,
                                                                                           NoPeers{0});
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
@@ -708,14 +745,14 @@ void attention_bwd_peer(const std::vector<at::Tensor>& q_peers, const std::vecto
   pk.out2 = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
   pk.out_stride = dk.stride(0);
   CUtensorMap tq64 = make_head_map(q, KV_QT), tdo64 = make_head_map(do_peers[rank], KV_QT);
-  attn_bwd_kv_kernel<PeerTiles><<<dim3(ntiles, hkv), NUM_THREADS, SMEM_KV, stream>>>(tq64, tk, tv, tdo64, pk,
+  attn_bwd_kv_kernel<PeerTiles><<<dim3(ntiles, hkv), KV_THREADS, SMEM_KV, stream>>>(tq64, tk, tv, tdo64, pk,
                                                                                      kv_src);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   Params pq = p;
   pq.out = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
   pq.out2 = nullptr;
   pq.out_stride = dq.stride(0);
-  attn_bwd_q_kernel<PeerTiles><<<dim3(ntiles, hq), NUM_THREADS, SMEM_Q, stream>>>(tq, tk, tv, tdo, pq, q_src);
+  attn_bwd_q_kernel<PeerTiles><<<dim3(ntiles, hq), Q_THREADS, SMEM_Q, stream>>>(tq, tk, tv, tdo, pq, q_src);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
