@@ -521,7 +521,8 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
     const float dsum = row_ok ? p.dsum[(long)head * p.tq + q_seg + qq] : 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv && ok; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait_bounded(s_full, j & 1, abort_flag, p.status, kTimeoutEpilogue));
+      // decided jointly by all 256 compute threads, so both halves of a row take the same path
+      ok = named_barrier_and(mbar_wait_bounded(s_full, j & 1, abort_flag, p.status, kTimeoutEpilogue), 1, Q_COMPUTE);
       if (!ok) break;
       tc_fence_after();
       const int col0 = half * 64;

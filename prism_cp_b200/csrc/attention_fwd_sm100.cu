@@ -35,7 +35,12 @@ constexpr int BQ = 128;
 constexpr int BKV = 128;
 constexpr int KV_STAGES = 2;
 constexpr int TILE_BYTES = 128 * D * 2;  // 32 KiB: 128 rows x 128 dims (two 64-dim boxes)
-constexpr int NUM_THREADS = 192;
+// Eight softmax warps: warps w and w + 4 share TMEM lanes (query rows) 32(w % 4).. and split each
+// 128-key tile into two 64-column halves, exchanging their row maxima through shared memory, so
+// every SM sub-partition interleaves two warps of exponentials. Warp 8 is the TMA producer, warp 9
+// allocates TMEM and issues the MMAs.
+constexpr int NUM_THREADS = 320;
+constexpr int SOFTMAX_THREADS = 256;
 constexpr int TMEM_COLS = 512;
 constexpr int TMEM_O = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -45,7 +50,8 @@ constexpr int SMEM_K = SMEM_Q + TILE_BYTES;
 constexpr int SMEM_V = SMEM_K + KV_STAGES * TILE_BYTES;
 constexpr int SMEM_P = SMEM_V + KV_STAGES * TILE_BYTES;
 constexpr int SMEM_BAR = SMEM_P + TILE_BYTES;
-constexpr int SMEM_BYTES = SMEM_BAR + 256 + 1024;
+constexpr int SMEM_XMAX = SMEM_BAR + 256;              // [3 buffers][2 halves][128 rows] fp32
+constexpr int SMEM_BYTES = SMEM_XMAX + 3 * 2 * BQ * 4 + 1024;
 
 struct FwdParams {
   const int* cu_q;      // [nseq+1]
@@ -119,14 +125,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 128);
+      mbar_init(&s_free[s], SOFTMAX_THREADS);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, SOFTMAX_THREADS);
     mbar_init(pv_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
@@ -135,7 +141,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------------------------------------------------------- producer
     if (lane == 0 && n_kv > 0) {
       tma_prefetch_desc(&tmQ);
@@ -166,7 +172,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tma_load_3d(vd + TILE_BYTES / 2, mv, &kv_full[s], 64, kv_head, krow);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0 && n_kv > 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);  // Q,K both K-major (dim contiguous)
@@ -211,44 +217,62 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ---------------------------------------------------------------- softmax
-    const int r = threadIdx.x;  // 0..127 == TMEM lane
-    const int q_idx = q0 + r;   // within sequence
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-    float m = -INFINITY;  // running max in log2 units
-    float l = 0.f;
+    const int r = threadIdx.x & 127;  // 0..127 == TMEM lane
+    const int half = threadIdx.x >> 7;
+    const int col0 = half * 64;       // this thread's 64 keys of each tile
+    const int q_idx = q0 + r;         // within sequence
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    float* xmax = reinterpret_cast<float*>(smem + SMEM_XMAX);  // [buffer][half][row]
+    float m = -INFINITY;  // running max in log2 units (identical in both halves of a row)
+    float l = 0.f;        // this half's share of the row sum
     uint8_t* p_base = smem + SMEM_P;
     bool ok = true;
     for (int j = 0; j < n_kv && ok; ++j) {
       const int s = j & 1;
       const uint32_t ph = (j >> 1) & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[s], ph, abort_flag, p.status, kTimeoutEpilogue));
-      if (!ok) break;
-      tc_fence_after();
-      float sv[128];
+      // every wait is decided per warp, then jointly by all 256 softmax threads at the one named
+      // barrier of the iteration, so both halves of a row always take the same path
+      const bool got = __all_sync(0xffffffffu,
+                                  mbar_wait_bounded(&s_full[s], ph, abort_flag, p.status, kTimeoutEpilogue));
+      float sv[64];
+      if (got) {
+        tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t raw[32];
-        tmem_ld_32x32b_x32(lane_base + s * 128 + c * 32, raw);
-        tmem_wait_ld();
+        for (int c = 0; c < 2; ++c) {
+          uint32_t raw[32];
+          tmem_ld_32x32b_x32(lane_base + s * 128 + col0 + c * 32, raw);
+          tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(raw[e]) * p.scale_log2;
+          for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(raw[e]) * p.scale_log2;
+        }
+        tc_fence_before();
+        mbar_arrive(&s_free[s]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) sv[e] = -INFINITY;
       }
-      tc_fence_before();
-      mbar_arrive(&s_free[s]);
       // masking
-      const int k_base = j * BKV;
-      const bool need_mask = (k_base + BKV > k_len) || (p.causal && k_base + BKV - 1 > q0) || (q_idx >= q_len);
+      const int k_base = j * BKV + col0;
+      const bool need_mask = (k_base + 64 > k_len) || (p.causal && k_base + 63 > q0) || (q_idx >= q_len);
       if (need_mask) {
 #pragma unroll
-        for (int e = 0; e < 128; ++e) {
+        for (int e = 0; e < 64; ++e) {
           const int kk = k_base + e;
           const bool valid = kk < k_len && q_idx < q_len && (!p.causal || kk <= q_idx);
           if (!valid) sv[e] = -INFINITY;
         }
       }
-      float tmax = sv[0];
+      float hmax = sv[0];
 #pragma unroll
-      for (int e = 1; e < 128; ++e) tmax = fmaxf(tmax, sv[e]);
+      for (int e = 1; e < 64; ++e) hmax = fmaxf(hmax, sv[e]);
+      // P_j may only be written after PV_{j-1} finished reading P_{j-1}
+      const bool pv_ok = j == 0 || __all_sync(0xffffffffu, mbar_wait_bounded(pv_done, (j - 1) & 1, abort_flag,
+                                                                              p.status, kTimeoutEpilogue));
+      // the row maximum over both halves (a double buffer: a half can be one tile ahead)
+      xmax[(s * 2 + half) * BQ + r] = hmax;
+      ok = named_barrier_and(got && pv_ok, 1, SOFTMAX_THREADS);
+      if (!ok) break;
+      const float tmax = fmaxf(hmax, xmax[(s * 2 + (half ^ 1)) * BQ + r]);
       float alpha = 1.f;
       if (tmax > m + kRescaleThreshold || (m == -INFINITY && tmax > -INFINITY)) {
         const float m_new = fmaxf(tmax, m);
@@ -257,28 +281,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       const float mm = (m == -INFINITY) ? 0.f : m;
       float rowsum = 0.f;
-      // P_j may only be written after PV_{j-1} finished reading P_{j-1}
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait_bounded(pv_done, (j - 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
-        if (!ok) break;
-      }
       // tcgen05.ld/st are warp-collective (.sync.aligned): the rescale runs for the whole warp
-      // whenever any of its rows needs it (rows that do not multiply by alpha = 1)
+      // whenever any of its rows needs it (rows that do not multiply by alpha = 1); each half
+      // rescales its own 64 of the 128 output columns
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t raw[32];
-          tmem_ld_32x32b_x32(lane_base + TMEM_O + c * 32, raw);
+          tmem_ld_32x32b_x32(lane_base + TMEM_O + col0 + c * 32, raw);
           tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * alpha);
-          tmem_st_32x32b_x32(lane_base + TMEM_O + c * 32, raw);
+          tmem_st_32x32b_x32(lane_base + TMEM_O + col0 + c * 32, raw);
         }
         tmem_wait_st();
       }
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c = 0; c < 8; ++c) {
         float pe[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -287,14 +307,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         const uint4 packed = make_uint4(pack_bf16x2(pe[0], pe[1]), pack_bf16x2(pe[2], pe[3]),
                                         pack_bf16x2(pe[4], pe[5]), pack_bf16x2(pe[6], pe[7]));
-        write_p_chunk(p_base, r, c, packed);
+        write_p_chunk(p_base, r, half * 8 + c, packed);
       }
       l = l * alpha + rowsum;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    // epilogue
+    // epilogue: the row sum is the two halves' shares (its own buffer: the other half may still be
+    // reading the last tile's maxima)
+    xmax[(4 + half) * BQ + r] = l;
+    ok = named_barrier_and(ok, 1, SOFTMAX_THREADS);
+    l += xmax[(4 + (half ^ 1)) * BQ + r];
     if (ok && n_kv > 0) ok = mbar_wait_bounded(pv_done, (n_kv - 1) & 1, abort_flag, p.status, kTimeoutEpilogue);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
@@ -302,7 +326,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
     __nv_bfloat16* orow = p.out + (long)(q_seg + q_idx) * p.out_stride + (long)head * D;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 2 * half; c < 2 * half + 2; ++c) {
       uint32_t raw[32];
       if (n_kv > 0 && ok) {
         tmem_ld_32x32b_x32(lane_base + TMEM_O + c * 32, raw);
@@ -323,7 +347,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
-    if (row_valid) {
+    if (row_valid && half == 0) {
       const float lse = (l > 0.f) ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
       p.lse[(long)head * p.tq + q_seg + q_idx] = lse;
     }
@@ -331,7 +355,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
