@@ -90,6 +90,7 @@ def plan_for(args, batch, world: int, pattern: str, step: int, replays):
         sel = select(batch.lengths, world, pattern, _planner_model(args, world))
         if int(os.environ.get("RANK", "0")) == 0 and (step == 1 or step % max(1, args.log_interval) == 0):
             print(json.dumps({"step": step, "online_cp": {"gdn": sel.cp_gdn, "gqa": sel.cp_gqa},
+                              "plan": sel.description,
                               "predicted_update_ms": round(sel.predicted_update_ms, 3)}), flush=True)
         return sel.plan
     if args.sequence_packing_scheduler == "fixed":

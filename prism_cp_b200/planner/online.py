@@ -16,6 +16,11 @@ response profile). Candidates:
   ``Model.recompute_tokens`` set, such a document may instead run alone in a
   microbatch that recomputes every layer in the backward, priced as such.
 
+* dynamic plans: the CP degree chosen per document by the dynamic-CP
+  scheduler at a few per-rank capacities (teams of different sizes side by
+  side in one microbatch, short documents on CP1 ranks), kept when the model
+  predicts them faster than every uniform pair.
+
 The selection is deterministic (same lengths -> same plan on every rank), costs
 milliseconds of CPU per batch, and returns the plan with its predicted update
 time and the degree pair, so the executor can apply it without touching
@@ -34,10 +39,17 @@ from .joint.ir import Group, Layout, Microbatch, Plan, validate_plan
 @dataclass(frozen=True)
 class Selection:
     plan: Plan
-    cp_gdn: int
+    cp_gdn: int          # 0 for a dynamic plan (CP chosen per document)
     cp_gqa: int
     predicted_update_ms: float
     candidates: tuple
+    dynamic_capacity: int | None = None   # per-rank token capacity of a dynamic plan
+
+    @property
+    def description(self) -> str:
+        if self.dynamic_capacity is not None:
+            return f"dynamic CP per document (K = {self.dynamic_capacity})"
+        return f"cp_gdn{self.cp_gdn} cp_gqa{self.cp_gqa}"
 
 
 def _pack(lengths: dict, order, capacity_tokens: int, groups: int):
@@ -120,10 +132,47 @@ def candidate_plan(lengths: dict, world: int, pattern: str, cp_gdn: int, cp_gqa:
     return plan
 
 
+def dynamic_candidates(lengths: dict, world: int, pattern: str, model: Model,
+                       capacities=(16384, 24576, 32768)) -> list[tuple]:
+    """Plans with the CP degree chosen per document (the dynamic-CP scheduler at per-rank token
+    capacity K: a document gets the smallest dyadic team that holds it, short documents share CP1
+    ranks, teams of different sizes run side by side in one microbatch), as
+    ``(predicted ms, K, plan, rows)`` of the candidates that fit."""
+    from .studies import native_joint_plan
+    ev = Evaluator(model, lengths, world, pattern)
+    out = []
+    for cap in capacities:
+        if model.recompute_tokens is not None and cap > model.recompute_tokens:
+            continue
+        try:
+            plan = native_joint_plan(lengths, world, pattern, cap)
+        except ValueError:
+            continue
+        evid = [ev.evaluate(mb) for mb in plan.microbatches]
+        if all(e["fits"] for e in evid):
+            ms = sum(e["predicted_ms"] for e in evid) + model.update_ms
+            out.append((ms, cap, plan, {"dynamic_capacity": cap, "fits": True, "predicted_update_ms": ms,
+                                        "microbatches": len(plan.microbatches)}))
+    return out
+
+
 def select(lengths: dict, world: int, pattern: str, model: Model, degrees=(1, 2, 4, 8),
-           capacity: int | None = None) -> Selection:
-    """Best (cp_gdn, cp_gqa) plan for this batch under ``model``."""
+           capacity: int | None = None, dynamic: bool = True) -> Selection:
+    """Best plan for this batch under ``model``: a (cp_gdn, cp_gqa) pair for all documents, or
+    (with ``dynamic``) a per-document CP plan when the model predicts it faster."""
     degrees = tuple(d for d in degrees if d <= world and world % d == 0)
+    if dynamic and world > 1:
+        try:
+            uniform = select(lengths, world, pattern, model, degrees, capacity, dynamic=False)
+        except ValueError:
+            uniform = None
+        best = min(dynamic_candidates(lengths, world, pattern, model), default=None, key=lambda c: (c[0], c[1]))
+        if best is not None and (uniform is None or best[0] < uniform.predicted_update_ms):
+            rows = (uniform.candidates if uniform is not None else ()) + (best[3],)
+            return Selection(best[2], 0, 0, best[0], rows, best[1])
+        if uniform is None:
+            raise ValueError("no candidate plan fits this batch")
+        return uniform
     if capacity is None:
         # the memory model's token ceiling is necessary, not sufficient (CP workspaces come on top):
         # shrink the per-rank capacity until some candidate fits
@@ -135,7 +184,7 @@ def select(lengths: dict, world: int, pattern: str, model: Model, degrees=(1, 2,
         last = None
         for frac in (1.0, 0.9, 0.8, 0.7, 0.6, 0.5, 0.4, 0.3):
             try:
-                return select(lengths, world, pattern, model, degrees, max(1, int(top * frac)))
+                return select(lengths, world, pattern, model, degrees, max(1, int(top * frac)), dynamic=False)
             except ValueError as err:
                 last = err
         raise last

@@ -58,5 +58,4 @@ def build(cfg, world: int, workload: str = "lognormal", plan: str = "online", *,
     except ValueError as err:
         raise ValueError(f"no (cp_gdn, cp_gqa) plan of this batch fits {world} GPU(s) under the calibrated "
                          f"memory model ({err}); use more GPUs or shorter documents") from err
-    return Workload(batch, sel.plan, desc, f"online cp_gdn{sel.cp_gdn} cp_gqa{sel.cp_gqa} over {world}",
-                    sel.predicted_update_ms)
+    return Workload(batch, sel.plan, desc, f"online {sel.description} over {world}", sel.predicted_update_ms)

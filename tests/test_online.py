@@ -28,7 +28,7 @@ def test_selection_is_deterministic_and_prefers_cp1_for_short_documents():
 def test_long_documents_force_context_parallelism():
     model = model_from_config(hybrid_1p3b(), device_bytes=180 * 1024 ** 3)
     lengths = dict(enumerate(lognormal_lengths(1 << 20, 4096, 1.0, 512, 131072, 16, 3) + [131072]))
-    sel = select(lengths, 8, hybrid_1p3b().pattern, model, capacity=32768)
+    sel = select(lengths, 8, hybrid_1p3b().pattern, model, capacity=32768, dynamic=False)
     assert max(sel.cp_gdn, sel.cp_gqa) >= 4
     assert any(r["fits"] for r in sel.candidates)
 
@@ -51,3 +51,22 @@ def test_selection_shrinks_capacity_until_a_plan_fits_the_calibrated_memory():
     assert all(ev.evaluate(mb)["fits"] for mb in sel.plan.microbatches)
     placed = sorted(s for mb in sel.plan.microbatches for g in mb.ingress.groups for s in g.samples)
     assert placed == sorted(lengths)
+
+
+def test_dynamic_plan_gives_long_documents_big_teams_and_short_ones_cp1():
+    """One long document among short ones: the per-document plan runs the long one on a large team
+    and the short ones on CP1 ranks in the same microbatches, and is chosen when predicted faster."""
+    from prism_cp_b200.planner.online import dynamic_candidates
+    model = model_from_config(hybrid_1p3b(), device_bytes=180 * 1024 ** 3)
+    lengths = {0: 65536, **{i: 2048 for i in range(1, 97)}}
+    cands = dynamic_candidates(lengths, 8, hybrid_1p3b().pattern, model)
+    assert cands
+    _, cap, plan, _ = min(cands, key=lambda c: c[0])
+    validate_plan(plan, lengths)
+    first = plan.microbatches[0]
+    degree = {s: cp for s, cp in first.layers[3][0].sample_cp()}
+    assert degree[0] >= 65536 // cap and min(degree.values()) == 1
+    sel = select(lengths, 8, hybrid_1p3b().pattern, model)
+    uniform = select(lengths, 8, hybrid_1p3b().pattern, model, dynamic=False)
+    assert sel.predicted_update_ms <= uniform.predicted_update_ms
+    assert (sel.dynamic_capacity is not None) == (sel.predicted_update_ms < uniform.predicted_update_ms)
