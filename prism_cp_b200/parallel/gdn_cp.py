@@ -7,15 +7,16 @@ may continue on the next one. Two things cross ranks:
 * conv halo - the 3 tokens before a continuing segment, sent by the previous
   rank (forward) with the matching gradient sent back (backward);
 * recurrent state - the state a continuing sample carries into this rank.
-  Every rank runs a zero-start state pass over its last segment only (the one
-  that continues on the next rank), giving that segment's final state ``F``,
-  and, when one sample spans the whole rank, the tail's transition matrix
-  ``M`` (``S_out = M S_in + F``).
-  ``(F, M)`` are all-gathered over the team (differentiable), each rank folds
-  the prefix of its chain of predecessors and then runs the real state pass
-  from that state. Forward and backward are parallel across the team (no rank
-  waits for another rank's recurrence); gradients reach the predecessors' ``F``
-  and ``M`` through the all-gather's backward.
+  The recurrence is affine in that state, so every rank runs its segments from
+  zero (outputs and the last segment's final state ``F``) and, when its first
+  segment continues a sample, the zero-value recurrence of that segment from
+  the identity (per-token rows ``L`` and the transition matrix ``M``,
+  ``S_out = M S_in + F``) on a second stream. ``(F, M)`` are all-gathered over
+  the team (differentiable), each rank folds the prefix of its chain of
+  predecessors into ``S_in`` and adds ``L S_in`` to its first segment's
+  outputs. Forward and backward are parallel across the team (no rank waits
+  for another rank's recurrence); gradients reach the predecessors' ``F`` and
+  ``M`` through the all-gather's backward.
 
 Reference behaviour: Megatron GDN ``--linear-cp-mode chunkwise`` with the
 state exchange modelled at joint_cp/model.py:141-145.
@@ -27,8 +28,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops.elementwise import causal_conv1d_silu
-from ..ops.gdn import (chunk_output, chunk_prep, chunk_state, chunk_transition, fused_gated_delta_rule,
-                       fused_supported)
+from ..ops.gdn import chunk_gated_delta_rule, fused_gated_delta_rule, fused_supported
 from ..planner.joint.ir import spans as layout_spans
 
 HALO = 3
@@ -151,7 +151,38 @@ def conv_with_halo(ctx, x, weight):
     return causal_conv1d_silu(x, weight, ctx.cu_segments, halo)
 
 
+_SIDE: dict = {}
+
+
+def _side_stream(device) -> torch.cuda.Stream:
+    s = _SIDE.get(device.index)
+    if s is None:
+        s = _SIDE[device.index] = torch.cuda.Stream(device=device)
+    return s
+
+
+def _rule(q, k, v, g, beta, layout, initial_state=None):
+    """(o, per-segment final states) on the fused kernels where they apply, else the chunked torch form."""
+    if fused_supported(q, v):
+        return fused_gated_delta_rule(q, k, v, g, beta, layout, initial_state=initial_state)
+    return chunk_gated_delta_rule(q, k, v, g, beta, layout, initial_state=initial_state)
+
+
 def delta_rule_cp(ctx, q, k, v, g, beta):
+    """The recurrence of this rank's segments, with the state a continuing sample carries in.
+
+    The recurrence is affine in the incoming state S_in of the first segment: every output row is
+    o_t = o0_t + L_t S_in and the segment's final state is F + M S_in, where o0 and F come from the
+    pass started at zero and L (one dk-row per token and head) and M from the same recurrence with
+    zero values started at the identity. So each rank runs
+      * the zero-start pass over all its segments (outputs, and F of the last segment), and
+      * if its first segment continues a sample, the zero-value pass over that segment alone
+        (dv = dk, on a second stream, concurrently with the first),
+    all-gathers (F, M) of its last segment over the team, folds its predecessors' chain into S_in
+    and adds L S_in to the first segment's rows: no pass waits for another rank, and no pass is run
+    twice. Gradients reach both passes and the predecessors' (F, M) through autograd and the
+    all-gather's backward.
+    """
     layout = ctx.chunk_layout()
     links = rank_links(ctx)
     i = ctx.index
@@ -159,44 +190,38 @@ def delta_rule_cp(ctx, q, k, v, g, beta):
     H, DK, DV = q.shape[1], q.shape[2], v.shape[2]
     nseg = len(ctx.segment_lengths)
     f32 = torch.float32
-    fused = fused_supported(q, v)
-    prep = None if fused else chunk_prep(q, k, v, g, beta, layout)
-    if fused and last_cont:
-        # tail state from zero, and (for a single continuing segment) the linear
-        # map of the incoming state: the recurrence with zero values from I
-        # these passes only feed a small state: recomputed in the backward rather than kept
-        n_last = ctx.segment_lengths[-1]
-        if nseg > 1 and n_last >= 64:
-            # only the last segment continues on the next rank: run the tail pass over its rows alone
-            if getattr(ctx, "_tail_layout", None) is None:
+    n0 = ctx.segment_lengths[0] if nseg else 0
+    linear = None
+    if first_cont:
+        if nseg == 1:
+            lay0 = layout
+        else:
+            if getattr(ctx, "_first_layout", None) is None:
                 from ..ops.gdn import ChunkLayout
-                ctx._tail_layout = ChunkLayout((n_last,), q.device)
-            rows = slice(q.shape[0] - n_last, None)
-            _, S_last = fused_gated_delta_rule(q[rows], k[rows], v[rows], g[rows], beta[rows], ctx._tail_layout,
-                                               keep_intermediates=False)
-            F_tail = S_last[0]
+                ctx._first_layout = ChunkLayout((n0,), q.device)
+            lay0 = ctx._first_layout
+        def run():
+            eye = torch.eye(DK, dtype=f32, device=q.device).expand(1, H, DK, DK).contiguous()
+            return _rule(q[:n0], k[:n0], q.new_zeros((n0, H, DK)), g[:n0], beta[:n0], lay0, initial_state=eye)
+
+        if q.is_cuda:
+            main, side = torch.cuda.current_stream(q.device), _side_stream(q.device)
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                linear = run()
+            for t in (q, k, g, beta):
+                t.record_stream(side)
         else:
-            _, S_zero = fused_gated_delta_rule(q, k, v, g, beta, layout, keep_intermediates=False)
-            F_tail = S_zero[nseg - 1]
-        if first_cont and single:
-            eye = torch.eye(DK, dtype=f32, device=q.device).expand(nseg, H, DK, DK).contiguous()
-            _, M_all = fused_gated_delta_rule(q, k, torch.zeros_like(q), g, beta, layout, initial_state=eye,
-                                              keep_intermediates=False)
-            M_tail = M_all[nseg - 1]
-        else:
-            M_tail = torch.zeros((H, DK, DK), dtype=f32, device=q.device)
-    elif fused:
-        F_tail = torch.zeros((H, DK, DV), dtype=f32, device=q.device)
-        M_tail = torch.zeros((H, DK, DK), dtype=f32, device=q.device)
-    elif last_cont:
-        _, _, S_zero = chunk_state(prep, None)
-        F_tail = S_zero[nseg - 1]
-        if first_cont and single:
-            M_tail = chunk_transition(prep, nseg - 1)
-        else:
-            M_tail = torch.zeros((H, DK, DK), dtype=f32, device=q.device)
+            linear = run()
+    o, S_zero = _rule(q, k, v, g, beta, layout)
+    if linear is not None and q.is_cuda:
+        torch.cuda.current_stream(q.device).wait_stream(_side_stream(q.device))
+        for t in linear:
+            t.record_stream(torch.cuda.current_stream(q.device))
+    F_tail = S_zero[nseg - 1] if last_cont else torch.zeros((H, DK, DV), dtype=f32, device=q.device)
+    if last_cont and first_cont and single:
+        M_tail = linear[1][0]
     else:
-        F_tail = torch.zeros((H, DK, DV), dtype=f32, device=q.device)
         M_tail = torch.zeros((H, DK, DK), dtype=f32, device=q.device)
     packed = torch.cat([F_tail.reshape(-1), M_tail.reshape(-1)])
     if torch.is_grad_enabled() and not packed.requires_grad:
@@ -204,7 +229,6 @@ def delta_rule_cp(ctx, q, k, v, g, beta):
         # backward node, or the team's backward collectives would not match
         packed = packed.detach().requires_grad_(True)
     gathered = all_gather_rows(packed, ctx.team)
-    initial = None
     if first_cont:
         chain = [i - 1]
         while chain[-1] > 0 and links[chain[-1]][0] and links[chain[-1]][2]:
@@ -218,10 +242,7 @@ def delta_rule_cp(ctx, q, k, v, g, beta):
         for r in reversed(chain[:-1]):
             F_r, M_r = unpack(r)
             state = M_r @ state + F_r
-        rest = torch.zeros((nseg - 1, H, DK, DV), dtype=f32, device=q.device)
-        initial = torch.cat([state[None], rest], 0)
-    if fused:
-        o, _ = fused_gated_delta_rule(q, k, v, g, beta, layout, initial_state=initial)
-        return tie(o, gathered)
-    Delta, S_all, _ = chunk_state(prep, initial)
-    return tie(chunk_output(prep, Delta, S_all), gathered)
+        # o_t += L_t S_in for the first segment's rows (one [n0, dk] x [dk, dv] product per head)
+        corr = torch.einsum("thk,hkv->thv", linear[0].to(f32), state)
+        o = torch.cat([(o[:n0].to(f32) + corr).to(o.dtype), o[n0:]], 0)
+    return tie(o, gathered)

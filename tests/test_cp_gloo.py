@@ -132,6 +132,8 @@ def _gdn_case(rank, world, lengths):
 @pytest.mark.parametrize("world,lengths", [
     (2, ((0, 200), (1, 120))),            # sample 0 continues from rank 0 to rank 1
     (4, ((0, 448), (1, 64))),             # sample 0 spans ranks 0-3: ranks 1 and 2 pass the state through
+    (2, ((0, 200), (1, 120), (2, 90))),   # rank 1: a continuing first segment followed by a whole sample
+    (4, ((0, 96), (1, 380), (2, 36))),    # sample 1 from rank 0 through rank 3, starting mid-rank
 ])
 def test_gdn_chunkwise_cp_matches_single_rank(world, lengths):
     run_ranks(_gdn_case, world, lengths)
