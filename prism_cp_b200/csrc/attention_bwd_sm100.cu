@@ -1,7 +1,8 @@
 // Flash-attention backward on tcgen05 (sm_100a), varlen / causal / GQA, head_dim 128.
 //
-// Two atomic-free kernels share the CTA shape of the forward (warps 0-3 compute
-// with thread == TMEM lane == tile row, warp 4 TMA producer, warp 5 MMA issuer):
+// Two atomic-free kernels share the CTA shape of the forward (warps 0-7 compute, warps w
+// and w + 4 on TMEM lanes 32(w % 4).. == tile rows, each taking half of the columns; warp 8
+// TMA producer, warp 9 MMA issuer):
 //   kv kernel  one CTA per (128-key tile, kv head), looping over the query heads
 //              of the GQA group and the query tiles that see the keys:
 //                S^T = K Q^T, dP^T = V dO^T            (TMEM cols 0-255)
@@ -30,7 +31,6 @@ constexpr int D = 128;
 constexpr int TILE = 128;
 constexpr int TILE_BYTES = 128 * D * 2;  // 32 KiB
 constexpr int HALF = TILE_BYTES / 2;     // one 64-column box
-constexpr int NUM_THREADS = 192;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct Params {
@@ -83,12 +83,13 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int k) {
 constexpr int KV_THREADS = 320;
 constexpr int KV_COMPUTE = 256;
 constexpr int KV_QT = 64;                    // query rows per iteration
+constexpr int KV_STAGES = 3;                 // Q / dO ring: the load of tile it + 2 overlaps the dK/dV MMAs of it
 constexpr int KV_QBYTES = KV_QT * D * 2;     // 16 KiB: 64 rows x 128 dims (two 64-dim boxes)
 constexpr int KV_QHALF = KV_QBYTES / 2;
 constexpr int KV_PBYTES = 128 * KV_QT * 2;   // 16 KiB: 128 keys x 64 queries
-constexpr int KV_OFF_Q = 2 * TILE_BYTES;                 // Q[2]
-constexpr int KV_OFF_DO = KV_OFF_Q + 2 * KV_QBYTES;      // dO[2]
-constexpr int KV_OFF_PT = KV_OFF_DO + 2 * KV_QBYTES;
+constexpr int KV_OFF_Q = 2 * TILE_BYTES;                         // Q[KV_STAGES]
+constexpr int KV_OFF_DO = KV_OFF_Q + KV_STAGES * KV_QBYTES;      // dO[KV_STAGES]
+constexpr int KV_OFF_PT = KV_OFF_DO + KV_STAGES * KV_QBYTES;
 constexpr int KV_OFF_DST = KV_OFF_PT + KV_PBYTES;
 constexpr int KV_OFF_STAT = KV_OFF_DST + KV_PBYTES;      // lse[2][64], dsum[2][64]
 constexpr int KV_OFF_BAR = KV_OFF_STAT + 4 * KV_QT * 4;
@@ -109,15 +110,15 @@ __global__ void __launch_bounds__(KV_THREADS, 1)
   float* dsum_s = lse_s + 2 * KV_QT;                             // [2][64]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + KV_OFF_BAR);
   uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;    // [2]
-  uint64_t* q_empty = bars + 3;   // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_free = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* mma_done = bars + 10;
-  uint64_t* acc_done = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 13);
+  uint64_t* q_full = bars + 1;                  // [KV_STAGES]
+  uint64_t* q_empty = bars + 1 + KV_STAGES;     // [KV_STAGES]
+  uint64_t* s_full = bars + 1 + 2 * KV_STAGES;  // [2]
+  uint64_t* s_free = s_full + 2;                // [2]
+  uint64_t* p_full = s_full + 4;
+  uint64_t* mma_done = s_full + 5;
+  uint64_t* acc_done = s_full + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 7);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(s_full + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kv_head = blockIdx.y;
@@ -144,9 +145,11 @@ __global__ void __launch_bounds__(KV_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < KV_STAGES; ++b) {
       mbar_init(&q_full[b], 1);
       mbar_init(&q_empty[b], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&s_free[b], KV_COMPUTE);
     }
@@ -175,8 +178,9 @@ __global__ void __launch_bounds__(KV_THREADS, 1)
       tma_load_3d(sV + HALF, &tmV, kv_full, 64, kv_head, k_seg + k0);
       int issued = 0;
       for (int it = 0; it < n_it; ++it) {
-        const int s = it & 1;
-        if (it >= 2 && !mbar_wait_bounded(&q_empty[s], ((it >> 1) - 1) & 1, abort_flag, p.status, kTimeoutProducer))
+        const int s = it % KV_STAGES;
+        if (it >= KV_STAGES &&
+            !mbar_wait_bounded(&q_empty[s], (it / KV_STAGES - 1) & 1, abort_flag, p.status, kTimeoutProducer))
           break;
         const int h = kv_head * rep + it / per_head;
         const int i = i_start + it % per_head;
@@ -200,8 +204,8 @@ __global__ void __launch_bounds__(KV_THREADS, 1)
       }
       // copies still in flight after an abort land before the CTA exits
       mbar_wait_bounded(kv_full, 0, nullptr, nullptr, 0);
-      for (int it = issued > 2 ? issued - 2 : 0; it < issued; ++it)
-        mbar_wait_bounded(&q_full[it & 1], (it >> 1) & 1, nullptr, nullptr, 0);
+      for (int it = issued > KV_STAGES ? issued - KV_STAGES : 0; it < issued; ++it)
+        mbar_wait_bounded(&q_full[it % KV_STAGES], (it / KV_STAGES) & 1, nullptr, nullptr, 0);
     }
   } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA issuer
@@ -212,8 +216,8 @@ __global__ void __launch_bounds__(KV_THREADS, 1)
       bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, p.status, kTimeoutMma);
       for (int it = 0; ok && it <= n_it; ++it) {
         if (it < n_it) {
-          const int s = it & 1, b = it & 1;
-          if (!mbar_wait_bounded(&q_full[s], (it >> 1) & 1, abort_flag, p.status, kTimeoutMma)) break;
+          const int s = it % KV_STAGES, b = it & 1;
+          if (!mbar_wait_bounded(&q_full[s], (it / KV_STAGES) & 1, abort_flag, p.status, kTimeoutMma)) break;
           if (it >= 2 && !mbar_wait_bounded(&s_free[b], ((it >> 1) - 1) & 1, abort_flag, p.status, kTimeoutMma)) break;
           tc_fence_after();
           const uint32_t aQ = smem_u32(smem + KV_OFF_Q + s * KV_QBYTES);
@@ -233,7 +237,7 @@ __global__ void __launch_bounds__(KV_THREADS, 1)
           umma_commit(&s_full[b]);
         }
         if (it >= 1) {
-          const int jt = it - 1, s = jt & 1;
+          const int jt = it - 1, s = jt % KV_STAGES;
           if (!mbar_wait_bounded(p_full, jt & 1, abort_flag, p.status, kTimeoutMma)) break;
           tc_fence_after();
           const uint32_t aQ = smem_u32(smem + KV_OFF_Q + s * KV_QBYTES);
@@ -260,28 +264,43 @@ __global__ void __launch_bounds__(KV_THREADS, 1)
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const float c_log2 = p.scale * kLog2e;
     const bool row_ok = kk < k_len;
+    // LSE and D of a query tile: threads r < 64 of the first half load row r from global memory one
+    // iteration ahead (the loads are in flight during the previous tile's math) and store it into the
+    // shared double buffer [it & 1] at the end of that iteration.
+    const bool stat_thread = half == 0 && r < KV_QT;
+    auto fetch_stats = [&](int it2, float& l, float& d) {
+      const int h = kv_head * rep + it2 / per_head;
+      const int q0 = (i_start + it2 % per_head) * KV_QT;
+      const int qq = q0 + r;
+      const float* lse_src = p.lse;
+      const float* dsum_src = p.dsum;
+      long row = q_seg + qq;
+      if constexpr (PEER) {
+        int owner;
+        row = peer_row(src, seq, q0, owner) + r;
+        lse_src = src.lse[owner];
+        dsum_src = src.dsum[owner];
+      }
+      const bool v = qq < q_len;
+      l = v ? lse_src[(long)h * p.tq + row] * kLog2e : INFINITY;
+      d = v ? dsum_src[(long)h * p.tq + row] : 0.f;
+    };
+    if (stat_thread && n_it > 0) {
+      float l, d;
+      fetch_stats(0, l, d);
+      lse_s[r] = l;
+      dsum_s[r] = d;
+    }
     bool ok = true;
     for (int it = 0; it < n_it && ok; ++it) {
       const int b = it & 1;
-      const int h = kv_head * rep + it / per_head;
       const int i = i_start + it % per_head;
       const int q0 = i * KV_QT;
-      if (half == 0 && r < KV_QT) {
-        const int qq = q0 + r;
-        const bool v = qq < q_len;
-        const float* lse_src = p.lse;
-        const float* dsum_src = p.dsum;
-        long row = q_seg + qq;
-        if constexpr (PEER) {
-          int owner;
-          row = peer_row(src, seq, q0, owner) + r;
-          lse_src = src.lse[owner];
-          dsum_src = src.dsum[owner];
-        }
-        lse_s[b * KV_QT + r] = v ? lse_src[(long)h * p.tq + row] * kLog2e : INFINITY;
-        dsum_s[b * KV_QT + r] = v ? dsum_src[(long)h * p.tq + row] : 0.f;
-      }
+      // the stats of tile it are in smem; every thread has finished reading those of tile it - 1
       named_sync_kv();
+      float next_l = 0.f, next_d = 0.f;
+      const bool prefetch = stat_thread && it + 1 < n_it;
+      if (prefetch) fetch_stats(it + 1, next_l, next_d);
       ok = named_barrier_and(mbar_wait_bounded(&s_full[b], (it >> 1) & 1, abort_flag, p.status, kTimeoutEpilogue),
                              1, KV_COMPUTE);
       if (!ok) break;
@@ -293,14 +312,23 @@ __global__ void __launch_bounds__(KV_THREADS, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[b]);
-      // P^T and dS^T overwrite the loaded S^T / dP^T values in place (keeps register use flat)
+      // P^T and dS^T overwrite the loaded S^T / dP^T values in place (keeps register use flat); the
+      // stats are read as float4 broadcasts
+      const float4* lse4 = reinterpret_cast<const float4*>(lse_s + b * KV_QT + col0);
+      const float4* dsum4 = reinterpret_cast<const float4*>(dsum_s + b * KV_QT + col0);
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int qq = q0 + col0 + e;
-        const bool valid = row_ok && qq < q_len && (!p.causal || kk <= qq);
-        const float pe = valid ? exp2f(__uint_as_float(s_raw[e]) * c_log2 - lse_s[b * KV_QT + col0 + e]) : 0.f;
-        s_raw[e] = __float_as_uint(pe);
-        dp_raw[e] = __float_as_uint(pe * (__uint_as_float(dp_raw[e]) - dsum_s[b * KV_QT + col0 + e]));
+      for (int e4 = 0; e4 < 8; ++e4) {
+        const float4 l4 = lse4[e4], d4 = dsum4[e4];
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = 4 * e4 + u;
+          const int qq = q0 + col0 + e;
+          const bool valid = row_ok && qq < q_len && (!p.causal || kk <= qq);
+          const float pe = valid ? exp2f(__uint_as_float(s_raw[e]) * c_log2 - lv[u]) : 0.f;
+          s_raw[e] = __float_as_uint(pe);
+          dp_raw[e] = __float_as_uint(pe * (__uint_as_float(dp_raw[e]) - dv[u]));
+        }
       }
       const float* pv = reinterpret_cast<const float*>(s_raw);
       const float* dsv = reinterpret_cast<const float*>(dp_raw);
@@ -319,6 +347,10 @@ __global__ void __launch_bounds__(KV_THREADS, 1)
         *reinterpret_cast<uint4*>(sdST + off) =
             make_uint4(pack_bf16x2(dsv[8 * g], dsv[8 * g + 1]), pack_bf16x2(dsv[8 * g + 2], dsv[8 * g + 3]),
                        pack_bf16x2(dsv[8 * g + 4], dsv[8 * g + 5]), pack_bf16x2(dsv[8 * g + 6], dsv[8 * g + 7]));
+      }
+      if (prefetch) {
+        lse_s[(b ^ 1) * KV_QT + r] = next_l;
+        dsum_s[(b ^ 1) * KV_QT + r] = next_d;
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();

@@ -1,15 +1,16 @@
 // Variable-length causal / full GQA flash-attention forward on tcgen05 (sm_100a).
 //
 // One CTA computes one 128-query tile of one query head (head_dim 128):
-//   warps 0-3  softmax: thread r owns query row r of the tile, which is TMEM
-//              lane r, so the whole score row is in that thread's registers after
-//              tcgen05.ld (no shuffles). P = exp2(s - m) is written to shared
-//              memory in the 128-byte-swizzled K-major layout the tensor core
-//              reads as the A operand of P.V. The running max is only moved (and
-//              O in TMEM rescaled) when it grows by more than 2^8, which keeps
+//   warps 0-7  softmax: query row r of the tile is TMEM lane r; warps w and w + 4
+//              both own rows 32(w % 4).. and take one 64-key half of each score
+//              row (after tcgen05.ld, no shuffles; the two halves exchange their
+//              row maxima through shared memory). P = exp2(s - m) is written to
+//              shared memory in the 128-byte-swizzled K-major layout the tensor
+//              core reads as the A operand of P.V. The running max is only moved
+//              (and O in TMEM rescaled) when it grows by more than 2^8, which keeps
 //              the fp32 accumulators exact while making rescales rare.
-//   warp 4     TMA producer: Q once, then K/V tiles of 128 keys into a 2-stage ring.
-//   warp 5     allocates TMEM (S double buffer: cols 0-255, O: cols 256-383) and
+//   warp 8     TMA producer: Q once, then K/V tiles of 128 keys into a 2-stage ring.
+//   warp 9     allocates TMEM (S double buffer: cols 0-255, O: cols 256-383) and
 //              issues S_j = Q K_j^T and O += P_{j-1} V_{j-1} from one thread.
 // Q, K, V are read through 3-D tensor maps over [tokens, heads, 128] views with
 // arbitrary token stride, so the kernel consumes the fused QKV projection in place.

@@ -416,7 +416,10 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
 }
 
 // ============================================================================ state passes (tcgen05)
-constexpr int ST_THREADS = 192;  // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 one TMEM lane each
+// warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-9 the state lanes: warps w and w + 4 share TMEM lane
+// quarter w % 4 and split its columns in halves (state columns, Delta columns, output tokens)
+constexpr int ST_THREADS = 320;
+constexpr int ST_LANE_THREADS = 256;
 constexpr int VS = 128;          // value columns per CTA
 constexpr int ST_OFF_WN = 0;
 constexpr int ST_OFF_QG = 2 * BLK;
@@ -427,7 +430,8 @@ constexpr int ST_STAGE = 9 * BLK;
 constexpr int ST_STAGES = 2;
 constexpr int ST_OFF_A1 = ST_STAGES * ST_STAGE;  // state^T in bf16: 128 rows x 128 cols, 2 blocks of 16 KB
 constexpr int ST_OFF_A2 = ST_OFF_A1 + 2 * 128 * 128;  // (d)Delta^T in bf16: 128 rows x 64 cols
-constexpr int ST_OFF_BAR = ST_OFF_A2 + 128 * 128;
+constexpr int ST_OFF_ID = ST_OFF_A2 + 128 * 128;  // forward: 64 x 64 identity (adds U^T to Delta^T on the MMA)
+constexpr int ST_OFF_BAR = ST_OFF_ID + BLK;
 constexpr int ST_SMEM = ST_OFF_BAR + 256 + 1024;
 constexpr int ST_TMEM_COLS = 256;  // [0,128) state^T, [128,192) (d)Delta^T, [192,256) O^T
 
@@ -476,11 +480,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(a1_ready, 128);
+    mbar_init(a1_ready, ST_LANE_THREADS);
     mbar_init(d1_full, 1);
-    mbar_init(a2_ready, 128);
+    mbar_init(a2_ready, ST_LANE_THREADS);
     mbar_init(s_ready, 1);
-    mbar_init(o_empty, 128);
+    mbar_init(o_empty, ST_LANE_THREADS);
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -495,6 +499,16 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
   if (warp == 1) {
     tmem_alloc(tmem_slot, ST_TMEM_COLS);
     tmem_relinquish();
+  }
+  if (!BWD) {
+    // 64 x 64 bf16 identity in the 128-byte-swizzled layout: B operand of Delta^T += U^T x I
+    for (int i = threadIdx.x; i < 64 * 8; i += ST_THREADS) {
+      const int r = i >> 3, cc = i & 7;
+      uint4 z = make_uint4(0u, 0u, 0u, 0u);
+      if ((r >> 3) == cc) reinterpret_cast<__nv_bfloat16*>(&z)[r & 7] = __float2bfloat16(1.f);
+      *reinterpret_cast<uint4*>(smem + ST_OFF_ID + swz(r, cc)) = z;
+    }
+    fence_proxy_async();
   }
   tc_fence_before();
   __syncthreads();
@@ -556,12 +570,14 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         for (int k = 0; k < 8; ++k)
           umma_bf16_ss(tmem + 128, make_smem_desc_sw128(a1 + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
                        make_smem_desc_sw128(bsrc + (k >> 2) * BLK + (k & 3) * 32, 16, 1024), id_n64, k > 0);
-        if (BWD) {
-          // += dO^T x Aqk: K = query rows, A and B MN-major
+        {
+          // bwd: += dO^T x Aqk; fwd: += U^T x I (Delta = U + Wn S exactly in fp32). K = chunk rows, A and B
+          // MN-major
+          const uint32_t bsum = BWD ? st + ST_OFF_AQK : smem_u32(smem + ST_OFF_ID);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             umma_bf16_ss(tmem + 128, make_smem_desc_sw128(st + ST_OFF_X + k * 2048, BLK, 1024),
-                         make_smem_desc_sw128(st + ST_OFF_AQK + k * 2048, BLK, 1024), id_do_aqk, 1);
+                         make_smem_desc_sw128(bsum + k * 2048, BLK, 1024), id_do_aqk, 1);
         }
         umma_commit(d1_full);
         if (BWD) {
@@ -603,7 +619,9 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     }
   } else {
     // ---------------------------------------------------------------- state lanes
-    const int quarter = warp & 3;
+    // lane quarter = warp % 4 (the TMEM lanes this warp may access), half = which warp of the pair:
+    // state columns [64 half, 64 half + 64), Delta columns and output tokens [32 half, 32 half + 32)
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
     const int vl = quarter * 32 + lane;
     const int v = v0 + vl;
     const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
@@ -613,22 +631,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
 
     auto drain_out = [&](int jj) {
       const int c = c_begin + jj;
-      const int t0 = p.tok0[c], n = p.len[c];
-      uint32_t r0[32], r1[32];
-      tmem_ld_32x32b_x32(tl + 192, r0);
-      tmem_ld_32x32b_x32(tl + 224, r1);
+      const int t0 = p.tok0[c] + 32 * half, n = p.len[c] - 32 * half;
+      uint32_t r0[32];
+      tmem_ld_32x32b_x32(tl + 192 + 32 * half, r0);
       tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        if (i < n) {
-          const float val = __uint_as_float(i < 32 ? r0[i] : r1[i - 32]);
-          p.out[((long)(t0 + i) * H + h) * DV + v] = __float2bfloat16(val);
-        }
-      }
+      for (int i = 0; i < 32; ++i)
+        if (i < n) p.out[((long)(t0 + i) * H + h) * DV + v] = __float2bfloat16(__uint_as_float(r0[i]));
     };
 
 #pragma unroll 1
-    for (int q4 = 0; q4 < 4; ++q4) {
+    for (int q4 = 2 * half; q4 < 2 * half + 2; ++q4) {
       uint32_t r[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(p.S_in ? p.S_in[sbase + (long)(q4 * 32 + i) * DV] : 0.f);
@@ -640,7 +653,6 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     for (int j = 0; j < nch; ++j) {
       const int c = BWD ? c_end - 1 - j : c_begin + j;
       const long ch = (long)c * H + h;
-      const int s = j & 1;
       if (j > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait_bounded(s_ready, (j - 1) & 1, abort_flag, p.status,
                                                        kTimeoutEpilogue));
@@ -648,21 +660,27 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
       }
       tc_fence_after();
       const float gm = p.gam[ch];
-#pragma unroll 1
-      for (int q4 = 0; q4 < 4; ++q4) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tl + q4 * 32, r);
+      {
+        // both 32-column pieces of this half in flight before the first wait
+        uint32_t r[2][32];
+        tmem_ld_32x32b_x32(tl + 64 * half, r[0]);
+        tmem_ld_32x32b_x32(tl + 64 * half + 32, r[1]);
         tmem_wait_ld();
-        uint8_t* blk = A1 + (q4 >> 1) * 16384;
+        uint8_t* blk = A1 + half * 16384;
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const uint4 pk = pack8u(r + 8 * m);
-          *reinterpret_cast<uint4*>(blk + swz(vl, (q4 & 1) * 4 + m)) = pk;
-          if (p.states != nullptr) reinterpret_cast<uint4*>(p.states + (ch * DV + v) * DK + q4 * 32)[m] = pk;
+        for (int e = 0; e < 2; ++e) {
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            const uint4 pk = pack8u(r[e] + 8 * m);
+            *reinterpret_cast<uint4*>(blk + swz(vl, e * 4 + m)) = pk;
+            if (p.states != nullptr)
+              reinterpret_cast<uint4*>(p.states + (ch * DV + v) * DK + (2 * half + e) * 32)[m] = pk;
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[e][i] = __float_as_uint(__uint_as_float(r[e][i]) * gm);
         }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * gm);
-        tmem_st_32x32b_x32(tl + q4 * 32, r);
+        tmem_st_32x32b_x32(tl + 64 * half, r[0]);
+        tmem_st_32x32b_x32(tl + 64 * half + 32, r[1]);
       }
       tmem_wait_st();
       fence_proxy_async();
@@ -676,31 +694,14 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(d1_full, j & 1, abort_flag, p.status, kTimeoutEpilogue));
       if (!ok) break;
       tc_fence_after();
-      uint32_t r0[32], r1[32];
-      tmem_ld_32x32b_x32(tl + 128, r0);
-      tmem_ld_32x32b_x32(tl + 160, r1);
+      uint32_t r0[32];
+      tmem_ld_32x32b_x32(tl + 128 + 32 * half, r0);
       tmem_wait_ld();
-      float d[64];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        d[i] = __uint_as_float(r0[i]);
-        d[i + 32] = __uint_as_float(r1[i]);
-      }
-      if (!BWD) {
-        // Delta = U + Wn S (U from this stage's TMA tile; the stage cannot be refilled before a2_ready)
-        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (j >> 1) & 1, abort_flag, p.status,
-                                                       kTimeoutEpilogue));
-        if (!ok) break;
-        const uint8_t* ub = smem + s * ST_STAGE + ST_OFF_X + (vl >> 6) * BLK + ((vl & 7) << 1);
-        const int uc = (vl & 63) >> 3;
-#pragma unroll
-        for (int i = 0; i < 64; ++i) d[i] += bf2f(*reinterpret_cast<const __nv_bfloat16*>(ub + swz(i, uc)));
-      }
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const uint4 pk = pack8(d + 8 * m);
-        *reinterpret_cast<uint4*>(A2 + swz(vl, m)) = pk;
-        if (p.rows != nullptr) reinterpret_cast<uint4*>(p.rows + (ch * DV + v) * C)[m] = pk;
+      for (int m = 0; m < 4; ++m) {
+        const uint4 pk = pack8u(r0 + 8 * m);
+        *reinterpret_cast<uint4*>(A2 + swz(vl, 4 * half + m)) = pk;
+        if (p.rows != nullptr) reinterpret_cast<uint4*>(p.rows + (ch * DV + v) * C)[4 * half + m] = pk;
       }
       fence_proxy_async();
       tc_fence_before();
@@ -708,7 +709,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     }
     if (nch == 0 && p.S_out != nullptr) {
       // an empty sequence leaves its state unchanged
-      for (int d = 0; d < DK; ++d) p.S_out[sbase + (long)d * DV] = p.S_in ? p.S_in[sbase + (long)d * DV] : 0.f;
+      for (int d = 64 * half; d < 64 * half + 64; ++d)
+        p.S_out[sbase + (long)d * DV] = p.S_in ? p.S_in[sbase + (long)d * DV] : 0.f;
     }
     if (ok) {
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(s_ready, (nch - 1) & 1, abort_flag, p.status,
@@ -718,7 +720,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         if (!BWD && want_out) drain_out(nch - 1);
         if (p.S_out != nullptr) {
 #pragma unroll 1
-          for (int q4 = 0; q4 < 4; ++q4) {
+          for (int q4 = 2 * half; q4 < 2 * half + 2; ++q4) {
             uint32_t r[32];
             tmem_ld_32x32b_x32(tl + q4 * 32, r);
             tmem_wait_ld();
