@@ -52,8 +52,10 @@ def parse():
     ap.add_argument("--total-tokens", type=int, default=1 << 20)
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--overlap-grad-reduce", action="store_true",
-                    help="reduce-scatter gradient buckets during the last backward (side stream)")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="reduce-scatter the gradients after the backward and all-gather the parameters after the "
+                         "update on the compute stream (default: both bucketed on side streams, overlapping the "
+                         "last backward and the next forward)")
     ap.add_argument("--recompute-tokens", type=int, default=32768,
                     help="microbatches with more tokens than this on a rank recompute their layers in the backward "
                          "(0: never)")
@@ -165,8 +167,8 @@ def main():
 
     model = HybridModel(cfg, dtype=torch.bfloat16, device=device, seed=0)
     teams = Teams(world)
-    trainer = Trainer(model, teams, device, overlap_grad_reduce=args.overlap_grad_reduce,
-                      recompute_tokens=args.recompute_tokens or None)
+    trainer = Trainer(model, teams, device, overlap_grad_reduce=not args.no_overlap,
+                      overlap_param_gather=not args.no_overlap, recompute_tokens=args.recompute_tokens or None)
     host_inputs = trainer.prepare(batch, plan, pin=True)
     dev_inputs = [h.to(device) for h in host_inputs]
     torch.cuda.synchronize()
@@ -234,6 +236,8 @@ def main():
                                  f"{cfg.parameter_count() / 1e9:.2f}B params)",
                            parallelism=plan_desc, workload=args.workload, microbatches=len(plan.microbatches),
                            planner_predicted_ms_per_step=predicted_ms, recompute_tokens=args.recompute_tokens,
+                           grad_sync="serial" if args.no_overlap else
+                           "overlapped (reduce-scatter in the last backward, all-gather in the next forward)",
                            l2="per-step working set (32K-token activations) far exceeds the 126 MB L2",
                            **workload),
             "clocks": clocks.summary(), "e2e": e2e, "gpu_launches": launches * args.steps,

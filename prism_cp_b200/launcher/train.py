@@ -154,6 +154,7 @@ def main(argv=None) -> int:
                           clip_grad=args.clip_grad, warmup_steps=args.lr_warmup_iters,
                           decay_steps=args.lr_decay_iters or args.train_iters, records=args.records,
                           overlap_grad_reduce=args.overlap_grad_reduce,
+                          overlap_param_gather=args.overlap_param_gather,
                           bucket_bytes=(args.ddp_bucket_size or (64 << 20)) * 4)
     replays = json.loads(Path(args.joint_replay).read_text()) if args.joint_replay else None
     start = 1

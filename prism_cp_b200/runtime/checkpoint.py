@@ -39,6 +39,7 @@ def _keys(trainer) -> tuple[str, str]:
 
 def _state(trainer, plan_cursor: int) -> dict:
     opt = trainer.optimizer
+    opt.wait_parameters()  # an overlapped all-gather may still be writing the parameters
     prefix, shard = _keys(trainer)
     return {"model": {prefix + k: v for k, v in trainer.model.state_dict().items()},
             "optimizer": {shard: {"master": opt.master, "m": opt.m, "v": opt.v}},

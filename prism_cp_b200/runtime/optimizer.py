@@ -12,7 +12,10 @@ rank r owns shard r: fp32 master weights, Adam m and v. One update is
     all-gather(bf16 shard) -> flat bf16 params
 
 Gradient buckets (``bucket_bytes``) let the reduce-scatter of finished layers
-overlap the rest of the backward on a side stream (``--overlap-grad-reduce``).
+overlap the rest of the backward on a side stream (``--overlap-grad-reduce``),
+and the all-gather of the updated parameters overlap the next forward
+(``--overlap-param-gather``): each bucket is gathered on a side stream and the
+compute stream waits for it only when the first module that reads it runs.
 """
 
 from __future__ import annotations
@@ -143,6 +146,7 @@ class DistributedAdamW:
         self.stats = {"reduce_scatter_bytes": 0, "all_gather_bytes": 0, "overlapped_buckets": 0}
         self.audit = None
         self._overlap = None
+        self._param_gather = None
 
     @property
     def lo(self) -> int:
@@ -182,15 +186,31 @@ class DistributedAdamW:
             if b not in done:
                 self._reduce_bucket(b)
 
+    def _gather_bucket(self, b: int):
+        lo, hi, _, size, sh = self.slices[b]
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.flat.flat[lo:hi], self.shard_bf16[sh:sh + size], group=self.group)
+            self.stats["all_gather_bytes"] += (hi - lo) * self.flat.flat.element_size()
+        else:
+            self.flat.flat[lo:hi].copy_(self.shard_bf16[sh:sh + size])
+        if self.audit is not None:
+            self.audit.all_gather((hi - lo) * self.flat.flat.element_size())
+
     def gather_parameters(self):
-        if self.world == 1:
-            self.flat.flat.copy_(self.shard_bf16)
-        for lo, hi, _, size, sh in self.slices:
-            if self.world > 1:
-                dist.all_gather_into_tensor(self.flat.flat[lo:hi], self.shard_bf16[sh:sh + size], group=self.group)
-                self.stats["all_gather_bytes"] += (hi - lo) * self.flat.flat.element_size()
-            if self.audit is not None:
-                self.audit.all_gather((hi - lo) * self.flat.flat.element_size())
+        if self._param_gather is not None:
+            self._param_gather.launch()
+            return
+        for b in range(len(self.slices)):
+            self._gather_bucket(b)
+
+    def wait_parameters(self, top_only: bool = False):
+        """Make the current stream wait for the parameter all-gathers still in flight (only those of
+        the model's own parameters with ``top_only``; the layers wait in their pre-hooks)."""
+        if self._param_gather is not None:
+            if top_only:
+                self._param_gather.wait_top()
+            else:
+                self._param_gather.wait_all()
 
     # -------------------------------------------------------------- overlap
     def enable_overlap(self):
@@ -198,6 +218,13 @@ class DistributedAdamW:
         of the last microbatch has produced all of its gradients."""
         self._overlap = _GradOverlap(self)
         return self._overlap
+
+    def enable_param_gather_overlap(self, model: torch.nn.Module):
+        """Gather each bucket's updated parameters on a side stream after the update; the compute
+        stream waits per bucket in a forward pre-hook of every module that owns parameters, and for
+        the model's own parameters (embedding, final norm, head) before the next forward."""
+        self._param_gather = _ParamGather(self, model)
+        return self._param_gather
 
     # -------------------------------------------------------------- update
     def grad_norm_sq(self) -> torch.Tensor:
@@ -220,6 +247,8 @@ class DistributedAdamW:
         return self.sumsq
 
     def step(self):
+        # the previous gathers read shard_bf16, which this update rewrites
+        self.wait_parameters()
         self.flat.fold_param_grads()
         self.reduce_gradients()
         self.grad_norm_sq()
@@ -332,3 +361,65 @@ class _GradOverlap:
         for h in self.handles:
             h.remove()
         set_grad_listener(None)
+
+
+class _ParamGather:
+    """Parameter all-gather overlapped with the next forward (``--overlap-param-gather``).
+
+    ``launch`` runs after the update: the side stream waits for it, then gathers first the
+    buckets holding the model's own parameters (read before the first layer and by the head),
+    then the layers' buckets in forward order (the flat layout is backward order, so the last
+    bucket first), recording one event per bucket. A forward pre-hook on every submodule that
+    owns parameters makes the compute stream wait for its buckets' events; the trainer calls
+    ``wait_top`` before the first microbatch. Without a side stream (CPU) the gather is
+    synchronous.
+    """
+
+    def __init__(self, opt: DistributedAdamW, model: torch.nn.Module):
+        self.opt = opt
+        flat = opt.flat
+        self.side = torch.cuda.Stream(device=flat.flat.device) if flat.flat.is_cuda else None
+        self.pending: dict = {}
+        of = flat.bucket_of
+        self.top = tuple(sorted({of[id(p)] for p in model.parameters(recurse=False) if id(p) in of}))
+        rest = [b for b in reversed(range(len(opt.slices))) if b not in self.top]
+        self.order = list(self.top) + rest
+        self.handles = []
+        for mod in model.modules():
+            if mod is model:
+                continue
+            own = tuple(sorted({of[id(p)] for p in mod.parameters(recurse=False) if id(p) in of}))
+            if own:
+                self.handles.append(mod.register_forward_pre_hook(lambda m, args, own=own: self.wait(own)))
+
+    def launch(self):
+        if self.side is None:
+            for b in self.order:
+                self.opt._gather_bucket(b)
+            return
+        ready = torch.cuda.Event()
+        ready.record()
+        with torch.cuda.stream(self.side):
+            self.side.wait_event(ready)
+            for b in self.order:
+                self.opt._gather_bucket(b)
+                ev = torch.cuda.Event()
+                ev.record(self.side)
+                self.pending[b] = ev
+
+    def wait(self, buckets):
+        for b in buckets:
+            ev = self.pending.pop(b, None)
+            if ev is not None:
+                torch.cuda.current_stream().wait_event(ev)
+
+    def wait_top(self):
+        self.wait(self.top)
+
+    def wait_all(self):
+        self.wait(list(self.pending))
+
+    def close(self):
+        self.wait_all()
+        for h in self.handles:
+            h.remove()

@@ -56,7 +56,8 @@ class Trainer:
     def __init__(self, model, teams, device, lr=3e-4, min_lr=3e-5, weight_decay=0.1, clip_grad=1.0,
                  warmup_steps=0, decay_steps=1000, group=None, hbm_guard=True, records: str | None = None,
                  numerics=None, audit: bool = False, overlap_grad_reduce: bool = False,
-                 bucket_bytes: int = 256 << 20, logical=None, recompute_tokens: int | None = None):
+                 bucket_bytes: int = 256 << 20, logical=None, recompute_tokens: int | None = None,
+                 overlap_param_gather: bool = False):
         self.model, self.teams, self.device = model, teams, device
         self.world = teams.world
         self.rank = teams.rank
@@ -66,12 +67,14 @@ class Trainer:
             # every TP index updates its own copy of the model; shards never mix across indices
             group = teams.world_group
         self.group = group
-        self.flat = FlatParameters(model, self.world, bucket_bytes=bucket_bytes if overlap_grad_reduce else None)
+        bucketed = overlap_grad_reduce or overlap_param_gather
+        self.flat = FlatParameters(model, self.world, bucket_bytes=bucket_bytes if bucketed else None)
         self.optimizer = DistributedAdamW(self.flat, group=group, lr=lr, min_lr=min_lr,
                                           weight_decay=weight_decay, clip_grad=clip_grad,
                                           warmup_steps=warmup_steps, decay_steps=decay_steps, world=self.world,
                                           tp_group=self.tp.group if self.tp is not None else None)
         self.overlap = self.optimizer.enable_overlap() if overlap_grad_reduce else None
+        self.param_gather = self.optimizer.enable_param_gather_overlap(model) if overlap_param_gather else None
         self.cache = LayoutCache(self.world, self.rank, device, teams)
         self.hbm_guard = hbm_guard and device.type == "cuda"
         self.loss_acc = torch.zeros((), dtype=torch.float32, device=device)
@@ -100,6 +103,8 @@ class Trainer:
 
     # ------------------------------------------------------------------ step
     def forward_backward(self, batch_lengths: dict, plan: Plan, inputs: list):
+        # embedding, final norm and head; the layers wait for their own gathers in pre-hooks
+        self.optimizer.wait_parameters(top_only=True)
         self.loss_acc.zero_()
         last = len(plan.microbatches) - 1
         for index, (mb, host) in enumerate(zip(plan.microbatches, inputs)):
@@ -205,6 +210,7 @@ class Trainer:
         grad_norm = float(self.optimizer.sumsq.sqrt().item())
         finite_ok = math.isfinite(value) and math.isfinite(grad_norm)
         admitted, mem = self.admission()
+        self.optimizer.wait_parameters()
         if self.numerics is not None:
             self.numerics.observe(self.step_index, self.optimizer)
         if self.audit is not None:

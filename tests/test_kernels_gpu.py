@@ -301,6 +301,38 @@ def test_recomputed_layers_on_cuda_match_stored_activations():
     assert ((g0 - g1).norm() / g0.norm()).item() < 1e-2
 
 
+def test_overlapped_gradient_and_parameter_sync_on_cuda_match_serial():
+    """Bucketed reduce-scatter during the backward and parameter all-gather on a side stream during
+    the next forward (forward pre-hooks wait per bucket) give the same three steps as the serial
+    single-bucket sync."""
+    from prism_cp_b200.models.config import HybridConfig
+    from prism_cp_b200.models.hybrid import HybridModel
+    from prism_cp_b200.parallel.teams import Teams
+    from prism_cp_b200.planner.fixed import uniform_plan
+    from prism_cp_b200.runtime.batch import make_batch
+    from prism_cp_b200.runtime.trainer import Trainer
+    cfg = HybridConfig(num_layers=4, hidden_size=256, ffn_hidden_size=512, vocab_size=4096,
+                       num_attention_heads=4, num_query_groups=2, kv_channels=128,
+                       linear_num_key_heads=2, linear_key_head_dim=128, linear_value_head_dim=256)
+    dev = torch.device(DEV, torch.cuda.current_device())
+    out = []
+    for overlap in (False, True):
+        model = HybridModel(cfg, dtype=torch.bfloat16, device=dev, seed=0)
+        batch = make_batch([640, 384], cfg.vocab_size, seed=2)
+        plan = uniform_plan(batch.lengths, 1, 1, 1024, cfg.pattern)
+        tr = Trainer(model, Teams(1), dev, overlap_grad_reduce=overlap, overlap_param_gather=overlap,
+                     bucket_bytes=1 << 20)
+        if overlap:
+            assert len(tr.flat.buckets) > 2
+        losses = [tr.train_step(batch, plan).loss for _ in range(3)]
+        tr.optimizer.wait_parameters()
+        torch.cuda.synchronize()
+        out.append((losses, torch.cat([p.detach().float().reshape(-1) for p in model.parameters()])))
+    (l0, p0), (l1, p1) = out
+    assert l0 == pytest.approx(l1, rel=2e-3)
+    assert ((p0 - p1).norm() / p0.norm()).item() < 1e-3
+
+
 @pytest.mark.parametrize("j", [5, 200, 511])
 def test_cuda_model_is_causal(j):
     """Changing token j changes no hidden state before position j on the CUDA kernels (GEMMs,

@@ -103,7 +103,8 @@ def test_launcher_runs_native_and_fixed_schedulers(capsys):
 
 
 def test_overlapped_bucket_reduce_matches_single_bucket():
-    """Bucketed ownership with overlapped reduce-scatter gives the same update as one bucket."""
+    """Bucketed ownership with overlapped reduce-scatter and parameter all-gather gives the same
+    update as one bucket."""
     import torch
     from prism_cp_b200.models.config import hybrid_tiny
     from prism_cp_b200.models.hybrid import HybridModel
@@ -115,17 +116,23 @@ def test_overlapped_bucket_reduce_matches_single_bucket():
     batch = make_batch([512, 256, 256], cfg.vocab_size, seed=3)
     plan = uniform_plan(batch.lengths, 1, 1, 512, cfg.pattern)
     results = []
-    for overlap in (False, True):
+    for grads, params_overlap in ((False, False), (True, False), (True, True), (False, True)):
         model = HybridModel(cfg, dtype=torch.float32, device="cpu", seed=0)
-        tr = Trainer(model, Teams(1), torch.device("cpu"), overlap_grad_reduce=overlap, bucket_bytes=64 << 10)
-        if overlap:
+        tr = Trainer(model, Teams(1), torch.device("cpu"), overlap_grad_reduce=grads,
+                     overlap_param_gather=params_overlap, bucket_bytes=64 << 10)
+        if grads or params_overlap:
             assert len(tr.flat.buckets) > 2
+        if params_overlap:
+            # the model's own parameters are gathered before the layers'
+            pg = tr.param_gather
+            assert pg.order[:len(pg.top)] == list(pg.top) and sorted(pg.order) == list(range(len(tr.flat.buckets)))
         losses = [tr.train_step(batch, plan).loss for _ in range(2)]
         params = torch.cat([p.detach().reshape(-1) for p in model.parameters()])
         results.append((losses, params))
-    (l0, p0), (l1, p1) = results
-    assert l0 == pytest.approx(l1, rel=1e-6)
-    assert torch.allclose(p0, p1, rtol=1e-5, atol=1e-6)
+    l0, p0 = results[0]
+    for l1, p1 in results[1:]:
+        assert l0 == pytest.approx(l1, rel=1e-6)
+        assert torch.allclose(p0, p1, rtol=1e-5, atol=1e-6)
 
 
 def test_logical_gate_flags_a_different_model(tmp_path):
