@@ -86,10 +86,8 @@ class _CompiledP2PRoute:
         self.block_route = torch.tensor(block_route, dtype=torch.int64, device=device)
         self.block_row0 = torch.tensor(block_row0, dtype=torch.int64, device=device)
         out = sorted((e for e in edges if e[0] == rank), key=lambda e: e[2])
-        idx = []
-        for _, _, src_off, _, n in out:
-            idx.extend(range(src_off, src_off + n))
-        self.send_index = torch.tensor(idx, dtype=torch.int64, device=device)
+        idx = [torch.arange(src_off, src_off + n, dtype=torch.int64) for _, _, src_off, _, n in out]
+        self.send_index = (torch.cat(idx) if idx else torch.zeros(0, dtype=torch.int64)).to(device)
         self.rows_out = sum(e[4] for e in incoming)
         self.row_bytes, self.rows_per_block = row_bytes, rows_per_block
 
@@ -112,12 +110,19 @@ class P2PTransport:
         self.heap = heap
         self.rows_per_block = rows_per_block
         self.half = heap.nbytes // 2
+        self._routes: dict = {}  # (edges, row bytes) -> compiled block tables, built once per route
 
     def exchange(self, x: torch.Tensor, edges) -> torch.Tensor:
         heap = self.heap
         row_bytes = x[0].numel() * x.element_size() if x.shape[0] else 0
-        r = _CompiledP2PRoute(edges, heap.rank, row_bytes, self.rows_per_block, x.device, self.half,
-                              staging_offsets(edges, heap.world))
+        key = (edges, row_bytes)
+        r = self._routes.get(key)
+        if r is None:
+            r = _CompiledP2PRoute(edges, heap.rank, row_bytes, self.rows_per_block, x.device, self.half,
+                                  staging_offsets(edges, heap.world))
+            if len(self._routes) >= 512:
+                self._routes.clear()
+            self._routes[key] = r
         need = max(1, r.send_index.numel()) * row_bytes
         if need > self.half:
             raise ValueError(f"reshard needs {need} staging bytes, heap half is {self.half}")

@@ -37,6 +37,7 @@ class CompiledRoute:
         self.recv_index = torch.tensor(recv_idx, dtype=torch.int64, device=device)
         self.remote = any(e[0] != e[1] for e in edges)
         self.world, self.rank = world, rank
+        self.edges = tuple(edges)
 
 
 def _exchange(x: torch.Tensor, r: CompiledRoute, group) -> torch.Tensor:
@@ -108,7 +109,5 @@ def move(x: torch.Tensor, source, target, group=None) -> torch.Tensor:
         return x
     fwd, bwd = compiled
     if _P2P["transport"] is not None and fwd.remote:
-        edges = route(source.layout, target.layout, source.lengths, source.world)
-        inverse = tuple((d, s, b, a, n) for s, d, a, b, n in edges)
-        return _PermuteP2P.apply(x, edges, inverse, _P2P["transport"])
+        return _PermuteP2P.apply(x, fwd.edges, bwd.edges, _P2P["transport"])
     return _Permute.apply(x, fwd, bwd, group)

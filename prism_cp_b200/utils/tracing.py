@@ -255,8 +255,8 @@ def distributed_breakdown(model_name: str, seqs: int, seq_len: int, tokens_per_r
         gathered = [summary]
     if rank != 0:
         return None
-    return format_breakdown(gathered, dict(model=model_name, seqs=len(batch.lengths), seq_len=max(batch.lengths),
-                                           world=world, impl=os.environ.get("PRISM_CP_ATTENTION", "peer"),
+    return format_breakdown(gathered, dict(model=model_name, seqs=len(batch.lengths),
+                                           seq_len=max(batch.lengths.values()), world=world, impl=os.environ.get("PRISM_CP_ATTENTION", "peer"),
                                            plan=wl.parallelism, workload=workload))
 
 
