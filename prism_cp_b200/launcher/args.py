@@ -83,6 +83,9 @@ def build_parser() -> argparse.ArgumentParser:
     t.add_argument("--ddp-bucket-size", type=int, default=None)
     t.add_argument("--train-iters", type=int, default=10)
     t.add_argument("--recompute-granularity", default=None, choices=(None, "full", "selective"))
+    t.add_argument("--recompute-tokens", type=int, default=None,
+                   help="recompute the layers of microbatches holding more than this many tokens on a rank "
+                        "(--recompute-granularity full: every microbatch)")
     t.add_argument("--distributed-backend", default="nccl", choices=("nccl", "gloo"))
     t.add_argument("--distributed-timeout-minutes", type=int, default=30)
     k = p.add_argument_group("checkpoint and logging")

@@ -22,6 +22,7 @@ import datetime
 import json
 import os
 import sys
+import time
 from pathlib import Path
 
 import torch
@@ -72,8 +73,20 @@ def _planner_model(args, world: int):
         from ..planner.joint.cost import model_from_config
         m = model_from_config(model_config(args), B200_ENVELOPE["device_bytes"],
                               **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"})
-        _PLANNER_MODEL[key] = calibrated(m)
+        m = calibrated(m)
+        limit = recompute_limit(args)
+        if limit is not None:
+            from dataclasses import replace
+            m = replace(m, recompute_tokens=limit)
+        _PLANNER_MODEL[key] = m
     return _PLANNER_MODEL[key]
+
+
+def recompute_limit(args) -> int | None:
+    """Tokens per rank above which a microbatch recomputes its layers in the backward (None: never)."""
+    if args.recompute_granularity == "full":
+        return 0
+    return args.recompute_tokens
 
 
 def plan_for(args, batch, world: int, pattern: str, step: int, replays):
@@ -139,7 +152,8 @@ def main(argv=None) -> int:
         pipeline = PipelineTrainer(model, info, device, lr=args.lr, min_lr=args.min_lr,
                                    weight_decay=args.weight_decay, clip_grad=args.clip_grad,
                                    warmup_steps=args.lr_warmup_iters,
-                                   decay_steps=args.lr_decay_iters or args.train_iters, records=args.records)
+                                   decay_steps=args.lr_decay_iters or args.train_iters, records=args.records,
+                                   recompute_tokens=recompute_limit(args))
         plan_world = info.stage_world
         trainer = pipeline
     else:
@@ -155,7 +169,8 @@ def main(argv=None) -> int:
                           decay_steps=args.lr_decay_iters or args.train_iters, records=args.records,
                           overlap_grad_reduce=args.overlap_grad_reduce,
                           overlap_param_gather=args.overlap_param_gather,
-                          bucket_bytes=(args.ddp_bucket_size or (64 << 20)) * 4)
+                          bucket_bytes=(args.ddp_bucket_size or (64 << 20)) * 4,
+                          recompute_tokens=recompute_limit(args))
     replays = json.loads(Path(args.joint_replay).read_text()) if args.joint_replay else None
     start = 1
     if args.load and checkpoint.latest(args.load) is not None:
@@ -167,12 +182,28 @@ def main(argv=None) -> int:
         batch = global_batch(args, world, step, pin=cuda)
         plan = plan_for(args, batch, plan_world, cfg.pattern, step, replays)
         window.before(step)
+        t0 = time.perf_counter()
         with nvtx(f"step {step}"):
             res = trainer.train_step(batch, plan)
+        step_ms = res.elapsed_ms
+        if step_ms is None:
+            # wall time of the step on this rank (train_step reads the loss, so the device has finished),
+            # max over ranks
+            if cuda:
+                torch.cuda.synchronize(device)
+            ms = torch.tensor([(time.perf_counter() - t0) * 1000.0], dtype=torch.float64, device=device)
+            if world > 1:
+                dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            step_ms = float(ms.item())
         window.after(step)
         if rank == 0 and step % args.log_interval == 0:
-            print(json.dumps({"step": step, "loss": res.loss, "lr": res.lr, "tokens": res.tokens,
-                              "microbatches": res.microbatches}), flush=True)
+            line = {"step": step, "loss": res.loss, "lr": res.lr, "tokens": res.tokens,
+                    "microbatches": res.microbatches, "step_ms": round(step_ms, 3),
+                    "tokens_per_s": round(res.tokens / step_ms * 1000.0, 1) if step_ms else None}
+            for key in ("bubble_fraction", "exposed_p2p_ms", "compute_ms", "pipeline_stages"):
+                if key in (res.extra or {}):
+                    line[key] = res.extra[key]
+            print(json.dumps(line), flush=True)
         if args.save and args.save_interval and step % args.save_interval == 0:
             checkpoint.save(trainer, args.save, plan_cursor=step)
     if world > 1:

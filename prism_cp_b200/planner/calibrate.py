@@ -150,6 +150,40 @@ def fit_cp_overhead(model: Model, pattern: str, lengths: dict, world: int, step_
     return 0.5 * (lo + hi)
 
 
+def fit_cp_factors(model: Model, records: list[dict]) -> dict:
+    """Per operator and CP degree: measured module time over the calibrated model's price.
+
+    ``records`` are module-bench rows at CP > 1 (one sequence of ``tokens`` over a team of ``cp``
+    ranks, forward + backward, max over ranks). The factor of (operator, cp) is the median over
+    the measured lengths of ``fb_ms / predicted``, where ``predicted`` is what ``model`` (with its
+    CP = 1 calibration, without CP factors) assigns the same group; the evaluator multiplies CP
+    prices by it. This replaces a single factor fitted to whole-step times with one measured
+    anchor set per operator and degree."""
+    from dataclasses import replace
+    import statistics
+    from .joint.ir import Group, Layout
+    base = replace(model, cp_overhead=None)
+    ratios: dict = {}
+    for r in records:
+        cp, sym = int(r.get("cp", 1)), MODULES.get(r["module"])
+        if cp <= 1 or sym not in ("G", "*") or int(r.get("sequences", 1)) != 1:
+            continue
+        tokens = int(r["tokens"])
+        ev = Evaluator(base, {0: tokens}, cp, sym)
+        layout = Layout((Group(tuple(range(cp)), (0,)),), "contiguous" if sym == "G" else "zigzag")
+        predicted = ev.operator(sym, layout)[0]
+        ratios.setdefault(sym, {}).setdefault(str(cp), []).append(float(r["fb_ms"]) / predicted)
+    return {sym: {cp: statistics.median(v) for cp, v in sorted(per.items(), key=lambda kv: int(kv[0]))}
+            for sym, per in sorted(ratios.items())}
+
+
+def _records_of(path: Path) -> list[dict]:
+    data = json.loads(path.read_text())
+    if "records" in data:
+        return list(data["records"])
+    return [r for v in data.values() if isinstance(v, dict) for r in v.get("records", [])]
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--records", type=Path, required=True, help="module records (one file per module or combined)")
@@ -160,16 +194,15 @@ def main(argv=None) -> int:
     ap.add_argument("--peak-tokens", type=int, default=32768)
     ap.add_argument("--bench-steps", type=float, nargs=2, default=None, metavar=("CP1_MS", "CP2_MS"),
                     help="measured bench.py ms/step on one GPU and on two (CP = 2), 8 x 32K tokens")
+    ap.add_argument("--cp-records", type=Path, nargs="*", default=None,
+                    help="module-bench JSON files at CP > 1: per-operator, per-degree factors (replaces "
+                         "--bench-steps)")
     args = ap.parse_args(argv)
     from dataclasses import replace
     from ..models.config import PRESETS
     from .cli import B200_ENVELOPE
     from .joint.cost import model_from_config
-    data = json.loads(args.records.read_text())
-    if "records" in data:
-        records = data["records"]
-    else:
-        records = [r for v in data.values() if isinstance(v, dict) for r in v.get("records", [])]
+    records = _records_of(args.records)
     cfg = PRESETS[args.model_config]()
     model = model_from_config(cfg, B200_ENVELOPE["device_bytes"],
                               **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"})
@@ -182,7 +215,12 @@ def main(argv=None) -> int:
         out["byte_scale"] = fit_byte_scale(model, cfg.pattern, args.peak_tokens, int(args.peak_gib * 2 ** 30))
         out["byte_scale_source"] = f"measured peak_allocated {args.peak_gib} GiB, one {args.peak_tokens}-token microbatch"
         model = replace(model, byte_scale=out["byte_scale"])
-    if args.bench_steps is not None:
+    if args.cp_records:
+        cp_rows = [r for path in args.cp_records for r in _records_of(path)]
+        out["cp_overhead"] = fit_cp_factors(model, cp_rows)
+        out["cp_overhead_source"] = ("module bench at CP > 1 (one sequence over a team, forward + backward, max over "
+                                     "ranks): " + ", ".join(str(p) for p in args.cp_records))
+    elif args.bench_steps is not None:
         lengths = {i: 32768 for i in range(8)}
         out["cp_overhead"] = {"2": fit_cp_overhead(model, cfg.pattern, lengths, 2, args.bench_steps[1],
                                                    args.bench_steps[0], 32768)}

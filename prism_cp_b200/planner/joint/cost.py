@@ -165,9 +165,15 @@ def _gdn_sheet(m: Model, n: int, squares: int, nseq: int, cp: int) -> Sheet:
 SHEETS = {"M": _mlp_sheet, "*": _gqa_sheet, "G": _gdn_sheet}
 
 
-def cp_overhead_factor(table: dict, cp: int) -> float:
+def cp_overhead_factor(table: dict, cp: int, symbol: str | None = None) -> float:
     """Measured CP overhead factor for degree ``cp``: its own entry, else the largest measured
-    degree below it, else the smallest measured degree."""
+    degree below it, else the smallest measured degree. ``table`` is either one table for every
+    CP operator ({"2": f, ...}) or one per operator symbol ({"G": {"2": f}, "*": {...}}); an
+    operator without its own table gets 1."""
+    if table and all(isinstance(v, dict) for v in table.values()):
+        table = table.get(symbol) if symbol is not None else None
+        if not table:
+            return 1.0
     measured = sorted(int(k) for k in table)
     usable = [k for k in measured if k <= cp] or measured[:1]
     return float(table[str(usable[-1])])
@@ -235,7 +241,7 @@ class Evaluator:
                       sheet.comm / (m.intra_gbps * 1e6) + latency)
         ms = self.profile.price(symbol, cp, parts, tokens, squares, cross)
         if cp > 1 and symbol != "M" and m.cp_overhead:
-            ms *= cp_overhead_factor(m.cp_overhead, cp)
+            ms *= cp_overhead_factor(m.cp_overhead, cp, symbol)
         return ms
 
     @lru_cache(maxsize=4096)

@@ -42,15 +42,20 @@ def build(records: list[dict], anchor_tokens: int, model_shape, name: str = "b20
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--records", type=Path, required=True, help="module bench JSON")
+    ap.add_argument("--records", type=Path, nargs="+", required=True,
+                    help="module bench JSON files (one per module and CP degree, or combined)")
     ap.add_argument("--anchor-tokens", type=int, required=True)
     ap.add_argument("--output", type=Path, required=True)
     ap.add_argument("--name", default="b200_module_bench")
     args = ap.parse_args(argv)
-    data = json.loads(args.records.read_text())
-    records = data["records"]
-    shape = data["model_shape"]
-    prof = build(records, args.anchor_tokens, shape, args.name, str(args.records))
+    records, shape = [], None
+    for path in args.records:
+        data = json.loads(path.read_text())
+        records += data["records"]
+        if shape is not None and list(data["model_shape"]) != list(shape):
+            raise ValueError(f"{path}: measured for a different model shape")
+        shape = data["model_shape"]
+    prof = build(records, args.anchor_tokens, shape, args.name, ", ".join(str(p) for p in args.records))
     args.output.write_text(json.dumps(prof, indent=2) + "\n")
     print(json.dumps({k: prof["anchors"][k]["milliseconds"] for k in prof["anchors"]}))
 

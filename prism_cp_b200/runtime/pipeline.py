@@ -93,8 +93,10 @@ class StageTeams(Teams):
 
 class PipelineTrainer:
     def __init__(self, model, info: StageInfo, device, lr=3e-4, min_lr=3e-5, weight_decay=0.1, clip_grad=1.0,
-                 warmup_steps=0, decay_steps=1000, records: str | None = None):
+                 warmup_steps=0, decay_steps=1000, records: str | None = None, recompute_tokens: int | None = None):
         self.model, self.info, self.device = model, info, device
+        # microbatches above this many tokens on a rank recompute this stage's layers in the backward
+        self.recompute_tokens = recompute_tokens
         self.teams = StageTeams(info)
         self.cache = LayoutCache(info.stage_world, info.stage_rank, device, self.teams)
         self.flat = FlatParameters(model, info.stage_world)
@@ -137,7 +139,8 @@ class PipelineTrainer:
             inputs = self.prepare(batch, plan)
         lengths = batch.lengths
         M = len(plan.microbatches)
-        runs = [MicrobatchRun(mb, lengths, self.cache, info.first_layer, info.num_layers)
+        runs = [MicrobatchRun(mb, lengths, self.cache, info.first_layer, info.num_layers,
+                              recompute_tokens=self.recompute_tokens)
                 for mb in plan.microbatches]
         h = self.model.cfg.hidden_size
         dtype = next(self.model.parameters()).dtype

@@ -228,3 +228,36 @@ def test_calibration_cli_reproduces_the_committed_file(tmp_path):
     assert got["calibration"] == committed["calibration"]
     assert abs(got["byte_scale"] - committed["byte_scale"]) < 1e-9
     assert abs(got["cp_overhead"]["2"] - committed["cp_overhead"]["2"]) < 1e-9
+
+
+def test_cp_factors_fit_from_module_anchors():
+    """Per-operator CP factors are the measured/predicted ratio of one-sequence CP module records;
+    the evaluator then prices each operator with its own factor (and 1 without one)."""
+    from dataclasses import replace
+    from prism_cp_b200.models.config import PRESETS
+    from prism_cp_b200.planner.calibrate import calibrated, fit_cp_factors
+    from prism_cp_b200.planner.cli import B200_ENVELOPE
+    from prism_cp_b200.planner.joint.cost import Evaluator, cp_overhead_factor, model_from_config
+    from prism_cp_b200.planner.joint.ir import Group, Layout
+    cfg = PRESETS["hybrid-1.3b"]()
+    m = replace(calibrated(model_from_config(cfg, B200_ENVELOPE["device_bytes"],
+                                             **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"})),
+                cp_overhead=None)
+
+    def predicted(sym, cp, tokens):
+        lay = Layout((Group(tuple(range(cp)), (0,)),), "contiguous" if sym == "G" else "zigzag")
+        return Evaluator(m, {0: tokens}, cp, sym).operator(sym, lay)[0]
+
+    scale = {("G", 2): 1.3, ("G", 4): 1.5, ("*", 2): 1.1, ("*", 4): 1.2}
+    records = [{"module": "GDN" if s == "G" else "GQA", "cp": cp, "tokens": n, "sequences": 1,
+                "fb_ms": f * predicted(s, cp, n)} for (s, cp), f in scale.items() for n in (65536, 131072)]
+    records.append({"module": "GQA", "cp": 1, "tokens": 65536, "sequences": 1, "fb_ms": 1.0})  # ignored
+    table = fit_cp_factors(m, records)
+    for (s, cp), f in scale.items():
+        assert abs(table[s][str(cp)] - f) < 1e-9
+    assert cp_overhead_factor(table, 8, "G") == table["G"]["4"]
+    assert cp_overhead_factor(table, 2, "M") == 1.0
+    priced = replace(m, cp_overhead=table)
+    lay = Layout((Group((0, 1), (0,)),), "contiguous")
+    got = Evaluator(priced, {0: 65536}, 2, "G").operator("G", lay)[0]
+    assert abs(got - 1.3 * predicted("G", 2, 65536)) < 1e-9
