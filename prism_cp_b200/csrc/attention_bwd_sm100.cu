@@ -43,6 +43,7 @@ struct Params {
   const float* lse;  // [hq, Tq] natural log
   const float* dsum; // [hq, Tq]
   int tq;
+  int tk;            // rows of K / V / dK / dV (bounds of the debug build)
   __nv_bfloat16* out;  // dK / dV (kv kernel) or dQ (q kernel)
   __nv_bfloat16* out2;
   long out_stride;
@@ -281,7 +282,7 @@ __global__ void __launch_bounds__(KV_THREADS, 1)
         lse_src = src.lse[owner];
         dsum_src = src.dsum[owner];
       }
-      const bool v = qq < q_len;
+      const bool v = qq < q_len && PRISM_IN_BOUNDS(row, p.tq, p.status);
       l = v ? lse_src[(long)h * p.tq + row] * kLog2e : INFINITY;
       d = v ? dsum_src[(long)h * p.tq + row] : 0.f;
     };
@@ -361,7 +362,7 @@ __global__ void __launch_bounds__(KV_THREADS, 1)
     tc_fence_after();
     {
       // every thread of the warp takes part in tcgen05.ld; only rows inside the sequence store
-      const bool store = kk < k_len;
+      const bool store = kk < k_len && PRISM_IN_BOUNDS(k_seg + kk, p.tk, p.status);
       const bool loaded = __all_sync(0xffffffffu, n_it > 0 && ok);
       __nv_bfloat16* dv_row = p.out2 + (long)(k_seg + kk) * p.out_stride + (long)kv_head * D;
       __nv_bfloat16* dk_row = p.out + (long)(k_seg + kk) * p.out_stride + (long)kv_head * D;
@@ -546,7 +547,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
     const int r = threadIdx.x & 127;
     const int half = threadIdx.x >> 7;   // which 64 of the tile's 128 key columns
     const int qq = q0 + r;
-    const bool row_ok = qq < q_len;
+    const bool row_ok = qq < q_len && PRISM_IN_BOUNDS(q_seg + qq, p.tq, p.status);
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const float c_log2 = p.scale * kLog2e;
     const float lse2 = row_ok ? p.lse[(long)head * p.tq + q_seg + qq] * kLog2e : INFINITY;
@@ -686,6 +687,7 @@ void attention_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Ten
   p.lse = lse.data_ptr<float>();
   p.dsum = dsum.data_ptr<float>();
   p.tq = Tq;
+  p.tk = k.size(0);
   p.status = status.data_ptr<int>();
   static bool configured = false;
   if (!configured) {
@@ -749,6 +751,7 @@ void attention_bwd_peer(const std::vector<at::Tensor>& q_peers, const std::vecto
   p.lse = lse_peers[rank].data_ptr<float>();
   p.dsum = dsum_peers[rank].data_ptr<float>();
   p.tq = Tq;
+  p.tk = k_peers[rank].size(0);
   p.status = status.data_ptr<int>();
   p.tiles = tiles.data_ptr<int>();
   static bool configured = false;

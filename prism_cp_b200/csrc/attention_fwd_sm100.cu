@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (ok && n_kv > 0) ok = mbar_wait_bounded(pv_done, (n_kv - 1) & 1, abort_flag, p.status, kTimeoutEpilogue);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    const bool row_valid = q_idx < q_len;
+    const bool row_valid = q_idx < q_len && PRISM_IN_BOUNDS(q_seg + q_idx, p.tq, p.status);
     const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
     __nv_bfloat16* orow = p.out + (long)(q_seg + q_idx) * p.out_stride + (long)head * D;
 #pragma unroll

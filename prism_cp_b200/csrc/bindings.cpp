@@ -76,7 +76,8 @@ at::Tensor symm_handle(int64_t ptr);
 int64_t symm_open(const at::Tensor& handle);
 void symm_close(int64_t ptr);
 void symm_signal(const at::Tensor& peer_signal_bases, int64_t slot, int64_t value);
-void symm_wait(int64_t my_signal_base, int64_t first, int64_t count, int64_t value, at::Tensor& status);
+void symm_wait(int64_t my_signal_base, int64_t first, int64_t count, int64_t value, at::Tensor& status,
+               int64_t limit_ns);
 void symm_gather_rows(const at::Tensor& peer_bases, const at::Tensor& routes, const at::Tensor& block_route,
                       const at::Tensor& block_row0, int64_t rows_per_block, int64_t row_bytes, at::Tensor& dst,
                       at::Tensor& status);

@@ -23,6 +23,7 @@ enum ErrorCode : int {
   kTimeoutEpilogue = 3,
   kTimeoutPeer = 4,
   kBadShape = 5,
+  kOutOfBounds = 6,  // debug build: an index from a host-built table fell outside its extent
 };
 
 // A wait gives up after this many nanoseconds of %globaltimer (about 2 s);
@@ -42,6 +43,24 @@ PRISM_DEVICE uint32_t smem_u32(const void* p) {
 PRISM_DEVICE void record_error(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }
+
+// ---------------------------------------------------------------- debug bounds checks
+// The debug build (-DPRISM_BOUNDS_CHECK, `python -m prism_cp_b200.csrc.build --debug`, loaded with
+// PRISM_KERNEL_DEBUG=1) compares the indices that come from host-built tables (sequence offsets,
+// tile lists, route tables) with the extent they address before the access: a bad index records
+// kOutOfBounds in the status word and the access is skipped, so it shows up as an error code instead
+// of a memory fault. In the release build PRISM_IN_BOUNDS is the constant true.
+PRISM_DEVICE bool index_in_bounds(long long idx, long long extent, int* status) {
+  if (idx >= 0 && idx < extent) return true;
+  record_error(status, kOutOfBounds);
+  return false;
+}
+#ifdef PRISM_BOUNDS_CHECK
+#define PRISM_IN_BOUNDS(idx, extent, status) \
+  ::prism::index_in_bounds((long long)(idx), (long long)(extent), (status))
+#else
+#define PRISM_IN_BOUNDS(idx, extent, status) true
+#endif
 
 // ---------------------------------------------------------------- peer flags
 // 64-bit sequence words in (possibly peer) global memory: writers publish with a

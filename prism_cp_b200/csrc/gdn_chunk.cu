@@ -445,6 +445,7 @@ struct StateParams {
   __nv_bfloat16* states;   // fwd: S_c^T; bwd: G_{c+1}^T          [Nc, H, DV, DK] (fwd nullable)
   __nv_bfloat16* rows;     // fwd: Delta_c^T; bwd: dDelta_c^T     [Nc, H, DV, C]  (fwd nullable)
   __nv_bfloat16* out;      // fwd: o [T, H, DV] (nullable)
+  int T;                   // rows of `out` (bounds of the debug build)
   int H, DV;
   int* status;
 };
@@ -637,7 +638,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
       tmem_wait_ld();
 #pragma unroll
       for (int i = 0; i < 32; ++i)
-        if (i < n) p.out[((long)(t0 + i) * H + h) * DV + v] = __float2bfloat16(__uint_as_float(r0[i]));
+        if (i < n && PRISM_IN_BOUNDS(t0 + i, p.T, p.status))
+          p.out[((long)(t0 + i) * H + h) * DV + v] = __float2bfloat16(__uint_as_float(r0[i]));
     };
 
 #pragma unroll 1
@@ -1905,6 +1907,7 @@ void gdn_chunk_fwd(const at::Tensor& Wn, const at::Tensor& U, const at::Tensor& 
   p.rows = rows.has_value() && rows->defined() ? reinterpret_cast<__nv_bfloat16*>(rows->data_ptr()) : nullptr;
   p.out = out.has_value() && out->defined() ? reinterpret_cast<__nv_bfloat16*>(out->data_ptr()) : nullptr;
   if (p.out != nullptr) check_bf16(*out, "out");
+  p.T = p.out != nullptr ? (int)out->size(0) : 0;
   p.H = H;
   p.DV = DV;
   p.status = status.data_ptr<int>();

@@ -7,7 +7,7 @@
 //    loads and stores.
 //  * Signals: a small region of each heap holds 64-bit sequence words. A writer
 //    publishes with a system-scope release store to the peer's word; a reader
-//    spins with acquire loads for at most kPeerWaitNs and returns an error
+//    spins with acquire loads for at most a given limit and returns an error
 //    status instead of hanging if the peer never arrives.
 //  * p2p_gather_rows: the CP-transition reshard as one kernel - every
 //    destination row block is copied straight from the owning peer's heap
@@ -23,14 +23,12 @@
 namespace prism {
 namespace symm {
 
-constexpr uint64_t kPeerWaitNs = 2000000000ull;  // 2 s
-
-// Spin until *flag >= target; false (and an error code) after kPeerWaitNs.
-__device__ __forceinline__ bool wait_flag(const uint64_t* flag, uint64_t target, int* status) {
+// Spin until *flag >= target; false (and an error code) after limit_ns of %globaltimer.
+__device__ __forceinline__ bool wait_flag(const uint64_t* flag, uint64_t target, int* status, uint64_t limit_ns) {
   if (ld_acquire_sys(flag) >= target) return true;
   const uint64_t t0 = globaltimer();
   while (ld_acquire_sys(flag) < target) {
-    if (globaltimer() - t0 > kPeerWaitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       record_error(status, kTimeoutPeer);
       return false;
     }
@@ -49,9 +47,10 @@ __global__ void signal_all_kernel(const int64_t* peer_signal_bases, int world, i
 }
 
 // Wait until signal slots [first, first + count) of MY heap reach `value`.
-__global__ void wait_all_kernel(const uint64_t* my_signals, int first, int count, uint64_t value, int* status) {
+__global__ void wait_all_kernel(const uint64_t* my_signals, int first, int count, uint64_t value, int* status,
+                                uint64_t limit_ns) {
   const int i = threadIdx.x;
-  if (i < count) wait_flag(my_signals + first + i, value, status);
+  if (i < count) wait_flag(my_signals + first + i, value, status, limit_ns);
 }
 
 // Route entry: copy `rows` rows from peer `src` (heap byte offset src_off) to
@@ -63,15 +62,20 @@ struct RouteEntry {
   int64_t rows;
 };
 
-__global__ void gather_rows_kernel(const int64_t* peer_bases, const RouteEntry* routes, int n_routes,
+__global__ void gather_rows_kernel(const int64_t* peer_bases, int world, const RouteEntry* routes, int n_routes,
                                    const int64_t* block_route, const int64_t* block_row0, int rows_per_block,
-                                   int64_t row_bytes, uint8_t* dst, int* status) {
+                                   int64_t row_bytes, uint8_t* dst, int64_t dst_bytes, int* status) {
   // a bounded wait before this launch gave up (peer missing or late): copy nothing rather than rows a
   // peer may not have finished writing; the host sees the status at its next check
   if (*reinterpret_cast<volatile int*>(status) != 0) return;
-  const RouteEntry e = routes[block_route[blockIdx.x]];
+  const int64_t ri = block_route[blockIdx.x];
+  if (!PRISM_IN_BOUNDS(ri, n_routes, status)) return;
+  const RouteEntry e = routes[ri];
   const int64_t r0 = block_row0[blockIdx.x];
   const int64_t r1 = min(e.rows, r0 + rows_per_block);
+  if (!PRISM_IN_BOUNDS(e.src_rank, world, status) || !PRISM_IN_BOUNDS(r0, e.rows, status) ||
+      !PRISM_IN_BOUNDS(e.dst_off + r1 * row_bytes - 1, dst_bytes, status))
+    return;
   // the block's rows are contiguous on both sides: copy them as one run of 16-byte vectors, four
   // independent loads in flight per thread (NVLink reads have a long latency)
   const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(peer_bases[e.src_rank]) +
@@ -129,11 +133,14 @@ void symm_signal(const at::Tensor& peer_signal_bases, int64_t slot, int64_t valu
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void symm_wait(int64_t my_signal_base, int64_t first, int64_t count, int64_t value, at::Tensor& status) {
+// limit_ns: how long a missing peer is waited for before the error status is set (bounded, > 0).
+void symm_wait(int64_t my_signal_base, int64_t first, int64_t count, int64_t value, at::Tensor& status,
+               int64_t limit_ns) {
   TORCH_CHECK(count <= 32, "symm_wait: at most 32 slots");
+  TORCH_CHECK(limit_ns > 0, "symm_wait: the wait needs a positive limit");
   symm::wait_all_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const uint64_t*>(my_signal_base), (int)first, (int)count, (uint64_t)value,
-      status.data_ptr<int>());
+      status.data_ptr<int>(), (uint64_t)limit_ns);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -147,9 +154,10 @@ void symm_gather_rows(const at::Tensor& peer_bases, const at::Tensor& routes, co
   if (blocks == 0) return;
   const c10::cuda::CUDAGuard guard(dst.device());
   symm::gather_rows_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      peer_bases.data_ptr<int64_t>(), reinterpret_cast<const symm::RouteEntry*>(routes.data_ptr<int64_t>()),
-      routes.size(0), block_route.data_ptr<int64_t>(), block_row0.data_ptr<int64_t>(), (int)rows_per_block,
-      row_bytes, reinterpret_cast<uint8_t*>(dst.data_ptr()), status.data_ptr<int>());
+      peer_bases.data_ptr<int64_t>(), (int)peer_bases.numel(),
+      reinterpret_cast<const symm::RouteEntry*>(routes.data_ptr<int64_t>()), routes.size(0),
+      block_route.data_ptr<int64_t>(), block_row0.data_ptr<int64_t>(), (int)rows_per_block, row_bytes,
+      reinterpret_cast<uint8_t*>(dst.data_ptr()), (int64_t)dst.nbytes(), status.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

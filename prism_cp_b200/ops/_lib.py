@@ -10,8 +10,12 @@ from __future__ import annotations
 
 import functools
 import importlib
+import os
 
 import torch
+
+# PRISM_KERNEL_DEBUG=1: load the bounds-checked build (``python -m prism_cp_b200.csrc.build --debug``)
+DEBUG = os.environ.get("PRISM_KERNEL_DEBUG", "0") == "1"
 
 
 class KernelLibraryMissing(RuntimeError):
@@ -20,11 +24,12 @@ class KernelLibraryMissing(RuntimeError):
 
 @functools.lru_cache(maxsize=1)
 def lib():
+    name, flag = ("_C_debug", " --debug") if DEBUG else ("_C", "")
     try:
-        return importlib.import_module("prism_cp_b200._C")
+        return importlib.import_module(f"prism_cp_b200.{name}")
     except ImportError as error:  # pragma: no cover - exercised on GPU hosts only
         raise KernelLibraryMissing(
-            "prism_cp_b200._C is not built; run `python -m prism_cp_b200.csrc.build` "
+            f"prism_cp_b200.{name} is not built; run `python -m prism_cp_b200.csrc.build{flag}` "
             "(CUDA ops never fall back to PyTorch)") from error
 
 
@@ -46,6 +51,8 @@ def check_status(device: torch.device) -> None:
     code = int(status(device).item())
     if code:
         status(device).zero_()
+        if code == 6:
+            raise RuntimeError("a prism kernel found an index outside its extent (debug build, code 6)")
         raise RuntimeError(f"device wait timed out in a prism kernel (code {code})")
 
 

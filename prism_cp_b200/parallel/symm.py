@@ -18,6 +18,8 @@ a half after every peer has signalled that it finished reading it.
 
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -25,11 +27,15 @@ from ..ops._lib import lib, status
 
 SIGNAL_SLOTS = 256
 READY, DONE = 0, 64      # slot bases: READY + src_rank, DONE + src_rank
+# how long a signal wait tolerates a late peer before it records an error (bounded; a rank that is
+# seconds behind its peers inside one step is a fault, not load imbalance)
+PEER_WAIT_NS = int(float(os.environ.get("PRISM_PEER_WAIT_S", "20")) * 1e9)
 
 
 class SymmetricHeap:
-    def __init__(self, group, nbytes: int, device: torch.device):
+    def __init__(self, group, nbytes: int, device: torch.device, wait_ns: int | None = None):
         self.group = group
+        self.wait_ns = PEER_WAIT_NS if wait_ns is None else int(wait_ns)
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.nbytes = (nbytes + 255) // 256 * 256
@@ -59,7 +65,7 @@ class SymmetricHeap:
         lib().symm_signal(self.signal_dev, slot, value)
 
     def wait(self, first: int, count: int, value: int):
-        lib().symm_wait(self.my_signals, first, count, value, status(self.device))
+        lib().symm_wait(self.my_signals, first, count, value, status(self.device), self.wait_ns)
 
     def close(self):
         L = lib()
@@ -70,8 +76,7 @@ class SymmetricHeap:
 
 
 class _CompiledP2PRoute:
-    def __init__(self, edges, rank: int, row_bytes: int, rows_per_block: int, device, half_bytes: int,
-                 send_rows_by_rank):
+    def __init__(self, edges, rank: int, row_bytes: int, rows_per_block: int, device, send_rows_by_rank):
         # the sender stages its outgoing rows in source-offset order; offsets of
         # each sender's rows inside its staging area are known to every rank
         routes, block_route, block_row0 = [], [], []
@@ -104,28 +109,53 @@ def staging_offsets(edges, world: int):
 
 
 class P2PTransport:
-    """Reshard rows between two layouts with P2P loads over NVLink (no NCCL)."""
+    """Reshard rows between two layouts with P2P loads over NVLink (no NCCL).
 
-    def __init__(self, heap: SymmetricHeap, rows_per_block: int = 64):
+    The staging heap is allocated on first use and regrown (after a barrier of the group) when a
+    route needs more than half of it; the size comes from the global route (the largest number of
+    rows any rank sends), so every rank makes the same decision at the same call."""
+
+    def __init__(self, heap: SymmetricHeap | None = None, rows_per_block: int = 64, group=None,
+                 device: torch.device | None = None, min_bytes: int = 256 << 20):
         self.heap = heap
+        self.group = heap.group if heap is not None else group
+        self.device = heap.device if heap is not None else device
         self.rows_per_block = rows_per_block
-        self.half = heap.nbytes // 2
+        self.min_bytes = min_bytes
+        self.half = heap.nbytes // 2 if heap is not None else 0
         self._routes: dict = {}  # (edges, row bytes) -> compiled block tables, built once per route
 
+    def _ensure(self, need: int) -> SymmetricHeap:
+        if self.heap is None or need > self.half:
+            if self.heap is not None:
+                dist.barrier(group=self.group)
+                self.heap.close()
+            self.heap = SymmetricHeap(self.group, max(2 * need, self.min_bytes), self.device)
+            self.half = self.heap.nbytes // 2
+        return self.heap
+
+    def close(self):
+        if self.heap is not None:
+            self.heap.close()
+            self.heap = None
+
     def exchange(self, x: torch.Tensor, edges) -> torch.Tensor:
-        heap = self.heap
         row_bytes = x[0].numel() * x.element_size() if x.shape[0] else 0
+        world = dist.get_world_size(self.group)
+        rank = dist.get_rank(self.group)
         key = (edges, row_bytes)
         r = self._routes.get(key)
         if r is None:
-            r = _CompiledP2PRoute(edges, heap.rank, row_bytes, self.rows_per_block, x.device, self.half,
-                                  staging_offsets(edges, heap.world))
+            r = _CompiledP2PRoute(edges, rank, row_bytes, self.rows_per_block, x.device,
+                                  staging_offsets(edges, world))
+            sent = [0] * world
+            for s_, _, _, _, n in edges:
+                sent[s_] += n
+            r.max_stage_bytes = max(1, max(sent)) * row_bytes
             if len(self._routes) >= 512:
                 self._routes.clear()
             self._routes[key] = r
-        need = max(1, r.send_index.numel()) * row_bytes
-        if need > self.half:
-            raise ValueError(f"reshard needs {need} staging bytes, heap half is {self.half}")
+        heap = self._ensure(r.max_stage_bytes)
         heap.seq += 1
         seq = heap.seq
         parity = seq % 2

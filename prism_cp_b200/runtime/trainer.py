@@ -32,6 +32,8 @@ from ..utils.tracing import nvtx
 
 
 DEBUG_SYNC = os.environ.get("PRISM_DEBUG_SYNC", "0") in ("1", "2")
+# transport of the CP-transition reshard on CUDA: "p2p" (gather over NVLink, default) or "nccl" (all-to-all)
+RESHARD = os.environ.get("PRISM_RESHARD", "p2p")
 
 
 def hbm_budget(total_bytes: int) -> int:
@@ -74,6 +76,12 @@ class Trainer:
                                           warmup_steps=warmup_steps, decay_steps=decay_steps, world=self.world,
                                           tp_group=self.tp.group if self.tp is not None else None)
         self.overlap = self.optimizer.enable_overlap() if overlap_grad_reduce else None
+        if device.type == "cuda" and self.world > 1 and self.tp is None and RESHARD == "p2p":
+            # CP-transition reshards pull their rows over NVLink from a symmetric heap (one gather
+            # kernel per reshard) instead of an NCCL all-to-all
+            from ..parallel import transport
+            from ..parallel.symm import P2PTransport
+            transport.use_p2p(P2PTransport(group=teams.world_group, device=device))
         self.param_gather = self.optimizer.enable_param_gather_overlap(model) if overlap_param_gather else None
         self.cache = LayoutCache(self.world, self.rank, device, teams)
         self.hbm_guard = hbm_guard and device.type == "cuda"

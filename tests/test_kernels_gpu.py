@@ -404,10 +404,10 @@ def test_a_device_wait_that_runs_out_reports_an_error_and_the_context_survives()
     flags = torch.zeros(8, dtype=torch.int64, device=dev)
     torch.cuda.synchronize()
     t0 = time.monotonic()
-    lib().symm_wait(flags.data_ptr(), 0, 1, 1, status(dev))
+    lib().symm_wait(flags.data_ptr(), 0, 1, 1, status(dev), 1_000_000_000)  # a flag nothing sets: 1 s limit
     torch.cuda.synchronize()
     waited = time.monotonic() - t0
-    assert 1.5 < waited < 60, waited
+    assert 0.8 < waited < 60, waited
     # a gather queued behind the failed wait copies nothing (no stale rows reach the output)
     src = torch.arange(64 * 8, dtype=torch.float32, device=dev).view(64, 8)
     dst = torch.full((64, 8), -1.0, device=dev)
