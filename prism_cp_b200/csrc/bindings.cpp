@@ -59,7 +59,7 @@ std::vector<at::Tensor> gdn_chunk_bwd_local(const at::Tensor& q, const at::Tenso
                                             const at::Tensor& states,
                                             const at::Tensor& dstates, const at::Tensor& rows,
                                             const at::Tensor& drows, const at::Tensor& dout, double scale,
-                                            at::Tensor& status);
+                                            at::Tensor& status, const std::vector<at::Tensor>& second);
 void attention_fwd_peer(const at::Tensor& q, const std::vector<at::Tensor>& k_peers,
                         const std::vector<at::Tensor>& v_peers, const at::Tensor& tiles, const at::Tensor& seq_n,
                         const at::Tensor& seq_row0, at::Tensor& out, at::Tensor& lse, double softmax_scale,

@@ -752,11 +752,30 @@ struct DvParams {
   float* dQgT;   // [Nc, H, DK, C]   dQg^T
   float* dKdT;   // [Nc, H, DK, C]   dKd^T
   float* dAqk;   // [Nc, H, C, C]
-  float* dDV;    // [Nc, H, C, C]    dDelta V^T
+  float* dDV;    // [Nc, H, C, C]    dDelta V^T (nullable: not computed)
   float* dgam;   // [Nc, H]
   int H, DV;
   int* status;
+  int accumulate;  // add to the outputs instead of writing them (a second state pass over the same chunks)
 };
+
+// 16 fp32 values of one TMEM row half (r0: columns 0..31 of the pair, r1: 32..63) into dst[0..16)
+PRISM_DEVICE void put_row64(float4* dst, const uint32_t* r0, const uint32_t* r1, bool acc) {
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    float4 a = make_float4(__uint_as_float(r0[4 * m]), __uint_as_float(r0[4 * m + 1]),
+                           __uint_as_float(r0[4 * m + 2]), __uint_as_float(r0[4 * m + 3]));
+    float4 b = make_float4(__uint_as_float(r1[4 * m]), __uint_as_float(r1[4 * m + 1]),
+                           __uint_as_float(r1[4 * m + 2]), __uint_as_float(r1[4 * m + 3]));
+    if (acc) {
+      const float4 x = dst[m], y = dst[m + 8];
+      a = make_float4(a.x + x.x, a.y + x.y, a.z + x.z, a.w + x.w);
+      b = make_float4(b.x + y.x, b.y + y.y, b.z + y.z, b.w + y.w);
+    }
+    dst[m] = a;
+    dst[m + 8] = b;
+  }
+}
 
 // Tile order in shared memory (bytes, DV = value width):
 //   S^T [DV x DK] | G^T [DV x DK] | dO [C x DV] | dDelta^T [DV x C] | Delta^T [DV x C]
@@ -836,7 +855,7 @@ __global__ void __launch_bounds__(DV_THREADS, 1)
       }
       umma_commit(mma_a);
       ok = mbar_wait_bounded(mma_a, 0, nullptr, p.status, kTimeoutMma);
-      if (ok) {
+      if (ok && p.dDV != nullptr) {
         // the value tile replaces dO
         mbar_arrive_expect_tx(full_b, DV * 128);
         for (int rb = 0; rb < nb; ++rb) tma_load_2d(smem + OFF_DO + rb * BLK, &mV, full_b, h * DV + rb * 64, tr);
@@ -876,28 +895,14 @@ __global__ void __launch_bounds__(DV_THREADS, 1)
       tmem_ld_32x32b_x32(tl + cols[o], r0);
       tmem_ld_32x32b_x32(tl + cols[o] + 32, r1);
       tmem_wait_ld();
-      float4* dst = reinterpret_cast<float4*>(outs[o] + (ch * DK + r) * C);
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        dst[m] = make_float4(__uint_as_float(r0[4 * m]), __uint_as_float(r0[4 * m + 1]),
-                             __uint_as_float(r0[4 * m + 2]), __uint_as_float(r0[4 * m + 3]));
-        dst[m + 8] = make_float4(__uint_as_float(r1[4 * m]), __uint_as_float(r1[4 * m + 1]),
-                                 __uint_as_float(r1[4 * m + 2]), __uint_as_float(r1[4 * m + 3]));
-      }
+      put_row64(reinterpret_cast<float4*>(outs[o] + (ch * DK + r) * C), r0, r1, p.accumulate);
     }
     if (warp < 2) {
       uint32_t r0[32], r1[32];
       tmem_ld_32x32b_x32(tl + 128, r0);
       tmem_ld_32x32b_x32(tl + 160, r1);
       tmem_wait_ld();
-      float4* dst = reinterpret_cast<float4*>(p.dAqk + (ch * C + r) * C);
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        dst[m] = make_float4(__uint_as_float(r0[4 * m]), __uint_as_float(r0[4 * m + 1]),
-                             __uint_as_float(r0[4 * m + 2]), __uint_as_float(r0[4 * m + 3]));
-        dst[m + 8] = make_float4(__uint_as_float(r1[4 * m]), __uint_as_float(r1[4 * m + 1]),
-                                 __uint_as_float(r1[4 * m + 2]), __uint_as_float(r1[4 * m + 3]));
-      }
+      put_row64(reinterpret_cast<float4*>(p.dAqk + (ch * C + r) * C), r0, r1, p.accumulate);
     }
     {
       // diagonal element (r, r) of S G^T: columns 256 + 32 * warp .. + 31 hold it at index lane
@@ -911,25 +916,19 @@ __global__ void __launch_bounds__(DV_THREADS, 1)
     }
   }
   if (lane == 0) red[warp] = gsum;
-  const bool ok_b = ok_a && __all_sync(0xffffffffu, mbar_wait_bounded(mma_b, 0, nullptr, p.status, kTimeoutEpilogue));
+  const bool ok_b = ok_a && p.dDV != nullptr &&
+                    __all_sync(0xffffffffu, mbar_wait_bounded(mma_b, 0, nullptr, p.status, kTimeoutEpilogue));
   if (ok_b && warp < 2) {
     tc_fence_after();
     uint32_t r0[32], r1[32];
     tmem_ld_32x32b_x32(tl + 384, r0);
     tmem_ld_32x32b_x32(tl + 416, r1);
     tmem_wait_ld();
-    float4* dst = reinterpret_cast<float4*>(p.dDV + (ch * C + r) * C);
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      dst[m] = make_float4(__uint_as_float(r0[4 * m]), __uint_as_float(r0[4 * m + 1]),
-                           __uint_as_float(r0[4 * m + 2]), __uint_as_float(r0[4 * m + 3]));
-      dst[m + 8] = make_float4(__uint_as_float(r1[4 * m]), __uint_as_float(r1[4 * m + 1]),
-                               __uint_as_float(r1[4 * m + 2]), __uint_as_float(r1[4 * m + 3]));
-    }
+    put_row64(reinterpret_cast<float4*>(p.dDV + (ch * C + r) * C), r0, r1, p.accumulate);
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) p.dgam[ch] = red[0] + red[1] + red[2] + red[3];
+  if (threadIdx.x == 0) p.dgam[ch] = (p.accumulate ? p.dgam[ch] : 0.f) + red[0] + red[1] + red[2] + red[3];
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, DV_TMEM_COLS);
@@ -1956,13 +1955,16 @@ bool gdn_local_tc_enabled(int64_t set) {
 }
 
 // Chunk-local backward: dv-contractions on tcgen05, then the WY/decay backward.
+// `second` (optional): {states, dstates, rows, drows, dout} of a second state pass with zero values
+// over the first states.size(0) chunks (the same prep, dv = dk): its contractions are added to the
+// first pass's before the local backward (it adds nothing through the values, which are zero).
 std::vector<at::Tensor> gdn_chunk_bwd_local(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                             const at::Tensor& g, const at::Tensor& beta, const at::Tensor& tok0,
                                             const at::Tensor& len, const at::Tensor& Gc, const at::Tensor& aux,
                                             const at::Tensor& states,
                                             const at::Tensor& dstates, const at::Tensor& rows,
                                             const at::Tensor& drows, const at::Tensor& dout, double scale,
-                                            at::Tensor& status) {
+                                            at::Tensor& status, const std::vector<at::Tensor>& second) {
   using namespace gdnc;
   const int Nc = tok0.numel(), H = q.size(1), DV = v.size(2);
   const c10::cuda::CUDAGuard guard(q.device());
@@ -1979,7 +1981,7 @@ std::vector<at::Tensor> gdn_chunk_bwd_local(const at::Tensor& q, const at::Tenso
   CUtensorMap mDO = map2d(dout, dout.size(0), (int64_t)H * DV, (int64_t)H * DV);
   CUtensorMap mV = map2d(v, v.size(0), (int64_t)H * DV, (int64_t)H * DV);
   DvParams dp{tok0.data_ptr<int>(), dWnT.data_ptr<float>(), dQgT.data_ptr<float>(), dKdT.data_ptr<float>(),
-              dAqk.data_ptr<float>(), dDV.data_ptr<float>(), dgam.data_ptr<float>(), H, DV, status.data_ptr<int>()};
+              dAqk.data_ptr<float>(), dDV.data_ptr<float>(), dgam.data_ptr<float>(), H, DV, status.data_ptr<int>(), 0};
   const int dv_smem = DV * 896 + 128 + 1024;
   static int attr_dv = 0;
   if (attr_dv < dv_smem) {
@@ -1989,6 +1991,29 @@ std::vector<at::Tensor> gdn_chunk_bwd_local(const at::Tensor& q, const at::Tenso
   auto stream = at::cuda::getCurrentCUDAStream();
   gdn_bwd_dv_kernel<<<Nc * H, DV_THREADS, dv_smem, stream>>>(mS, mG, mDO, mDD, mDL, mV, dp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (!second.empty()) {
+    TORCH_CHECK(second.size() == 5, "gdn_chunk_bwd_local: second pass = {states, dstates, rows, drows, dout}");
+    const at::Tensor &s2 = second[0], &g2 = second[1], &r2 = second[2], &dr2 = second[3], &do2 = second[4];
+    check_bf16(do2, "second dout");
+    const int Nc2 = s2.size(0), DV2 = s2.size(2);
+    TORCH_CHECK(Nc2 <= Nc && s2.size(1) == H && DV2 == DK && do2.size(2) == DV2,
+                "gdn_chunk_bwd_local: the second pass covers the first chunks with dv = dk");
+    const int64_t srows2 = (int64_t)Nc2 * H * DV2;
+    CUtensorMap mS2 = map2d(s2, srows2, DK, DK), mG2 = map2d(g2, srows2, DK, DK);
+    CUtensorMap mDL2 = map2d(r2, srows2, C, C), mDD2 = map2d(dr2, srows2, C, C);
+    CUtensorMap mDO2 = map2d(do2, do2.size(0), (int64_t)H * DV2, (int64_t)H * DV2);
+    DvParams dp2 = dp;
+    dp2.DV = DV2;
+    dp2.dDV = nullptr;  // dDelta V^T with zero values
+    dp2.accumulate = 1;
+    const int dv_smem2 = DV2 * 896 + 128 + 1024;
+    if (attr_dv < dv_smem2) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(gdn_bwd_dv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dv_smem2));
+      attr_dv = dv_smem2;
+    }
+    gdn_bwd_dv_kernel<<<Nc2 * H, DV_THREADS, dv_smem2, stream>>>(mS2, mG2, mDO2, mDD2, mDL2, mDO2, dp2);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
   LocalArgs la{reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k.data_ptr()),
                reinterpret_cast<const __nv_bfloat16*>(v.data_ptr()), g.data_ptr<float>(), beta.data_ptr<float>(),
                tok0.data_ptr<int>(), len.data_ptr<int>(), Gc.data_ptr<float>(), aux.data_ptr<float>(),

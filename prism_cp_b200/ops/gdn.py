@@ -341,9 +341,107 @@ class _FusedChunkRule(torch.autograd.Function):
         watchdog.beat("gdn backward reverse state pass")
         main.wait_stream(side)
         dq, dk, dv, dg, dbeta = L.gdn_chunk_bwd_local(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, Gc, aux, states,
-                                                      dstates, rows, drows, dob, ctx.scale, st)
+                                                      dstates, rows, drows, dob, ctx.scale, st, [])
         tq, tk, tv, tg, tb = ctx.dtypes
         return dq.to(tq), dk.to(tk), dv.to(tv), dg.to(tg), dbeta.to(tb), None, None, dS0, None
+
+
+class _FusedAffineRule(torch.autograd.Function):
+    """The zero-start recurrence of every segment plus the linear part of the first segment, on one prep.
+
+    Outputs ``(o, S_final, L, M)``: ``o`` and ``S_final`` as ``_FusedChunkRule`` with no initial state;
+    ``L`` [n0, H, dk] and ``M`` [H, dk, dk] are the outputs and the final state of the first segment's
+    recurrence with zero values started from the identity (o_t += L_t S_in and S_out += M S_in for an
+    incoming state S_in). Both state passes read the same prep (W, Kd, Qg, Aqk, decays do not depend
+    on the values); the identity pass runs on a second stream next to the main one, forward and
+    backward, and its dv contractions are added to the main pass's before the one local backward.
+    """
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, layout, first, scale):
+        L_ = lib()
+        bf = torch.bfloat16
+        qb, kb, vb = (t.to(bf).contiguous() for t in (q, k, v))
+        gf, bt = g.float().contiguous(), beta.float().contiguous()
+        st = status(q.device)
+        Wn, U, Kd, Qg, Aqk, gam, Gc, aux = L_.gdn_chunk_prep(qb, kb, vb, gf, bt, layout.tok0_dev, layout.len_dev,
+                                                             scale, True, st)
+        T, H, DV = vb.shape
+        DK = qb.shape[-1]
+        Nc, nc0, n0 = Wn.shape[0], first.num_chunks, first.lengths[0]
+        dev = q.device
+        o = torch.empty_like(vb)
+        S_final = torch.empty((len(layout.lengths), H, DK, DV), dtype=torch.float32, device=dev)
+        states = torch.empty((Nc, H, DV, DK), dtype=bf, device=dev)
+        rows = torch.empty((Nc, H, DV, CHUNK), dtype=bf, device=dev)
+        main = torch.cuda.current_stream(dev)
+        side = _side_stream(dev)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            eye = torch.eye(DK, dtype=torch.float32, device=dev).expand(1, H, DK, DK).contiguous()
+            U0 = torch.zeros((nc0, H, CHUNK, DK), dtype=bf, device=dev)
+            Lo = torch.empty((n0, H, DK), dtype=bf, device=dev)
+            M = torch.empty((1, H, DK, DK), dtype=torch.float32, device=dev)
+            states2 = torch.empty((nc0, H, DK, DK), dtype=bf, device=dev)
+            rows2 = torch.empty((nc0, H, DK, CHUNK), dtype=bf, device=dev)
+            L_.gdn_chunk_fwd(Wn[:nc0], U0, Kd[:nc0], Qg[:nc0], Aqk[:nc0], gam[:nc0], first.tok0_dev, first.len_dev,
+                             first.seq_chunks_dev, eye, Lo, M, states2, rows2, st)
+        L_.gdn_chunk_fwd(Wn, U, Kd, Qg, Aqk, gam, layout.tok0_dev, layout.len_dev, layout.seq_chunks_dev, None, o,
+                         S_final, states, rows, st)
+        main.wait_stream(side)
+        for t in (Wn, Kd, Qg, Aqk, gam):
+            t.record_stream(side)
+        for t in (Lo, M, states2, rows2):
+            t.record_stream(main)
+        ctx.save_for_backward(qb, kb, vb, gf, bt, Wn, Kd, Qg, Aqk, gam, Gc, aux, states, rows, states2, rows2)
+        ctx.layout, ctx.first, ctx.scale = layout, first, scale
+        ctx.dtypes = (q.dtype, k.dtype, v.dtype, g.dtype, beta.dtype)
+        return o.to(v.dtype), S_final, Lo, M[0]
+
+    @staticmethod
+    def backward(ctx, do, dS_final, dLo, dM):
+        L_ = lib()
+        lay, first = ctx.layout, ctx.first
+        (qb, kb, vb, gf, bt, Wn, Kd, Qg, Aqk, gam, Gc, aux, states, rows, states2, rows2) = ctx.saved_tensors
+        st = status(qb.device)
+        dev = qb.device
+        nc0 = first.num_chunks
+        bf = torch.bfloat16
+        dob = (do if do is not None else torch.zeros_like(vb)).to(bf).contiguous()
+        dsf = dS_final.float().contiguous() if dS_final is not None else None
+        dL = (dLo if dLo is not None else torch.zeros((first.lengths[0],) + tuple(qb.shape[1:]),
+                                                      dtype=bf, device=dev)).to(bf).contiguous()
+        dMf = dM.float().contiguous()[None] if dM is not None else None
+        main = torch.cuda.current_stream(dev)
+        side = _side_stream(dev)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            dstates2, drows2 = torch.empty_like(states2), torch.empty_like(rows2)
+            L_.gdn_chunk_bwd_state(Wn[:nc0], Kd[:nc0], Qg[:nc0], Aqk[:nc0], gam[:nc0], dL, first.tok0_dev,
+                                   first.len_dev, first.seq_chunks_dev, dMf, None, dstates2, drows2, st)
+        dstates, drows = torch.empty_like(states), torch.empty_like(rows)
+        L_.gdn_chunk_bwd_state(Wn, Kd, Qg, Aqk, gam, dob, lay.tok0_dev, lay.len_dev, lay.seq_chunks_dev, dsf, None,
+                               dstates, drows, st)
+        main.wait_stream(side)
+        for t in (dstates2, drows2):
+            t.record_stream(main)
+        for t in (Wn, Kd, Qg, Aqk, gam, states2, dL) + ((dMf,) if dMf is not None else ()):
+            t.record_stream(side)
+        dq, dk, dv, dg, dbeta = L_.gdn_chunk_bwd_local(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, Gc, aux,
+                                                       states, dstates, rows, drows, dob, ctx.scale, st,
+                                                       [states2, dstates2, rows2, drows2, dL])
+        tq, tk, tv, tg, tb = ctx.dtypes
+        return dq.to(tq), dk.to(tk), dv.to(tv), dg.to(tg), dbeta.to(tb), None, None, None
+
+
+def fused_affine_delta_rule(q, k, v, g, beta, layout: ChunkLayout, first: ChunkLayout,
+                            scale: float | None = None):
+    """``(o, S_final, L, M)``: the zero-start rule over ``layout`` and the identity-started, zero-value
+    rule over its first segment (``first`` = the layout of that segment alone), sharing one prep."""
+    if not (fused_supported(q, v) and first.lengths[0] >= CHUNK and first.lengths[0] == layout.lengths[0]):
+        raise ValueError("fused affine rule needs the fused kernels and a first segment of at least one chunk")
+    scale = q.shape[-1] ** -0.5 if scale is None else scale
+    return _FusedAffineRule.apply(q, k, v, g, beta, layout, first, scale)
 
 
 def fused_gated_delta_rule(q, k, v, g, beta, layout: ChunkLayout, scale: float | None = None,

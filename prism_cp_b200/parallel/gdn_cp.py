@@ -28,7 +28,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops.elementwise import causal_conv1d_silu
-from ..ops.gdn import chunk_gated_delta_rule, fused_gated_delta_rule, fused_supported
+from ..ops.gdn import chunk_gated_delta_rule, fused_affine_delta_rule, fused_gated_delta_rule, fused_supported
 from ..planner.joint.ir import spans as layout_spans
 
 HALO = 3
@@ -168,6 +168,35 @@ def _rule(q, k, v, g, beta, layout, initial_state=None):
     return chunk_gated_delta_rule(q, k, v, g, beta, layout, initial_state=initial_state)
 
 
+def _first_layout(ctx, layout, nseg: int, n0: int):
+    if nseg == 1:
+        return layout
+    if getattr(ctx, "_first_layout", None) is None:
+        from ..ops.gdn import ChunkLayout
+        ctx._first_layout = ChunkLayout((n0,), layout.tok0_dev.device)
+    return ctx._first_layout
+
+
+def _identity_pass(q, k, g, beta, n0: int, lay0):
+    """(L, M) of the first segment by a separate zero-value rule from the identity (a second CUDA
+    stream next to the caller's; the torch form on CPU)."""
+    H, DK = q.shape[1], q.shape[2]
+
+    def run():
+        eye = torch.eye(DK, dtype=torch.float32, device=q.device).expand(1, H, DK, DK).contiguous()
+        return _rule(q[:n0], k[:n0], q.new_zeros((n0, H, DK)), g[:n0], beta[:n0], lay0, initial_state=eye)
+
+    if not q.is_cuda:
+        return run()
+    main, side = torch.cuda.current_stream(q.device), _side_stream(q.device)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        out = run()
+    for t in (q, k, g, beta):
+        t.record_stream(side)
+    return out
+
+
 def delta_rule_cp(ctx, q, k, v, g, beta):
     """The recurrence of this rank's segments, with the state a continuing sample carries in.
 
@@ -177,7 +206,8 @@ def delta_rule_cp(ctx, q, k, v, g, beta):
     zero values started at the identity. So each rank runs
       * the zero-start pass over all its segments (outputs, and F of the last segment), and
       * if its first segment continues a sample, the zero-value pass over that segment alone
-        (dv = dk, on a second stream, concurrently with the first),
+        (dv = dk, on a second stream, concurrently with the first); on the fused kernels both
+        passes share one prep and one local backward (``ops.gdn.fused_affine_delta_rule``),
     all-gathers (F, M) of its last segment over the team, folds its predecessors' chain into S_in
     and adds L S_in to the first segment's rows: no pass waits for another rank, and no pass is run
     twice. Gradients reach both passes and the predecessors' (F, M) through autograd and the
@@ -192,32 +222,18 @@ def delta_rule_cp(ctx, q, k, v, g, beta):
     f32 = torch.float32
     n0 = ctx.segment_lengths[0] if nseg else 0
     linear = None
-    if first_cont:
-        if nseg == 1:
-            lay0 = layout
-        else:
-            if getattr(ctx, "_first_layout", None) is None:
-                from ..ops.gdn import ChunkLayout
-                ctx._first_layout = ChunkLayout((n0,), q.device)
-            lay0 = ctx._first_layout
-        def run():
-            eye = torch.eye(DK, dtype=f32, device=q.device).expand(1, H, DK, DK).contiguous()
-            return _rule(q[:n0], k[:n0], q.new_zeros((n0, H, DK)), g[:n0], beta[:n0], lay0, initial_state=eye)
-
-        if q.is_cuda:
-            main, side = torch.cuda.current_stream(q.device), _side_stream(q.device)
-            side.wait_stream(main)
-            with torch.cuda.stream(side):
-                linear = run()
-            for t in (q, k, g, beta):
-                t.record_stream(side)
-        else:
-            linear = run()
-    o, S_zero = _rule(q, k, v, g, beta, layout)
-    if linear is not None and q.is_cuda:
-        torch.cuda.current_stream(q.device).wait_stream(_side_stream(q.device))
-        for t in linear:
-            t.record_stream(torch.cuda.current_stream(q.device))
+    if first_cont and fused_supported(q, v) and n0 >= 64:
+        o, S_zero, L_rows, M_first = fused_affine_delta_rule(q, k, v, g, beta, layout,
+                                                             _first_layout(ctx, layout, nseg, n0))
+        linear = (L_rows, M_first[None])
+    else:
+        if first_cont:
+            linear = _identity_pass(q, k, g, beta, n0, _first_layout(ctx, layout, nseg, n0))
+        o, S_zero = _rule(q, k, v, g, beta, layout)
+        if linear is not None and q.is_cuda:
+            torch.cuda.current_stream(q.device).wait_stream(_side_stream(q.device))
+            for t in linear:
+                t.record_stream(torch.cuda.current_stream(q.device))
     F_tail = S_zero[nseg - 1] if last_cont else torch.zeros((H, DK, DV), dtype=f32, device=q.device)
     if last_cont and first_cont and single:
         M_tail = linear[1][0]

@@ -110,3 +110,40 @@ def test_tensor_core_local_backward_matches_cuda_core_kernel(lens, dv):
     for name, a, b in zip(("q", "k", "v", "g", "beta"), grads[1], grads[0]):
         assert torch.isfinite(a).all(), name
         assert rel_err(a, b) < 2e-2, f"d{name}: {rel_err(a, b)}"
+
+
+@pytest.mark.parametrize("lens", [(1024,), (576, 448)])
+def test_fused_affine_rule_matches_two_separate_passes(lens):
+    """One prep for the zero-start pass and the identity pass of the first segment (dv contractions
+    summed before one local backward) gives the outputs and gradients of the two separate passes."""
+    from prism_cp_b200.ops.gdn import ChunkLayout, fused_affine_delta_rule, fused_gated_delta_rule
+    dev = torch.device(DEV, torch.cuda.current_device())
+    q, k, v, g, beta, _ = (t.to(dev) if t is not None else None for t in _inputs(lens, 4, 256, 7, False))
+    layout, first = ChunkLayout(lens, dev), ChunkLayout(lens[:1], dev)
+    n0, H, DK = lens[0], q.shape[1], q.shape[2]
+    gen = torch.Generator(device=dev).manual_seed(3)
+    w_o = torch.randn(sum(lens), H, 256, device=dev, generator=gen)
+    w_L = torch.randn(n0, H, DK, device=dev, generator=gen)
+    w_S = torch.randn(len(lens), H, DK, 256, device=dev, generator=gen)
+    w_M = torch.randn(H, DK, DK, device=dev, generator=gen)
+
+    def run(fused):
+        ins = [t.detach().clone().requires_grad_(True) for t in (q, k, v, g, beta)]
+        if fused:
+            o, S, L, M = fused_affine_delta_rule(*ins, layout, first)
+        else:
+            o, S = fused_gated_delta_rule(*ins, layout)
+            eye = torch.eye(DK, device=dev).expand(1, H, DK, DK).contiguous()
+            L, Mf = fused_gated_delta_rule(ins[0][:n0], ins[1][:n0], torch.zeros_like(ins[0][:n0]), ins[3][:n0],
+                                           ins[4][:n0], first, initial_state=eye)
+            M = Mf[0]
+        loss = (o.float() * w_o).sum() + (L.float() * w_L).sum() + (S * w_S).sum() + (M * w_M).sum()
+        loss.backward()
+        torch.cuda.synchronize()
+        return [o.float(), L.float(), S, M] + [t.grad.float() for t in ins]
+
+    a, b = run(True), run(False)
+    names = ["o", "L", "S", "M", "dq", "dk", "dv", "dg", "dbeta"]
+    for name, x, y in zip(names, a, b):
+        err = ((x - y).norm() / y.norm().clamp_min(1e-6)).item()
+        assert err < 1e-2, (name, err)
