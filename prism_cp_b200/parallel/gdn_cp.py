@@ -24,6 +24,8 @@ state exchange modelled at joint_cp/model.py:141-145.
 
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -152,6 +154,9 @@ def conv_with_halo(ctx, x, weight):
 
 
 _SIDE: dict = {}
+# PRISM_GDN_SHARED_PREP=1: both passes of a continuing rank on one prep and one local backward
+# (``ops.gdn.fused_affine_delta_rule``); the default runs them as two fused rules on two streams
+SHARED_PREP = os.environ.get("PRISM_GDN_SHARED_PREP", "0") == "1"
 
 
 def _side_stream(device) -> torch.cuda.Stream:
@@ -206,8 +211,8 @@ def delta_rule_cp(ctx, q, k, v, g, beta):
     zero values started at the identity. So each rank runs
       * the zero-start pass over all its segments (outputs, and F of the last segment), and
       * if its first segment continues a sample, the zero-value pass over that segment alone
-        (dv = dk, on a second stream, concurrently with the first); on the fused kernels both
-        passes share one prep and one local backward (``ops.gdn.fused_affine_delta_rule``),
+        (dv = dk, on a second stream, concurrently with the first); with PRISM_GDN_SHARED_PREP=1
+        both passes share one prep and one local backward (``ops.gdn.fused_affine_delta_rule``),
     all-gathers (F, M) of its last segment over the team, folds its predecessors' chain into S_in
     and adds L S_in to the first segment's rows: no pass waits for another rank, and no pass is run
     twice. Gradients reach both passes and the predecessors' (F, M) through autograd and the
@@ -222,7 +227,7 @@ def delta_rule_cp(ctx, q, k, v, g, beta):
     f32 = torch.float32
     n0 = ctx.segment_lengths[0] if nseg else 0
     linear = None
-    if first_cont and fused_supported(q, v) and n0 >= 64:
+    if SHARED_PREP and first_cont and fused_supported(q, v) and n0 >= 64:
         o, S_zero, L_rows, M_first = fused_affine_delta_rule(q, k, v, g, beta, layout,
                                                              _first_layout(ctx, layout, nseg, n0))
         linear = (L_rows, M_first[None])

@@ -13,15 +13,19 @@ and ``fixed_ms`` the per-call overhead. The result goes into
 ``Model.operator_calibration``; CP > 1 keeps the analytic communication terms
 (at the measured NVLink bandwidth) unless a measured CP response profile is
 given. ``fit_byte_scale`` does the same for memory: the activation-byte scale at
-which the evaluator's peak of one microbatch equals a measured peak. The
-committed ``data/b200_operator_calibration.json`` holds both, plus a CP = 2
-overhead factor fitted to the bench's one- and two-GPU step times, for this
-framework's own kernels on B200 and the 1.3B shape. It is regenerated with
+which the evaluator's peak of one microbatch equals a measured peak.
+``rescale`` moves the multi-length CP = 1 fit to newer one-length records of the
+same modules (the kernels got faster since the fit), and ``fit_cp_factors``
+gives every CP operator and degree its measured/predicted factor from module
+anchors at CP 2/4/8. The committed ``data/b200_operator_calibration.json``
+holds all of them, for this framework's own kernels on B200 and the 1.3B shape;
+it is regenerated with
 
     python -m prism_cp_b200.planner.calibrate \
         --records prism_cp_b200/planner/data/b200_module_records.json \
-        --output prism_cp_b200/planner/data/b200_operator_calibration.json \
-        --peak-gib 141.15 --bench-steps 5780 3126
+        --output prism_cp_b200/planner/data/b200_operator_calibration.json --peak-gib 141.15 \
+        --rescale-records prism_cp_b200/planner/data/b200_anchor_records.json \
+        --cp-records prism_cp_b200/planner/data/b200_anchor_records.json
 """
 
 from __future__ import annotations
@@ -150,6 +154,38 @@ def fit_cp_overhead(model: Model, pattern: str, lengths: dict, world: int, step_
     return 0.5 * (lo + hi)
 
 
+def rescale(cal: dict, model: Model, records: list[dict]) -> dict:
+    """The CP = 1 calibration moved to newer measurements of the same modules.
+
+    The multi-length fit keeps its shape (the ratio of token-linear, quadratic and fixed terms); each
+    operator with newer one-sequence CP = 1 records is scaled so that its price matches their median
+    measured/predicted ratio (faster kernels since the fit divide every term by the same factor).
+    Operators without newer records keep their fit."""
+    import statistics
+    from dataclasses import replace
+    out = {k: dict(v) for k, v in cal.items()}
+    m = replace(model, operator_calibration={k: {x: v[x] for x in ("linear", "quadratic", "fixed_ms") if x in v}
+                                             for k, v in cal.items()}, cp_overhead=None)
+    ratios: dict = {}
+    for r in records:
+        sym = MODULES.get(r["module"])
+        if int(r.get("cp", 1)) != 1 or int(r.get("sequences", 1)) != 1 or sym not in out:
+            continue
+        lin, quad = _analytic_ms(m, sym, int(r["tokens"]))
+        c = out[sym]
+        predicted = lin / c["linear"] + (quad / c["quadratic"] if "quadratic" in c else 0.0) + c.get("fixed_ms", 0.0)
+        ratios.setdefault(sym, []).append(float(r["fb_ms"]) / predicted)
+    for sym, v in ratios.items():
+        f = statistics.median(v)
+        c = out[sym]
+        c["linear"] /= f
+        if "quadratic" in c:
+            c["quadratic"] /= f
+        c["fixed_ms"] = c.get("fixed_ms", 0.0) * f
+        c["rescaled_by"] = f
+    return out
+
+
 def fit_cp_factors(model: Model, records: list[dict]) -> dict:
     """Per operator and CP degree: measured module time over the calibrated model's price.
 
@@ -194,6 +230,8 @@ def main(argv=None) -> int:
     ap.add_argument("--peak-tokens", type=int, default=32768)
     ap.add_argument("--bench-steps", type=float, nargs=2, default=None, metavar=("CP1_MS", "CP2_MS"),
                     help="measured bench.py ms/step on one GPU and on two (CP = 2), 8 x 32K tokens")
+    ap.add_argument("--rescale-records", type=Path, nargs="*", default=None,
+                    help="newer module-bench JSON files: their CP = 1 rows rescale the fitted operators")
     ap.add_argument("--cp-records", type=Path, nargs="*", default=None,
                     help="module-bench JSON files at CP > 1: per-operator, per-degree factors (replaces "
                          "--bench-steps)")
@@ -209,6 +247,10 @@ def main(argv=None) -> int:
     cal = calibrate(records, model)
     out = {"model_config": args.model_config, "compute_tflops": model.compute_tflops,
            "source": str(args.records), "calibration": cal}
+    if args.rescale_records:
+        cal = rescale(cal, model, [r for path in args.rescale_records for r in _records_of(path)])
+        out["calibration"] = cal
+        out["rescale_source"] = ", ".join(str(p) for p in args.rescale_records)
     model = replace(model, operator_calibration={k: {x: v[x] for x in ("linear", "quadratic", "fixed_ms") if x in v}
                                                  for k, v in cal.items()})
     if args.peak_gib is not None:

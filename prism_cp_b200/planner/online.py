@@ -132,6 +132,14 @@ def candidate_plan(lengths: dict, world: int, pattern: str, cp_gdn: int, cp_gqa:
     return plan
 
 
+def _packing_threshold(model: Model) -> int | None:
+    """Per-rank tokens above which a microbatch recomputes, when that is a threshold (packing keeps
+    ordinary microbatches below it); None when nothing recomputes or everything does (0: full
+    recompute, where the memory model alone bounds the capacity)."""
+    r = model.recompute_tokens
+    return r if r is not None and r > 0 else None
+
+
 def dynamic_candidates(lengths: dict, world: int, pattern: str, model: Model,
                        capacities=(16384, 24576, 32768)) -> list[tuple]:
     """Plans with the CP degree chosen per document (the dynamic-CP scheduler at per-rank token
@@ -141,8 +149,9 @@ def dynamic_candidates(lengths: dict, world: int, pattern: str, model: Model,
     from .studies import native_joint_plan
     ev = Evaluator(model, lengths, world, pattern)
     out = []
+    threshold = _packing_threshold(model)
     for cap in capacities:
-        if model.recompute_tokens is not None and cap > model.recompute_tokens:
+        if threshold is not None and cap > threshold:
             continue
         try:
             plan = native_joint_plan(lengths, world, pattern, cap)
@@ -177,10 +186,11 @@ def select(lengths: dict, world: int, pattern: str, model: Model, degrees=(1, 2,
         # the memory model's token ceiling is necessary, not sufficient (CP workspaces come on top):
         # shrink the per-rank capacity until some candidate fits
         top = max(1, model.token_capacity_upper_bound(pattern, world) // world)
-        if model.recompute_tokens is not None:
+        threshold = _packing_threshold(model)
+        if threshold is not None:
             # pack ordinary microbatches below the recompute threshold; only documents longer than
             # a team's share run alone with recompute
-            top = min(top, model.recompute_tokens)
+            top = min(top, threshold)
         last = None
         for frac in (1.0, 0.9, 0.8, 0.7, 0.6, 0.5, 0.4, 0.3):
             try:

@@ -70,3 +70,20 @@ def test_dynamic_plan_gives_long_documents_big_teams_and_short_ones_cp1():
     uniform = select(lengths, 8, hybrid_1p3b().pattern, model, dynamic=False)
     assert sel.predicted_update_ms <= uniform.predicted_update_ms
     assert (sel.dynamic_capacity is not None) == (sel.predicted_update_ms < uniform.predicted_update_ms)
+
+
+def test_full_recompute_keeps_the_memory_bounded_capacity():
+    """With every microbatch recomputing (recompute_tokens = 0, ``--recompute-granularity full``) the
+    packing capacity comes from the memory model, not from the threshold: the batch is not split
+    into one document per microbatch."""
+    from dataclasses import replace
+    from prism_cp_b200.planner.calibrate import calibrated
+    from prism_cp_b200.planner.cli import B200_ENVELOPE
+    cfg = hybrid_1p3b()
+    m = calibrated(model_from_config(cfg, B200_ENVELOPE["device_bytes"],
+                                     **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"}))
+    lengths = dict(enumerate(lognormal_lengths(1 << 20, 8192, 1.0, 512, 131072, 8, 1237)))
+    full = select(lengths, 4, cfg.pattern, replace(m, recompute_tokens=0))
+    assert len(full.plan.microbatches) < len(lengths) // 2, len(full.plan.microbatches)
+    threshold = select(lengths, 4, cfg.pattern, replace(m, recompute_tokens=32768))
+    assert len(full.plan.microbatches) <= len(threshold.plan.microbatches) + 2
