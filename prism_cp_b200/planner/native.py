@@ -5,17 +5,22 @@ it from an external Megatron source tree (experiments/sequence_dynamic_cp/
 native.py:14-86). That tree is not available, so this is a re-derivation of its
 documented behaviour - workload ``(L^2 + beta L) / cp``, minimum CP, greedy fill
 with tie-breaks, per-rank token capacity ``K`` - checked against the frozen
-``rank_ids`` it produced (golden plans from the reference's results):
+``rank_ids`` it produced (golden plans from the reference's results), its two
+unit regressions and its square-vs-hybrid counterexample (the square workload
+packs short samples to the token capacity and the idle ranks then double the
+long sample's group; a token-weighted workload spreads them):
 
 one microbatch (``next_group``):
   1. samples are visited in descending workload order (ties: input order);
   2. a sample needs ``cp = max(min_cp, 2^ceil(log2(L / K)))`` ranks;
-  3. if an aligned block of ``cp`` idle ranks exists (lowest start first) the
-     sample opens a new group there;
-  4. otherwise it joins the least-loaded existing group (ties: lowest start)
+  3. the candidate group is the least-loaded existing group (ties: lowest start)
      whose per-rank tokens stay <= K, whose per-rank workload stays within
      ``(local_tall + beta) * K * (1 + DELTA)`` (``local_tall`` = longest sample
-     of the microbatch) and that divides the sample by 2*cp; else it is left over;
+     of the microbatch) and that divides the sample by 2*cp;
+  4. the sample joins it when that does not raise the heaviest group's workload
+     (it fills the room the tallest sample leaves); otherwise it opens a new
+     group on the first aligned block of ``cp`` idle ranks; with no idle block
+     it joins the candidate anyway; with no candidate it is left over;
   5. idle ranks are filled by doubling the smallest group (lowest start first)
      and shifting later groups right; when a world is not a power of two, or no
      doubling fits, all samples of the microbatch become one world-wide group.
@@ -87,13 +92,7 @@ def next_group(remaining: list[tuple[int, int]], world: int, cap: int, min_cp: i
         need = gpus_needed(L, cap, min_cp)
         if need > world:
             raise ValueError(f"sample {sid} of length {L} needs CP{need} > world {world}")
-        start = _aligned_free(free, need)
-        if start is not None:
-            for r in range(start, start + need):
-                free[r] = False
-            groups.append({"start": start, "size": need, "samples": [sid], "tokens": L / need,
-                           "load": (L * L + beta_tokens * L) / need})
-            continue
+        work = L * L + beta_tokens * L
         best = None
         for g in groups:
             c = g["size"]
@@ -101,19 +100,27 @@ def next_group(remaining: list[tuple[int, int]], world: int, cap: int, min_cp: i
                 continue
             if g["tokens"] + L / c > cap:
                 continue
-            load = g["load"] + (L * L + beta_tokens * L) / c
-            if load > limit * (1 + 1e-12):
+            if g["load"] + work / c > limit * (1 + 1e-12):
                 continue
             key = (g["load"], g["start"])
             if best is None or key < best[0]:
                 best = (key, g)
+        heaviest = max((g["load"] for g in groups), default=0.0)
+        start = None
+        if best is None or best[1]["load"] + work / best[1]["size"] > heaviest * (1 + 1e-12):
+            start = _aligned_free(free, need)
+        if start is not None:
+            for r in range(start, start + need):
+                free[r] = False
+            groups.append({"start": start, "size": need, "samples": [sid], "tokens": L / need, "load": work / need})
+            continue
         if best is None:
             leftovers.append((sid, L))
             continue
         g = best[1]
         g["samples"].append(sid)
         g["tokens"] += L / g["size"]
-        g["load"] += (L * L + beta_tokens * L) / g["size"]
+        g["load"] += work / g["size"]
     if not groups:
         raise ValueError("Native scheduler made no progress")
     groups = _fill_idle(groups, world)

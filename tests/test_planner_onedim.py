@@ -29,6 +29,22 @@ def test_native_unit_regressions():
     assert replay([(0, 50), (1, 50)], 14, 100) == [[[0, 1]] * 14]
 
 
+def test_square_and_token_weighted_native_plans_differ_on_the_counterexample():
+    """One 16K sample among 128 2K samples, 16 ranks, K = 32K: the square workload packs the short
+    samples to the token capacity and the idle ranks then double the long sample's group (CP2, a
+    32K-token rank); weighting tokens (the 1-GQA + 3-GDN stack coefficients, beta = 10.107 / 0.05545
+    * 1024 tokens) spreads them, so the long sample keeps one rank and no rank holds more than 18K."""
+    lengths = {0: 16384, **{i: 2048 for i in range(1, 129)}}
+    limits = Constraints(16, 32768, alignment=32)
+    square = native_plan(lengths, limits, ProxyCost("square", 1.0, 0.0))
+    weighted = native_plan(lengths, limits, ProxyCost("hybrid", 0.05545098956660255, 10.106780354385673))
+    assert len(square) == len(weighted) == 1
+    assert len(next(g for g in square[0] if 0 in g.ids).ranks) == 2
+    assert len(next(g for g in weighted[0] if 0 in g.ids).ranks) == 1
+    assert max(sum(lengths[i] for i in g.ids) / len(g.ranks) for g in square[0]) == 32768
+    assert max(sum(lengths[i] for i in g.ids) / len(g.ranks) for g in weighted[0]) == 18432
+
+
 @pytest.mark.parametrize("plan,reason", [
     (((Group((0,), (0,)), Group((1,), (0,))),), "exactly once"),
     (((Group((0,), (0,)),),), "All ranks"),
