@@ -29,7 +29,6 @@ process groups (all dyadic teams exist from start-up).
 
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 
 from .joint.cost import Evaluator, Model
