@@ -55,3 +55,31 @@ def test_gather_tables_reproduce_the_route(world, lengths, src_mode, dst_mode, r
     # the largest staging area any rank needs is what the heap must hold per half
     sent = [sum(n for s, _, _, _, n in edges if s == r) for r in range(world)]
     assert max(sent) == max(int(c.send_index.numel()) for c in compiled)
+
+
+def test_staging_heap_grows_only_when_a_route_needs_more(monkeypatch):
+    """The transport's heap is allocated on first use and regrown, after a barrier of the group, only
+    when a route's largest staging area exceeds half of it (the same decision on every rank)."""
+    from prism_cp_b200.parallel import symm
+
+    made, barriers, closed = [], [], []
+
+    class FakeHeap:
+        def __init__(self, group, nbytes, device):
+            self.group, self.nbytes, self.device = group, nbytes, device
+            made.append(nbytes)
+
+        def close(self):
+            closed.append(self.nbytes)
+
+    monkeypatch.setattr(symm, "SymmetricHeap", FakeHeap)
+    monkeypatch.setattr(symm.dist, "barrier", lambda group=None: barriers.append(group))
+    t = symm.P2PTransport(group="team", device=torch.device("cpu"), min_bytes=1 << 20)
+    t._ensure(1000)
+    assert made == [1 << 20] and not barriers and t.half == 1 << 19
+    t._ensure(1 << 19)                      # fits in half: no new heap
+    assert made == [1 << 20]
+    t._ensure((1 << 19) + 1)                # does not fit: barrier, close, twice the need
+    assert barriers == ["team"] and closed == [1 << 20] and made[-1] == 2 * ((1 << 19) + 1)
+    t.close()
+    assert t.heap is None
