@@ -449,8 +449,8 @@ def fused_gated_delta_rule(q, k, v, g, beta, layout: ChunkLayout, scale: float |
     """``(o, final_state)`` of the chunked gated delta rule on the fused sm_100a kernels.
 
     ``keep_intermediates`` (default: on unless ``PRISM_GDN_SAVE=0``) keeps the forward's prep
-    outputs and per-chunk states for the backward; auxiliary passes that only feed a small state
-    (the CP tail state and transition map) pass False and are recomputed in the backward."""
+    outputs and per-chunk states for the backward; False keeps only the inputs and recomputes the
+    prep and the states in the backward (less memory for passes whose outputs are small)."""
     if not fused_supported(q, v):
         raise ValueError("fused gated delta rule needs CUDA tensors with dk = 128 and dv in {128, 256}")
     scale = q.shape[-1] ** -0.5 if scale is None else scale
