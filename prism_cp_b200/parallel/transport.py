@@ -1,13 +1,19 @@
 """CP-transition reshard: exact token permutation between two ownership layouts.
 
 ``move(x, source, target)`` moves this rank's rows of ``x`` (local order of
-``source``) to their owners in ``target`` using the interval route of the IR.
-The collective is an all-to-all with per-peer split sizes over the world; the
-backward runs the inverse route (reference behaviour:
+``source``) to their owners in ``target`` using the interval route of the IR;
+the backward runs the inverse route (reference behaviour:
 experiments/sequence_dynamic_cp/joint_cp/transport.py:12-70). Identity routes
-(same rank, same offset) cost nothing. Routes are compiled once per
-(source, target, lengths) into per-peer row index tensors, so the pack and
-unpack are single gathers/scatters on the device.
+(same rank, same offset) cost nothing. Two transports:
+
+* P2P (``use_p2p``; the trainer's default on GPUs): the sender stages its rows
+  in a symmetric heap and one gather kernel pulls them over NVLink into the
+  destination layout (``parallel/symm.py``);
+* NCCL (CPU / gloo, or ``PRISM_RESHARD=nccl``): an all-to-all with per-peer
+  split sizes over the world.
+
+Routes are compiled once per (source, target, lengths) into per-peer row index
+tensors, so the pack and unpack are single gathers/scatters on the device.
 """
 
 from __future__ import annotations
