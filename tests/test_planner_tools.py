@@ -279,3 +279,33 @@ def test_cp_factors_fit_from_module_anchors():
     lay = Layout((Group((0, 1), (0,)),), "contiguous")
     got = Evaluator(priced, {0: 65536}, 2, "G").operator("G", lay)[0]
     assert abs(got - 1.3 * predicted("G", 2, 65536)) < 1e-9
+
+
+def test_committed_b200_anchor_profile_prices_its_own_anchors():
+    """The B200 anchor profile built from the committed module records validates against the 1.3B
+    model and, used as the CP response, prices a 65,536-token sequence at every measured CP degree at
+    exactly its measured time."""
+    import json
+    from dataclasses import replace
+    from pathlib import Path
+    from prism_cp_b200.models.config import PRESETS
+    from prism_cp_b200.planner import profile_builder
+    from prism_cp_b200.planner.cli import B200_ENVELOPE
+    from prism_cp_b200.planner.joint.cost import Evaluator, model_from_config
+    from prism_cp_b200.planner.joint.ir import Group, Layout
+    data = Path(profile_builder.__file__).resolve().parent / "data"
+    committed = json.loads((data / "b200_cp_anchors.json").read_text())
+    records = json.loads((data / "b200_anchor_records.json").read_text())
+    rebuilt = profile_builder.build(records["records"], 65536, records["model_shape"], committed["name"],
+                                    committed["source"])
+    assert rebuilt == committed
+    cfg = PRESETS["hybrid-1.3b"]()
+    m = replace(model_from_config(cfg, B200_ENVELOPE["device_bytes"],
+                                  **{k: v for k, v in B200_ENVELOPE.items() if k != "device_bytes"}),
+                cp_response=committed)
+    for kind, sym in (("GQA", "*"), ("GDN", "G")):
+        for cp, ms in committed["anchors"][kind]["milliseconds"].items():
+            cp = int(cp)
+            lay = Layout((Group(tuple(range(cp)), (0,)),), "zigzag" if sym == "*" else "contiguous")
+            got = Evaluator(m, {0: 65536}, cp, sym).operator(sym, lay)[0]
+            assert abs(got - ms) < 1e-6 * ms, (kind, cp, got, ms)
