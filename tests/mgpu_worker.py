@@ -106,7 +106,7 @@ def main():
 
     # 3. chunkwise GDN CP on the GPU state kernels vs one GPU
     # sample 1 spans a rank boundary, so a rank holds a finished sample and a continuing one (the
-    # tail pass then runs over the continuing segment alone)
+    # identity pass then runs over the continuing first segment alone)
     glen = {0: 640 * world // 2, 1: 2560 * world // 2, 2: 640 * world // 2}
     gctx = LocalLayout(Layout((Group(ranks, (0, 1, 2)),), "contiguous"), glen, world, rank, dev, teams)
     Tg, H, dk, dv = sum(glen.values()), 4, 128, 256
@@ -125,11 +125,27 @@ def main():
     o = gctx.delta_rule(*loc)
     (o * gout[rows]).sum().backward()
     torch.cuda.synchronize()
-    # the CP path runs the bf16 fused kernels (dk 128, dv 256) three times (tail state, transition map
-    # from the identity, output from the incoming state); the oracle is fp32 on one GPU
+    # the CP path runs the bf16 fused kernels (dk 128, dv 256): the zero-start pass over every segment
+    # and the identity pass over a continuing first segment; the oracle is fp32 on one GPU
     assert rel(o, ref[rows]) < 2e-2, f"GDN CP output {rel(o, ref[rows])}"
     for name, t, r in zip("qkvgb", loc, ins):
         assert rel(t.grad, r.grad[rows]) < 1e-1, f"GDN CP gradient d{name} {rel(t.grad, r.grad[rows])}"
+
+    # 3b. the same with both passes on one prep (PRISM_GDN_SHARED_PREP)
+    from prism_cp_b200.parallel import gdn_cp
+    gdn_cp.SHARED_PREP = True
+    try:
+        sctx = LocalLayout(Layout((Group(ranks, (0, 1, 2)),), "contiguous"), glen, world, rank, dev, teams)
+        loc2 = [t[rows].clone().requires_grad_(True) for t in (qq, kk, vv, gg, bb)]
+        o2 = sctx.delta_rule(*loc2)
+        (o2 * gout[rows]).sum().backward()
+        torch.cuda.synchronize()
+        check_status(dev)
+    finally:
+        gdn_cp.SHARED_PREP = False
+    assert rel(o2, ref[rows]) < 2e-2, f"GDN CP (shared prep) output {rel(o2, ref[rows])}"
+    for name, t, r in zip("qkvgb", loc2, ins):
+        assert rel(t.grad, r.grad[rows]) < 1e-1, f"GDN CP (shared prep) gradient d{name} {rel(t.grad, r.grad[rows])}"
 
     # 4. tensor parallelism over all ranks (TP = world, CP = 1) on the sm_100a kernels vs one GPU
     from prism_cp_b200.models.config import HybridConfig
