@@ -490,6 +490,11 @@ def solve(lengths: dict, world: int, pattern: str, model, options: SearchOptions
         raise ValueError("Invalid lengths, world or pattern")
     if options.mode == "exact" and (len(lengths) > 6 or world > 4):
         raise ValueError("Exact domain is limited to <=6 samples and <=4 ranks; use bounded mode")
+    if getattr(model, "recompute_tokens", None) is not None:
+        # the search prices a microbatch layer by layer; whether it recomputes depends on all of its
+        # layouts at once, which the incremental objective cannot see
+        raise ValueError("The joint solver prices microbatches without recompute; pass a model with "
+                         "recompute_tokens=None (the online selector handles recompute)")
     search = _Search(lengths, world, pattern, model, options)
     limit_hit = False
     try:

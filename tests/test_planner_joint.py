@@ -224,3 +224,17 @@ def test_replay_rows_keep_logical_ids_and_reject_edits():
     rows[-1]["capacity_tokens"] += 1
     with pytest.raises(ValueError, match="changed"):
         validate_replay(rows[-1], 2)
+
+
+def test_solver_rejects_recompute_priced_models():
+    """Recompute depends on every layout of a microbatch at once, which the solver's layer-by-layer
+    objective cannot price: such a model is refused with a clear error instead of a wrong plan."""
+    from dataclasses import replace
+    import pytest as _pytest
+    from prism_cp_b200.models.config import hybrid_tiny
+    from prism_cp_b200.planner.joint.cost import model_from_config
+    from prism_cp_b200.planner.joint.solver import solve
+    cfg = hybrid_tiny()
+    m = replace(model_from_config(cfg, 80 << 30), recompute_tokens=1024)
+    with _pytest.raises(ValueError, match="recompute"):
+        solve({0: 2048, 1: 1024}, 2, cfg.pattern, m)
