@@ -41,15 +41,6 @@ def _normal(shape, std, dtype, device, generator, shard=None):
     return nn.Parameter(t.contiguous().to(device=device, dtype=dtype))
 
 
-_DEBUG_LEVEL = int(__import__("os").environ.get("PRISM_DEBUG_SYNC", "0") or 0)
-
-
-def _debug_sync(where: str) -> None:
-    """With PRISM_DEBUG_SYNC=2: synchronise after every mixer and MLP (pins a device hang to a block)."""
-    if _DEBUG_LEVEL >= 2 and torch.cuda.is_available() and torch.cuda.is_initialized():
-        torch.cuda.synchronize()
-
-
 def _replicated(t) -> nn.Parameter:
     """A parameter every TP rank holds in full (its gradient is identical on all of them)."""
     p = t if isinstance(t, nn.Parameter) else nn.Parameter(t)
@@ -169,11 +160,8 @@ class HybridLayer(nn.Module):
 
     def forward(self, x, ctx, mlp_ctx=None):
         x = x + self.mixer(x, ctx)
-        _debug_sync(f"mixer {self.symbol}")
         if mlp_ctx is None or mlp_ctx is ctx:
-            out = x + self.mlp(x)
-            _debug_sync("mlp")
-            return out
+            return x + self.mlp(x)
         # joint plans may run the MLP in a different ownership layout
         moved = mlp_ctx.enter(x, ctx)
         return x + mlp_ctx.leave(self.mlp(moved), ctx)

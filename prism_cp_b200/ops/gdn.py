@@ -29,7 +29,6 @@ import os
 import torch
 
 from ._lib import is_cuda, lib, status
-from ..utils import watchdog
 
 CHUNK = 64
 
@@ -287,10 +286,8 @@ class _FusedChunkRule(torch.autograd.Function):
             Nc = Wn.shape[0]
             states = torch.empty((Nc, H, DV, 128), dtype=torch.bfloat16, device=q.device)
             rows = torch.empty((Nc, H, DV, CHUNK), dtype=torch.bfloat16, device=q.device)
-        watchdog.beat("gdn forward prep")
         L.gdn_chunk_fwd(Wn, U, Kd, Qg, Aqk, gam, layout.tok0_dev, layout.len_dev, layout.seq_chunks_dev, s0, o,
                         S_final, states, rows, st)
-        watchdog.beat("gdn forward state pass")
         if keep:
             ctx.save_for_backward(qb, kb, vb, gf, bt, s0, Wn, U, Kd, Qg, Aqk, gam, Gc, aux, states, rows)
         else:
@@ -323,11 +320,9 @@ class _FusedChunkRule(torch.autograd.Function):
             # scans over a few dozen SMs each: run them side by side on two streams
             side = _side_stream(qb.device) if SIDE_STREAM else main
             side.wait_stream(main)
-            watchdog.beat("gdn backward prep")
             with torch.cuda.stream(side):
                 L.gdn_chunk_fwd(Wn, U, Kd, Qg, Aqk, gam, lay.tok0_dev, lay.len_dev, lay.seq_chunks_dev, s0, None,
                                 None, states, rows, st)
-                watchdog.beat("gdn backward state recompute (side stream)")
             for t in (Wn, U, Kd, Qg, Aqk, gam, states, rows) + ((s0,) if s0 is not None else ()):
                 t.record_stream(side)
         dstates, drows = torch.empty_like(states), torch.empty_like(rows)
@@ -338,7 +333,6 @@ class _FusedChunkRule(torch.autograd.Function):
         dsf = dS_final.float().contiguous() if dS_final is not None else None
         L.gdn_chunk_bwd_state(Wn, Kd, Qg, Aqk, gam, dob, lay.tok0_dev, lay.len_dev, lay.seq_chunks_dev, dsf, dS0,
                               dstates, drows, st)
-        watchdog.beat("gdn backward reverse state pass")
         main.wait_stream(side)
         dq, dk, dv, dg, dbeta = L.gdn_chunk_bwd_local(qb, kb, vb, gf, bt, lay.tok0_dev, lay.len_dev, Gc, aux, states,
                                                       dstates, rows, drows, dob, ctx.scale, st, [])

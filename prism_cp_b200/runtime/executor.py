@@ -17,7 +17,6 @@ import torch.utils.checkpoint
 from ..parallel.layout import LocalLayout
 from ..parallel.transport import move
 from ..planner.joint.ir import Microbatch
-from ..utils import watchdog
 from ..utils.tracing import nvtx
 
 
@@ -59,14 +58,11 @@ class MicrobatchRun:
             if ctx is not prev:
                 with nvtx(f"route cp{getattr(prev, 'cp', '?')}->cp{getattr(ctx, 'cp', '?')}"):
                     x = move(x, prev, ctx)
-            if watchdog._ACTIVE is not None and x.requires_grad:
-                x.register_hook(lambda g, i=i: watchdog.beat(f"layer {i} backward done"))
             with nvtx(f"layer {i} {type(layer).__name__} cp{getattr(ctx, 'cp', '?')}"):
                 if self.recompute and x.requires_grad:
                     x = torch.utils.checkpoint.checkpoint(layer, x, ctx, mctx, use_reentrant=False)
                 else:
                     x = layer(x, ctx, mctx)
-            watchdog.beat(f"layer {i} forward done")
             prev = ctx
         return x, prev
 
