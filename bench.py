@@ -9,8 +9,10 @@ uniform over the vocabulary, random-init weights). The online planner picks
 the CP degree of the GDN and of the GQA layers for the batch on N GPUs from
 the calibrated B200 cost model and packs the documents into microbatches;
 a microbatch that holds more than 32K tokens on a rank (a document too long
-for its team) recomputes its layers in the backward. ``--workload fixed
---plan uniform`` runs 8 documents x 32768 tokens at CP = N instead.
+for its team) recomputes its layers in the backward. Gradient reduce-scatter
+overlaps the last backward and the parameter all-gather the next forward
+(``--no-overlap``: both after the step). ``--workload fixed --plan uniform``
+runs 8 documents x 32768 tokens at CP = N instead.
 
 Measured: W warm-up steps, then exactly K steps between barrier +
 synchronize, timed with CUDA events on the launching stream, max over ranks.
