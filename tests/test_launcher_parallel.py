@@ -68,3 +68,18 @@ def test_launcher_tensor_parallel_records_save_and_resume(tmp_path):
     argv = list(base)
     argv[argv.index("--train-iters") + 1] = "3"
     _run(argv + ["--load", str(ck)])
+
+
+def test_launcher_pipeline_parallel_with_full_recompute():
+    """``--recompute-granularity full`` reaches the pipeline stages (every stage layer recomputes)."""
+    _run(TINY + ["--pipeline-model-parallel-size", "2", "--context-parallel-size", "1",
+                 "--recompute-granularity", "full"])
+
+
+def test_launcher_online_scheduler_with_full_recompute():
+    """The online planner with every microbatch recomputing packs by its memory model (no capacity
+    collapse) and the trainer recomputes every microbatch."""
+    argv = [a for a in TINY]
+    i = argv.index("--sequence-packing-scheduler")
+    argv[i + 1] = "online"
+    _run(argv + ["--use-varlen-dataset", "--recompute-granularity", "full"])
