@@ -18,14 +18,17 @@
 //                          state is held TRANSPOSED in tensor memory (lane = value
 //                          column v, 128 fp32 columns = dk), so every product of the
 //                          recurrence is an M = 128 MMA:
-//                            Delta^T = U^T + S^T Wn^T      (A = S^T bf16, B = Wn  K-major)
+//                            Delta^T = U^T + S^T Wn^T      (A = S^T bf16, B = Wn  K-major;
+//                                                           U^T added as U^T x I on the tensor cores)
 //                            S^T    <- gamma S^T + Delta^T Kd (A = Delta^T, B = Kd MN-major)
 //                            O^T     = S^T Qg^T + Delta^T Aqk^T
 //   gdn_state_tc_kernel<1> the reverse pass for the gradient G = dL/dS_{c+1}:
 //                            dDelta^T = G^T Kd^T + dO^T Aqk
 //                            G^T     <- gamma G^T + dO^T Qg + dDelta^T Wn
 //   gdn_bwd_dv_kernel      tcgen05, one CTA per (chunk, head): every product that
-//                          contracts over dv (dWn, dKd, dQg, dAqk, dDelta V^T, dgamma).
+//                          contracts over dv (dWn, dKd, dQg, dAqk, dDelta V^T, dgamma);
+//                          a second launch can add the products of another state pass
+//                          over the same chunks (the identity pass of GDN CP).
 //   gdn_bwd_local_tc_kernel tcgen05, one CTA per (chunk, head): the WY backward, decay
 //                          gradients and dq, dk, dv, dg, dbeta, every product on the
 //                          tensor cores (gdn_bwd_local_kernel: the same on CUDA cores,
