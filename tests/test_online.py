@@ -1,3 +1,5 @@
+import pytest
+
 """Online per-batch CP selection."""
 
 from prism_cp_b200.planner.joint import Model
@@ -87,3 +89,22 @@ def test_full_recompute_keeps_the_memory_bounded_capacity():
     assert len(full.plan.microbatches) < len(lengths) // 2, len(full.plan.microbatches)
     threshold = select(lengths, 4, cfg.pattern, replace(m, recompute_tokens=32768))
     assert len(full.plan.microbatches) <= len(threshold.plan.microbatches) + 2
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_benchmark_workload_builds_the_planned_batch(world):
+    """The benchmark's default workload: 1M tokens of log-normal documents (the same lengths at every
+    N), an online plan that validates, covers every document once and fits the calibrated memory
+    model, with its predicted step time."""
+    from prism_cp_b200.runtime.workload import build
+    cfg = hybrid_1p3b()
+    wl = build(cfg, world, "lognormal", "online", pin=False)
+    assert sum(wl.batch.lengths.values()) == wl.description["global_batch_tokens"] <= 1 << 20
+    assert wl.description["seq_len"] == max(wl.batch.lengths.values())
+    validate_plan(wl.plan, wl.batch.lengths)
+    seen = sorted(s for mb in wl.plan.microbatches for g in mb.ingress.groups for s in g.samples)
+    assert seen == sorted(wl.batch.lengths)
+    assert wl.predicted_ms and wl.predicted_ms > 0 and wl.parallelism.startswith("online")
+    fixed = build(cfg, world, "fixed", "uniform", seqs=8, seq_len=32768, pin=False)
+    assert fixed.parallelism == f"cp{world}" and fixed.predicted_ms is None
+    validate_plan(fixed.plan, fixed.batch.lengths)
