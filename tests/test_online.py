@@ -1,6 +1,6 @@
-import pytest
-
 """Online per-batch CP selection."""
+
+import pytest
 
 from prism_cp_b200.planner.joint import Model
 from prism_cp_b200.planner.joint.cost import model_from_config
