@@ -18,6 +18,7 @@ a half after every peer has signalled that it finished reading it.
 
 from __future__ import annotations
 
+import math
 import os
 
 import torch
@@ -140,7 +141,9 @@ class P2PTransport:
             self.heap = None
 
     def exchange(self, x: torch.Tensor, edges) -> torch.Tensor:
-        row_bytes = x[0].numel() * x.element_size() if x.shape[0] else 0
+        # from the row shape, not from a local row: a rank's local part may be empty, and the route's
+        # staging size (hence the heap decision) must be the same number on every rank
+        row_bytes = math.prod(x.shape[1:]) * x.element_size()
         world = dist.get_world_size(self.group)
         rank = dist.get_rank(self.group)
         key = (edges, row_bytes)
